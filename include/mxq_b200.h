@@ -1,0 +1,159 @@
+/* mxq_b200 — C ABI of the B200 (sm_100a) implementation of mxq's quantize-and-emulated-matmul hot path.
+ *
+ * Every entry point replaces one function of the reference Python package (chloe-wong/microscaling-quant,
+ * paths below are mxq/...:line) and computes bit-identical results on the device. Conventions:
+ *   - all array arguments are DEVICE pointers to contiguous row-major data; sizes are element counts;
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream); calls are asynchronous unless stated;
+ *   - the return value is MXQ_OK (0) or an MXQ_ERR_* code; mxq_last_error() returns this thread's message;
+ *   - kernels never trap on data: NaN and Inf are values, and results follow the reference's rules for them.
+ * Thread safety: the library keeps no mutable global state besides the per-thread error message and a per-device
+ * SM-count cache filled once.
+ */
+#ifndef MXQ_B200_H
+#define MXQ_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------------------------ status */
+#define MXQ_OK 0
+#define MXQ_ERR_VALUE 1      /* an argument the reference rejects with ValueError */
+#define MXQ_ERR_INDEX 2      /* an axis out of range (IndexError in the reference) */
+#define MXQ_ERR_UNSUPPORTED 3 /* a configuration this build has no kernel for */
+#define MXQ_ERR_CUDA 4       /* the CUDA runtime reported an error */
+
+/* rounding modes: mxq/rounding/__init__.py:25 MODES */
+#define MXQ_RM_TIES_AWAY 0
+#define MXQ_RM_RNE 1
+#define MXQ_RM_TRUNCATE 2
+/* microxcaling rounding names: mxq/microxcaling/elemwise.py:29-60 */
+#define MXQ_MS_NEAREST 0
+#define MXQ_MS_FLOOR 1
+#define MXQ_MS_EVEN 2
+/* float_em grids: mxq/element_quant/float_em.py:41 GRIDS */
+#define MXQ_GRID_QTORCH 0
+#define MXQ_GRID_IEEE 1
+#define MXQ_GRID_OCP 2
+
+const char* mxq_version(void);
+const char* mxq_last_error(void);
+
+/* ------------------------------------------------------------------------------ elementwise (n values) */
+/* mxq/rounding/__init__.py:51-55 round_bits: int64 bit patterns rounded to `keep` fraction bits. keep == NULL
+ * uses keep_scalar for every element; otherwise keep[i] per element (each in [0, 22]). */
+int mxq_round_bits(const int64_t* bits, const int64_t* keep, int32_t keep_scalar, int64_t* out, int64_t n,
+                   int32_t mode, void* stream);
+/* mxq/rounding/__init__.py:58-61 round_int */
+int mxq_round_int_f32(const float* k, float* out, int64_t n, int32_t mode, void* stream);
+int mxq_round_int_f64(const double* k, double* out, int64_t n, int32_t mode, void* stream);
+/* mxq/rounding/__init__.py:64-85 bf16 */
+int mxq_bf16(const float* x, float* out, int64_t n, void* stream);
+/* mxq/element_quant/float_em.py:50-61 quantize, float32 or float64 input, float32 output */
+int mxq_float_em_f32(const float* z, float* out, int64_t n, int32_t e, int32_t m, int32_t mode, int32_t grid,
+                     void* stream);
+int mxq_float_em_f64(const double* z, float* out, int64_t n, int32_t e, int32_t m, int32_t mode, int32_t grid,
+                     void* stream);
+/* mxq/microxcaling/elemwise.py:63-151 _quantize_elemwise_core (allow_denorm=True), as
+ * mxq/element_quant/microsoft.py:18-23 calls it. bits includes sign and implicit bit; exp_bits 0 = integer. */
+int mxq_microsoft(const float* A, float* out, int64_t n, int32_t bits, int32_t exp_bits, float max_norm,
+                  int32_t round, int32_t saturate_normals, void* stream);
+/* mxq/scale_factor.py:40-44 mxquant; floor = float32(floor) */
+int mxq_scale_mxquant(const float* amax, float* X, int64_t n, float floor, void* stream);
+/* mxq/scale_factor.py:47-59 ocp (and :62-65 ocp_below_top with emax - 1); scale_emax = float32(2^(bits-1) - 1) */
+int mxq_scale_ocp(const float* amax, float* X, int64_t n, int32_t emax, float scale_emax, void* stream);
+/* mxq/scale_factor.py:68-81 ocp_no_clip for the OCP element format (e, m) */
+int mxq_scale_ocp_no_clip(const float* amax, float* X, int64_t n, int32_t e, int32_t m, int32_t round,
+                          float scale_emax, void* stream);
+/* mxq/arith.py:68-103 exact_add */
+int mxq_exact_add(const float* a, const float* b, float* out, int64_t n, int32_t e, int32_t m, int32_t mode,
+                  int32_t grid, void* stream);
+/* mxq/arith.py:106-117 truncate_significand */
+int mxq_truncate_significand(const float* x, float* out, int64_t n, int32_t m, void* stream);
+/* mxq/arith.py:120-124 flush_product; thr = float32(2^floor_exp) */
+int mxq_flush_product(const float* x, float* out, int64_t n, float thr, void* stream);
+/* mxq/arith.py:127-137 saturate */
+int mxq_saturate(const float* x, float* out, int64_t n, float limit, float value, void* stream);
+
+/* ---------------------------------------------------------------------------- Arithmetic datapaths */
+/* An Arithmetic of mxq/matmul/_arithmetic.py: MXQUANT(prod_e, prod_m) (:64-73) or MXGEMMINI(prod_e, prod_m,
+ * prod_floor) (:111-134) with spike's saturation pair (:88-102). */
+#define MXQ_ARITH_MXQUANT 0
+#define MXQ_ARITH_MXGEMMINI 1
+typedef struct mxq_arith {
+  int32_t kind;
+  int32_t prod_e, prod_m;
+  int32_t has_floor;      /* MXGEMMINI: prod_floor is not None */
+  float floor_thr;        /* float32(2^prod_floor) */
+  float sat_limit, sat_value;
+} mxq_arith;
+/* Arithmetic.product / acc_add / tile_add as elementwise operations (the reducers inline the same code) */
+int mxq_arith_product(const float* a, const float* b, float* out, int64_t n, const mxq_arith* arith, void* stream);
+int mxq_arith_acc_add(const float* S, const float* p, float* out, int64_t n, const mxq_arith* arith, int32_t e,
+                      int32_t m, void* stream);
+int mxq_arith_tile_add(const float* C, const float* t, float* out, int64_t n, const mxq_arith* arith, void* stream);
+
+/* ------------------------------------------------------------------------------------ block quantizers */
+/* A tensor is viewed as [outer, len, inner] with blocks of `block` along len (mxq/block/_driver.py:23-32); the
+ * codes P have V's layout and the scales X are [outer, ceil(len / block), inner]. */
+#define MXQ_FAMILY_FP32 0        /* format "FP32": X = 1, P = V */
+#define MXQ_FAMILY_MXQUANT 1     /* mxq/block/mxquant.py:26-32 */
+#define MXQ_FAMILY_MXGEMMINI 2   /* mxq/block/mxgemmini.py:37-59 */
+#define MXQ_FAMILY_OCP 3         /* mxq/block/ocp.py:35-49 */
+typedef struct mxq_quant_spec {
+  int32_t family;
+  int32_t e, m;            /* element format */
+  int32_t rounding;        /* MXQ_RM_* (mxquant: ties away; mxgemmini: its rounding_mode) or MXQ_MS_* (ocp) */
+  float scale_floor;       /* mxquant / mxgemmini: float32(scale_floor) */
+  int32_t placement;       /* ocp: 0 top, 1 below_top, 2 no_clip (mxq/block/ocp.py:32) */
+  float scale_emax;        /* ocp: float32(2^(scale_bits - 1) - 1) */
+  int32_t via_e, via_m;    /* mxgemmini `via`: ieee pre-rounding format, 0 = none */
+} mxq_quant_spec;
+/* mxq/block/_driver.py:45-66 compose with a named quantizer's two steps, fused: block amax, scale, divide and
+ * element rounding in one pass. */
+int mxq_block_quantize(const float* V, float* P, float* X, int64_t outer, int64_t len, int64_t inner, int64_t block,
+                       const mxq_quant_spec* spec, void* stream);
+/* The pieces of compose with caller-supplied steps (mxq/block/_driver.py:23-42, :63-64): the blocked layout is
+ * [outer, inner, nblocks, block] (the block axis moved last, zero-padded). */
+int mxq_block_amax(const float* V, float* amax, int64_t outer, int64_t len, int64_t inner, int64_t block,
+                   void* stream);
+/* Z = pad(V) / X in the blocked layout; X is [outer, inner, nblocks] (NULL: a copy) */
+int mxq_to_blocks(const float* V, const float* X, float* Z, int64_t outer, int64_t len, int64_t inner, int64_t block,
+                  void* stream);
+/* blocked [outer, inner, nblocks, block] -> [outer, len, inner], padding dropped (codes_from_blocks, :35-37;
+ * with block = 1 and len = nblocks it is scales_from_blocks, :40-42) */
+int mxq_from_blocks(const float* Zb, float* P, int64_t outer, int64_t len, int64_t inner, int64_t block,
+                    void* stream);
+/* mxq/block/_driver.py:69-72 dequantize: P * expand(X) along len */
+int mxq_dequantize(const float* P, const float* X, float* out, int64_t outer, int64_t len, int64_t inner,
+                   int64_t block, void* stream);
+
+/* ------------------------------------------------------------------------------------------ reducers */
+/* Y (M x N) = A^T B from codes P_A (K x M), P_B (K x N) and scales X_A (ceil(K/block) x M), X_B (.. x N).
+ * The schedule is `size` lane formats (sched_e[i], sched_m[i]), host arrays. */
+/* mxq/matmul/_systolic.py:23-62 systolic */
+int mxq_systolic(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
+                 int64_t N, int64_t block, int64_t size, const mxq_arith* arith, const int32_t* sched_e,
+                 const int32_t* sched_m, void* stream);
+/* mxq/matmul/_adder.py:42-71 adder_tree: log2(size) levels, level formats (level_e[l], level_m[l]) */
+int mxq_adder_tree(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
+                   int64_t N, int64_t block, int64_t size, const mxq_arith* arith, const int32_t* level_e,
+                   const int32_t* level_m, void* stream);
+/* mxq/matmul/_anchor.py:95-138 anchor_tree; tree_bits is [size / width][nbits] level widths per tree */
+typedef struct mxq_anchor_spec {
+  int32_t width, nbits, drop_rne, headroom, has_emin, emin;
+} mxq_anchor_spec;
+int mxq_anchor_tree(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K,
+                    int64_t M, int64_t N, int64_t block, int64_t size, const mxq_arith* arith, const int32_t* tree_e,
+                    const int32_t* tree_m, const mxq_anchor_spec* anchor, const int32_t* tree_bits, void* stream);
+/* mxq/_fp64_accum.py:24-29 fp64_accum: dequantized operands, float64 products and sums in K order, float32 out */
+int mxq_fp64_accum(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
+                   int64_t N, int64_t block, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MXQ_B200_H */

@@ -486,4 +486,82 @@ MXQ_HD float saturate(float x, float limit, float value) {
 // MXGEMMINI's _unsigned_zero (mxq/matmul/_arithmetic.py:105-108)
 MXQ_HD float unsigned_zero(float x) { return (x == 0.0f) ? 0.0f : x; }
 
+// ------------------------------------------------------------------------------ dispatchers
+enum Grid : int { GRID_QTORCH = 0, GRID_IEEE = 1, GRID_OCP = 2 };
+// OCP element formats (mxq/element_quant/formats.py:23-29): max_norm by (e, m); 0 if not an OCP format
+MXQ_HD float ocp_max_norm(int e, int m) {
+  if (e == 4 && m == 3) return 448.0f;
+  if (e == 5 && m == 2) return 57344.0f;
+  if (e == 3 && m == 2) return 28.0f;
+  if (e == 2 && m == 3) return 7.5f;
+  if (e == 2 && m == 1) return 6.0f;
+  return 0.0f;
+}
+MXQ_HD int ocp_emax(int e, int m) {        // microxcaling emax (mxq/microxcaling/formats.py:92-106)
+  if (e == 5) return 15;
+  if (e == 4) return 8;
+  if (e == 3) return 4;
+  return 2;
+}
+// float_em.quantize(z, e, m, mode, grid) for a float32 input (float_em.py:50-61)
+MXQ_HD float q_float_em(float z, int e, int m, int mode, int grid) {
+  if (e == 8 && m == 23) return z;
+  if (grid == GRID_QTORCH) return q_qtorch(z, e, m, mode);
+  if (grid == GRID_IEEE) return q_ieee(z, e, m, mode);
+  return q_ocp_f(z, e, m, mode, ocp_max_norm(e, m));
+}
+// ... for a float64 input: the ieee and ocp grids round from float64; qtorch casts to float32 first
+MXQ_HD float q_float_em_d(double z, int e, int m, int mode, int grid) {
+  if (e == 8 && m == 23) return q_ieee_from_d(z, 8, 23, mode);
+  if (grid == GRID_QTORCH) return q_qtorch(x86_d2f(z), e, m, mode);
+  if (grid == GRID_IEEE) return q_ieee_from_d(z, e, m, mode);
+  return q_ocp_from_d(z, e, m, mode, (double)ocp_max_norm(e, m));
+}
+// exact_add (arith.py:68-103) for any rounding mode and grid: rne/ieee takes the float32 paths, every other
+// combination the float64 one.
+MXQ_HD float exact_add_any(float a, float b, int e, int m, int mode, int grid) {
+  if (mode == RM_RNE && grid == GRID_IEEE) return exact_add_rne(a, b, e, m);
+  if (a == 0.0f) return b;
+  if (b == 0.0f) return a;
+  return q_float_em_d(dadd_rn((double)a, (double)b), e, m, mode, grid);
+}
+// scale_factor.ocp_no_clip (mxq/scale_factor.py:68-81): the ocp scale, doubled where amax / X rounded to the
+// format without saturation overflows
+MXQ_HD float scale_ocp_no_clip(float amax, int e, int m, int round, float scale_emax) {
+  float X = scale_ocp(amax, ocp_emax(e, m), scale_emax);
+  float r = q_microsoft(x86_div(amax, X), m + 2, e, ocp_max_norm(e, m), round, false);
+  return isinf_f(r) ? mul_rn(X, 2.0f) : X;
+}
+
+// ------------------------------------------------------------------------ Arithmetic (_arithmetic.py)
+// The two datapaths of mxq/matmul/_arithmetic.py as plain parameters (mirrors mxq_arith of include/mxq_b200.h).
+struct ArithP {
+  int kind;               // 0 MXQUANT, 1 MXGEMMINI
+  int prod_e, prod_m;
+  int has_floor;
+  float floor_thr, sat_limit, sat_value;
+};
+// product: MXQUANT (:70) qtorch ties-away of the float32 product; MXGEMMINI (:131) truncate, flush, saturate
+MXQ_HD float ar_product(const ArithP& A, float a, float b) {
+  if (A.kind == 0) return q_qtorch(x86_mul(a, b), A.prod_e, A.prod_m, RM_TIES_AWAY);
+  float x = truncate_significand(mul_rn(a, b), A.prod_m);
+  if (A.has_floor) x = flush_below(x, A.floor_thr);
+  return saturate(x, A.sat_limit, A.sat_value);
+}
+// MXGEMMINI's lane rounding (:125-127): bf16 on the bits for (8, 7), the ieee grid otherwise; -0 -> +0
+MXQ_HD float lane_round(float x, int e, int m) {
+  float r = (e == 8 && m == 7) ? bf16_rne(x) : q_ieee(x, e, m, RM_RNE);
+  return unsigned_zero(r);
+}
+// acc_add: MXQUANT (:71) qtorch ties-away of the float32 sum; MXGEMMINI (:132) exact sum of the two lane values
+MXQ_HD float ar_acc_add(const ArithP& A, float S, float p, int e, int m) {
+  if (A.kind == 0) return q_float_em(x86_add(S, p), e, m, RM_TIES_AWAY, GRID_QTORCH);
+  return exact_add_rne(lane_round(S, e, m), lane_round(p, e, m), e, m);
+}
+// tile_add: MXQUANT (:72) float32 add; MXGEMMINI (:133) exact bf16 add of the two bf16-rounded values
+MXQ_HD float ar_tile_add(const ArithP& A, float C, float t) {
+  if (A.kind == 0) return add_rn(C, t);
+  return exact_add_rne(lane_round(C, 8, 7), lane_round(t, 8, 7), 8, 7);
+}
+
 }  // namespace mxq

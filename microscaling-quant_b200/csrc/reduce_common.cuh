@@ -1,0 +1,70 @@
+// Types and helpers shared by the reducer kernels.
+#pragma once
+#include <stdint.h>
+
+#include "common.cuh"
+#include "numerics.cuh"
+
+namespace mxq {
+
+constexpr int kMaxLanes = 256;     // schedule entries a kernel takes by value (size <= 256)
+constexpr int kMaxLevels = 8;      // adder tree levels (size <= 256)
+constexpr int kMaxWidth = 64;      // anchor tree width
+constexpr int kMaxTrees = 64;      // anchor trees per reduction
+constexpr int kMaxBits = 8;        // anchor level-width entries per tree
+
+// one float(e, m) per accumulator position (mxq/schedule.py), passed by value
+struct LaneTable {
+  int8_t e[kMaxLanes];
+  int8_t m[kMaxLanes];
+};
+
+// an anchor_tree configuration (mxq/matmul/_anchor.py:95-138) resolved on the host
+struct AnchorTable {
+  int width, nbits, drop_rne, headroom, has_emin, emin;
+  int8_t tree_e[kMaxTrees], tree_m[kMaxTrees];
+  int8_t bits[kMaxTrees * kMaxBits];
+};
+
+// the block's scale map X_A[g] (x) X_B[g] for a thread's RM x RN outputs (mxq/matmul/_common.py:32-34)
+template <int RM, int RN>
+__device__ __forceinline__ void load_scale_map(float (&sc)[RM][RN], const float* __restrict__ XA,
+                                               const float* __restrict__ XB, int64_t g, int64_t M, int64_t N,
+                                               int64_t r0, int64_t c0) {
+  float xa[RM], xb[RN];
+#pragma unroll
+  for (int i = 0; i < RM; i++) xa[i] = (r0 + i < M) ? XA[g * M + r0 + i] : 0.0f;
+#pragma unroll
+  for (int j = 0; j < RN; j++) xb[j] = (c0 + j < N) ? XB[g * N + c0 + j] : 0.0f;
+#pragma unroll
+  for (int i = 0; i < RM; i++)
+#pragma unroll
+    for (int j = 0; j < RN; j++) sc[i][j] = mul_rn(xa[i], xb[j]);
+}
+
+template <int RM, int RN>
+__device__ __forceinline__ void store_tile(float* __restrict__ Y, const float (&C)[RM][RN], int64_t M, int64_t N,
+                                           int64_t r0, int64_t c0) {
+#pragma unroll
+  for (int i = 0; i < RM; i++)
+#pragma unroll
+    for (int j = 0; j < RN; j++)
+      if (r0 + i < M && c0 + j < N) Y[(r0 + i) * N + c0 + j] = C[i][j];
+}
+
+int systolic_generic(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K,
+                     int64_t M, int64_t N, int64_t bs, int size, const ArithP& A, const LaneTable& lanes,
+                     cudaStream_t st);
+int adder_generic(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
+                  int64_t N, int64_t bs, int size, int levels, const ArithP& A, const LaneTable& lv, cudaStream_t st);
+int anchor_generic(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K,
+                   int64_t M, int64_t N, int64_t bs, int size, const ArithP& A, const AnchorTable& at,
+                   cudaStream_t st);
+int fp64_accum(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
+               int64_t N, int64_t bs, cudaStream_t st);
+// the specialised systolic kernels; returns MXQ_ERR_UNSUPPORTED when (arith, schedule, size, block) has none
+int systolic_fast(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
+                  int64_t N, int64_t bs, int size, const ArithP& A, const LaneTable& lanes, cudaStream_t st);
+int check_arith(const mxq_arith* a, const char* what);
+
+}  // namespace mxq

@@ -1,0 +1,72 @@
+// Test shim: the CUDA kernels' element math (microscaling-quant_b200/csrc/numerics.cuh) compiled for the host,
+// exported under the oracle's signatures (h_* for o_*) so tests/test_numerics_host.py can run it through the
+// same golden checks and compare it with the oracle on large corpora without a GPU.
+#include <math.h>
+#include "../../microscaling-quant_b200/csrc/numerics.cuh"
+
+using namespace mxq;
+#define X extern "C" __attribute__((visibility("default")))
+
+X void h_round_bits(const int64_t* bits, const int64_t* keep, int64_t n, int mode, int64_t* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = round_bits_i64(bits[i], (int)keep[i], mode);
+}
+X void h_round_int_f32(const float* k, int64_t n, int mode, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = round_int_f(k[i], mode);
+}
+X void h_round_int_f64(const double* k, int64_t n, int mode, double* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = round_int_d(k[i], mode);
+}
+X void h_bf16(const float* x, int64_t n, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = bf16_rne(x[i]);
+}
+X void h_float_em_f32(const float* z, int64_t n, int e, int m, int mode, int grid, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = q_float_em(z[i], e, m, mode, grid);
+}
+X void h_float_em_f64(const double* z, int64_t n, int e, int m, int mode, int grid, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = q_float_em_d(z[i], e, m, mode, grid);
+}
+X void h_microsoft(const float* A, int64_t n, int bits, int exp_bits, float max_norm, int round, int sat, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = q_microsoft(A[i], bits, exp_bits, max_norm, round, sat != 0);
+}
+X void h_scale_mxquant(const float* amax, int64_t n, float fl, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = scale_mxquant(amax[i], fl);
+}
+X void h_scale_ocp(const float* amax, int64_t n, int emax, float scale_emax, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = scale_ocp(amax[i], emax, scale_emax);
+}
+X void h_scale_ocp_no_clip(const float* amax, int64_t n, int e, int m, int round, float scale_emax, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = scale_ocp_no_clip(amax[i], e, m, round, scale_emax);
+}
+X void h_exact_add(const float* a, const float* b, int64_t n, int e, int m, int mode, int grid, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = exact_add_any(a[i], b[i], e, m, mode, grid);
+}
+X void h_truncate_significand(const float* x, int64_t n, int m, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = truncate_significand(x[i], m);
+}
+X void h_flush_product(const float* x, int64_t n, float thr, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = flush_below(x[i], thr);
+}
+X void h_saturate(const float* x, int64_t n, float limit, float value, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = saturate(x[i], limit, value);
+}
+// floor_log2_rn against floor(RN32(log2 x)) computed through libm's double log2, over bit patterns [lo, hi)
+X int64_t h_log2_mismatches(uint32_t lo, uint32_t hi) {
+  int64_t bad = 0;
+  for (uint32_t u = lo; u < hi; u++) {
+    float x = u2f(u);
+    float ref = floorf((float)log2((double)x));
+    if ((float)floor_log2_rn(x) != ref) bad++;
+  }
+  return bad;
+}
+// the thresholds floor_log2_rn implies: smallest bit pattern reading k, for k in [-149, 128]
+X void h_log2_thresholds(uint32_t* out) {
+  for (int k = -149; k <= 128; k++) {
+    uint32_t lo = 1, hi = 0x7f800000u;                     // first u with floor_log2_rn(u2f(u)) >= k
+    while (lo < hi) {
+      uint32_t mid = lo + (hi - lo) / 2;
+      if (floor_log2_rn(u2f(mid)) >= k) hi = mid; else lo = mid + 1;
+    }
+    out[k + 149] = lo;
+  }
+}

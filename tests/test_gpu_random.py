@@ -1,0 +1,87 @@
+"""The CUDA kernels against the CPU oracle on larger seeded inputs than the golden fixtures hold: every block
+quantizer family x format x axis on a config-2-like matrix with special values, and the reducers on random
+operands, including values that take every non-fast branch (saturation, overflow, NaN, Inf, tiny products)."""
+import numpy as np
+import pytest
+
+import mxq_adapter as prod
+from _util import assert_bits, assert_bits_where, nan_block_mask
+
+pytestmark = pytest.mark.gpu
+
+FMTS = ("MXFP8_E4M3", "MXFP8_E5M2", "MXFP6_E3M2", "MXFP6_E2M3", "MXFP4")
+HW = [(4, 4)] * 8 + [(4, 5)] * 2 + [(4, 6)] * 5 + [(8, 7)]
+
+
+def config2_like(rows, cols, seed, special=True):
+    """config 2's distribution: N(0,1) x 2^U[-20,20] per row, 1% zeros, 0.1% subnormal-range values."""
+    rng = np.random.default_rng(seed)
+    V = rng.standard_normal((rows, cols)) * 2.0 ** rng.uniform(-20, 20, (rows, 1))
+    V[rng.random((rows, cols)) < 0.01] = 0.0
+    sub = rng.random((rows, cols)) < 0.001
+    V[sub] = np.sign(rng.standard_normal(sub.sum())) * rng.uniform(2.0 ** -149, 2.0 ** -126, sub.sum())
+    V = V.astype(np.float32)
+    if special:
+        V[3, 5], V[100, 7], V[200, 9], V[64:96, 11] = np.inf, -np.inf, np.nan, 0.0
+        V[300, 0:32] = (rng.uniform(-1, 1, 32) * 2.0 ** -140).astype(np.float32)
+    return V
+
+
+@pytest.mark.parametrize("family", ["mxquant", "mxgemmini", "ocp"])
+@pytest.mark.parametrize("axis", [0, 1])
+def test_block_vs_oracle(oracle, family, axis):
+    V = config2_like(512, 1024, 21)
+    keep = ~nan_block_mask(V, axis) if family == "mxquant" else np.ones(V.shape, bool)
+    for fmt in FMTS:
+        P, X = prod.block_quantize(V, family, fmt, axis)
+        Po, Xo = oracle.block_quantize(V, family, fmt, axis)
+        assert_bits_where(P, Po, keep, f"{family}/{fmt}/{axis} P")
+        assert_bits(X, Xo, f"{family}/{fmt}/{axis} X")
+
+
+def test_block_layout_paths(oracle):
+    """The three kernel paths (rows of 32, column runs of 4/2/1, generic) on shapes that force each."""
+    rng = np.random.default_rng(5)
+    for shape, axis, bs in (((64, 256), 1, 32), ((96, 130), 0, 32), ((96, 66), 0, 32), ((96, 67), 0, 32),
+                            ((7, 33, 5), 1, 32), ((40, 70), 1, 32), ((40, 70), 0, 16), ((3, 50, 4), 1, 5)):
+        V = (rng.standard_normal(shape) * 2.0 ** rng.uniform(-8, 8, shape)).astype(np.float32)
+        for family, fmt in (("mxquant", "MXFP6_E3M2"), ("mxgemmini", "MXFP8_E4M3"), ("ocp", "MXFP4")):
+            P, X = prod.block_quantize(V, family, fmt, axis, bs)
+            Po, Xo = oracle.block_quantize(V, family, fmt, axis, bs)
+            assert_bits(P, Po, f"{shape} {axis} {bs} {family} P")
+            assert_bits(X, Xo, f"{shape} {axis} {bs} {family} X")
+
+
+def _operands(oracle, K, M, N, fmt, seed, special=False):
+    rng = np.random.default_rng(seed)
+    A = (rng.standard_normal((K, M)) * 2.0 ** rng.uniform(-4, 4, (1, M))).astype(np.float32)
+    B = (rng.standard_normal((K, N)) * 2.0 ** rng.uniform(-4, 4, (1, N))).astype(np.float32)
+    P_A, X_A = oracle.block_quantize(A, "mxgemmini", fmt, 0)
+    P_B, X_B = oracle.block_quantize(B, "mxgemmini", fmt, 0)
+    if special:
+        idx = rng.integers(0, K * M, 40)
+        P_A.reshape(-1)[idx[:10]] = np.array([np.inf, -np.inf, np.nan, 300.0, -500.0, 2.0 ** -20, 1e30, -1e-30,
+                                              0.0, -0.0], np.float32)
+        P_B.reshape(-1)[idx[10:20] % (K * N)] = np.array([400.0, -3.0, 2.0 ** -12, np.nan, 1e20, 7.0, -7.0, 0.5,
+                                                          2.0 ** -9, 100.0], np.float32)
+        X_A[0, :3] = np.array([2.0 ** 100, 2.0 ** -130, np.inf], np.float32)
+    return P_A, X_A, P_B, X_B
+
+
+@pytest.mark.parametrize("special", [False, True])
+def test_systolic_vs_oracle(oracle, special):
+    ops = _operands(oracle, 288, 160, 144, "MXFP8_E4M3", 31, special)
+    for arith_p, arith_o, sched in ((prod.arith_mxgemmini(), oracle.arith_mxgemmini(), HW),
+                                    (prod.arith_mxquant(4, 3), oracle.arith_mxquant(4, 3), HW),
+                                    (prod.arith_mxgemmini(), oracle.arith_mxgemmini(), [(8, 7)] * 16)):
+        assert_bits(prod.systolic(*ops, arith_p, sched), oracle.systolic(*ops, arith_o, sched), f"systolic {sched[0]}")
+
+
+def test_trees_vs_oracle(oracle):
+    ops = _operands(oracle, 160, 96, 80, "MXFP6_E2M3", 41, True)
+    lv = [(4, 4), (4, 5), (4, 6), (8, 7)]
+    assert_bits(prod.adder_tree(*ops, prod.arith_mxgemmini(), lv), oracle.adder_tree(*ops, oracle.arith_mxgemmini(), lv),
+                "adder")
+    assert_bits(prod.anchor_tree(*ops, prod.arith_mxgemmini()), oracle.anchor_tree(*ops, oracle.arith_mxgemmini()),
+                "anchor")
+    assert_bits(prod.fp64_accum(*ops), oracle.fp64_accum(*ops), "fp64_accum")

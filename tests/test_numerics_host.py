@@ -1,0 +1,100 @@
+"""The CUDA kernels' element math (numerics.cuh), compiled for the host with g++, checked without a GPU:
+against every elementwise golden fixture of the reference, against the CPU oracle on large random corpora, and
+floor(log2 x) exhaustively over all positive float32 against the torch-derived thresholds."""
+import ctypes
+import json
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from _util import GOLDEN, assert_bits, golden
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SHIM = os.path.join(HERE, "host", "numerics_shim.cpp")
+LIB = os.path.join(HERE, "host", "_build", "libnumerics_shim.so")
+
+
+@pytest.fixture(scope="module")
+def shim():
+    os.makedirs(os.path.dirname(LIB), exist_ok=True)
+    src_mtime = max(os.path.getmtime(SHIM), os.path.getmtime(
+        os.path.join(HERE, "..", "microscaling-quant_b200", "csrc", "numerics.cuh")))
+    if not os.path.exists(LIB) or os.path.getmtime(LIB) < src_mtime:
+        subprocess.run(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math",
+                        "-o", LIB, SHIM], check=True)
+    return ctypes.CDLL(LIB)
+
+
+class _Proxy:
+    """Routes the oracle's o_* calls to the shim's h_* twins."""
+
+    def __init__(self, cdll):
+        self.c = cdll
+
+    def __getattr__(self, name):
+        return getattr(self.c, "h_" + name[2:])
+
+
+@pytest.fixture()
+def host(oracle, shim):
+    saved = oracle._lib
+    oracle._lib = _Proxy(shim)
+    yield oracle
+    oracle._lib = saved
+
+
+def test_host_numerics_golden(host):
+    """The same fixtures tests/test_oracle_golden.py pins the oracle with, through numerics.cuh."""
+    import test_oracle_golden as t
+    for fn in (t.test_float_em_f32, t.test_float_em_f64, t.test_round_bits_int_bf16, t.test_microsoft,
+               t.test_scale_rules, t.test_arith):
+        fn(host)
+
+
+def test_host_numerics_random_vs_oracle(oracle, shim):
+    """Random bit patterns and grid-valued operands: numerics.cuh and the oracle agree everywhere."""
+    rng = np.random.default_rng(11)
+    z = rng.integers(0, 2 ** 32, 400000, dtype=np.uint64).astype(np.uint32).view(np.float32)
+    ref = {}
+    for grid in ("qtorch", "ieee", "ocp"):
+        ems = [(4, 3), (5, 2), (3, 2), (2, 3), (2, 1)] if grid == "ocp" else [(4, 4), (4, 6), (8, 7), (5, 10), (3, 3)]
+        for mode in ("ties_away", "rne", "truncate"):
+            for e, m in ems:
+                ref[(grid, mode, e, m)] = oracle.float_em(z, e, m, mode, grid)
+    saved = oracle._lib
+    oracle._lib = _Proxy(shim)
+    try:
+        for (grid, mode, e, m), want in ref.items():
+            assert_bits(oracle.float_em(z, e, m, mode, grid), want, f"{grid}/{mode}/{e}/{m}")
+    finally:
+        oracle._lib = saved
+    for fmt in ("MXFP8_E4M3", "MXFP6_E2M3", "MXFP4"):
+        for mode in ("nearest", "even", "floor"):
+            want = oracle.microsoft(z, fmt, mode, True)
+            oracle._lib = _Proxy(shim)
+            try:
+                assert_bits(oracle.microsoft(z, fmt, mode, True), want, f"ms/{fmt}/{mode}")
+            finally:
+                oracle._lib = saved
+
+
+def test_log2_thresholds_match_torch(shim):
+    """floor_log2_rn's thresholds equal the ones measured from torch.floor(torch.log2(x)) over all float32."""
+    want = json.load(open(os.path.join(GOLDEN, "log2_floor.json")))["thresholds"]
+    out = np.zeros(278, np.uint32)
+    shim.h_log2_thresholds(out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
+    got = {k: int(out[k + 149]) for k in range(-149, 129)}
+    assert {int(k): v for k, v in want.items()} == got
+
+
+def test_log2_exhaustive_vs_libm(shim):
+    """floor_log2_rn against floor((float)log2((double)x)) on every positive finite float32."""
+    f = shim.h_log2_mismatches
+    f.restype = ctypes.c_int64
+    from concurrent.futures import ThreadPoolExecutor
+    cuts = np.linspace(1, 0x7F800000, 9).astype(np.int64)
+    with ThreadPoolExecutor(8) as ex:
+        bad = sum(ex.map(lambda i: f(ctypes.c_uint32(int(cuts[i])), ctypes.c_uint32(int(cuts[i + 1]))), range(8)))
+    assert bad == 0
