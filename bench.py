@@ -1,0 +1,363 @@
+"""Benchmark of the mxq B200 hot path (the driver's bench contract).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 ... bench.py --gpus N ...
+
+Headline ("quantize GB/s"): the block-quantizer sweep. A step quantizes one float32
+8192 x 8192 matrix -- N(0,1) x 2^U[-20,20] per row, 1% exact zeros, 0.1% float32-subnormal values -- with each of
+block.mxquant / block.mxgemmini / block.ocp, each of the five MX formats, along axis 0 and axis 1: 30 fused kernel
+launches. Throughput counts the algorithmic bytes of the reference's contract, 8.125 B per element (read V, write
+P, write X once per 32 elements). Every rank quantizes its own row shard (weak scaling, no collective).
+
+Beside it, in the same JSON line, `systolic`: config 3's 4096^3 MXFP8_E4M3 systolic GEMM (MXGEMMINI / HW_FINAL,
+operands quantized by block.mxgemmini) in emulated GMAC/s, each rank reducing its own 4096-column panel of B.
+
+`e2e` runs the same sweep through the public API from pinned host buffers: every quantization's V is copied in and
+its P and X copied out inside the timed region. `cpu_baseline` times the CPU oracle (oracle/, a C restatement of the
+reference algorithm; the reference itself is Python and does not travel) on a row slice of the same workload.
+`--impl reference` is the reference arm: the oracle on all host cores, rank 0 only, same metric and unit.
+"""
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "microscaling-quant_b200"), os.path.join(ROOT, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+
+FAMILIES = ("mxquant", "mxgemmini", "ocp")
+FORMATS = ("MXFP8_E4M3", "MXFP8_E5M2", "MXFP6_E3M2", "MXFP6_E2M3", "MXFP4")
+ROWS, COLS = 8192, 8192
+BYTES_PER_ELEM = 8.125
+GEMM = 4096
+METRIC = "bit-exact MX block-quantize GB/s (config 2 sweep: 3 quantizers x 5 formats x 2 axes)"
+HW_FINAL = [(4, 4)] * 8 + [(4, 5)] * 2 + [(4, 6)] * 5 + [(8, 7)]
+
+
+def peaks():
+    """Measured peaks (MEASURED_PEAKS.json, written by the driver), else the pool's fallback figures."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        p = json.load(open(path))
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def synthetic(rows, cols, seed, device=None):
+    """config 2's matrix, generated on the device (torch) or the host (numpy) from a seed."""
+    import torch
+    g = torch.Generator(device=device or "cpu").manual_seed(seed)
+    V = torch.randn(rows, cols, generator=g, device=device) * torch.exp2(
+        torch.rand(rows, 1, generator=g, device=device) * 40 - 20)
+    zero = torch.rand(rows, cols, generator=g, device=device) < 0.01
+    V[zero] = 0.0
+    sub = torch.rand(rows, cols, generator=g, device=device) < 0.001
+    mag = (torch.rand(rows, cols, generator=g, device=device) * (2.0 ** -126 - 2.0 ** -149) + 2.0 ** -149)
+    V[sub] = (torch.sign(V) * mag)[sub]
+    return V.contiguous()
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=lambda: self.lines.extend(self.proc.stdout), daemon=True)
+            self.reader.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except Exception:
+                self.proc.kill()
+            self.reader.join(2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def traffic_table():
+    """DRAM bytes per launch of the sweep's kernels from the committed ncu summary (profiles/), else {}."""
+    path = os.path.join(ROOT, "profiles", "quantize_traffic.json")
+    try:
+        return json.load(open(path))
+    except Exception:
+        return {}
+
+
+# ------------------------------------------------------------------------------------------------ GPU arm
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+    import mxq
+    from mxq import block, matmul, schedule
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    quant = {"mxquant": block.mxquant.quantize, "mxgemmini": block.mxgemmini.quantize, "ocp": block.ocp.quantize}
+    V = synthetic(ROWS, COLS, 1000 + rank, dev)             # this rank's row shard of the global matrix
+    runs = [(f, fmt, ax) for f in FAMILIES for fmt in FORMATS for ax in (0, 1)]
+
+    def step():
+        for f, fmt, ax in runs:
+            quant[f](V, fmt, axis=ax)
+
+    # -- device-resident sweep: per-launch CUDA events on the launching stream, then the whole timed loop
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    per = {}
+    for f, fmt, ax in runs:                                 # per-kernel launch durations (after warm-up)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * 3)]
+        for i in range(3):
+            ev[2 * i].record(stream)
+            quant[f](V, fmt, axis=ax)
+            ev[2 * i + 1].record(stream)
+        torch.cuda.synchronize()
+        per[(f, fmt, ax)] = sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(3)) / 3
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        barrier()
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        barrier()
+    ms = max_over_ranks(start.elapsed_time(end))
+    ms_step = ms / args.steps
+    elems = ROWS * COLS
+    total_bytes = BYTES_PER_ELEM * elems * len(runs) * world
+    value = total_bytes / (ms_step * 1e-3) / 1e9
+
+    # dominant kernel: the (family, axis) pair with the largest share of the sweep
+    by_kernel = {}
+    for (f, fmt, ax), t in per.items():
+        by_kernel.setdefault((f, ax), []).append(t)
+    dom, dom_ms = max(((k, sum(v)) for k, v in by_kernel.items()), key=lambda kv: kv[1])
+    dom_avg = dom_ms / len(by_kernel[dom])
+    hbm, peak_kind = peaks()
+    achieved = BYTES_PER_ELEM * elems / (dom_avg * 1e-3) / 1e9
+    kname = f"{dom[0]}/axis{dom[1]}"
+    tr = traffic_table().get(kname)
+
+    # -- end to end through the public API from pinned host buffers
+    Vh = V.cpu().pin_memory()
+    Ph = torch.empty_like(Vh).pin_memory()
+    Xh0 = torch.empty((ROWS // 32, COLS), dtype=torch.float32).pin_memory()
+    Xh1 = torch.empty((ROWS, COLS // 32), dtype=torch.float32).pin_memory()
+    e2e_steps = max(1, min(3, args.steps))
+
+    def e2e_step():
+        for f, fmt, ax in runs:
+            Vd = Vh.to(dev, non_blocking=True)
+            P, X = quant[f](Vd, fmt, axis=ax)
+            Ph.copy_(P, non_blocking=True)
+            (Xh0 if ax == 0 else Xh1).copy_(X, non_blocking=True)
+
+    e2e_step()
+    barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e2.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2)) / e2e_steps
+    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
+    h2d = 4 * elems * len(runs)
+    d2h = (4 * elems + 4 * elems // 32) * len(runs)
+
+    # -- config 3: the systolic GEMM, one 4096-column panel per rank
+    gsteps = max(1, args.gemm_steps)
+    gen = torch.Generator(device=dev).manual_seed(7)
+    A = torch.randn(GEMM, GEMM, generator=gen, device=dev)
+    B = torch.randn(GEMM, GEMM, generator=torch.Generator(device=dev).manual_seed(8 + rank), device=dev)
+    arith = matmul.MXGEMMINI()
+
+    def gemm():
+        P_A, X_A = block.mxgemmini.quantize(A, "MXFP8_E4M3", axis=0)
+        P_B, X_B = block.mxgemmini.quantize(B, "MXFP8_E4M3", axis=0)
+        return matmul.systolic(P_A, X_A, P_B, X_B, arith, schedule.HW_FINAL)
+
+    for _ in range(max(1, args.warmup // 2)):
+        gemm()
+    barrier()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    for _ in range(gsteps):
+        gemm()
+    g1.record(stream)
+    barrier()
+    gms = max_over_ranks(g0.elapsed_time(g1)) / gsteps
+    gmacs = GEMM ** 3 * world / (gms * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_rows)
+    clocks = clk.summary()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded config-2 distribution, generated on device)",
+        "config": {"workload": "config 2: block.{mxquant,mxgemmini,ocp}.quantize x 5 MX formats x axis {0,1} on an "
+                               "8192x8192 fp32 matrix per GPU", "rows_per_gpu": ROWS, "cols": COLS,
+                   "launches_per_step": len(runs), "bytes_per_element": BYTES_PER_ELEM,
+                   "l2": "inputs (256 MiB per matrix) larger than L2; no flush", "parallelism": f"rows x{world}"},
+        "roofline": {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1), "peak": hbm,
+                     "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "traffic": tr},
+        "kernels": {f"{f}/{fmt}/axis{ax}": round(BYTES_PER_ELEM * elems / (t * 1e-3) / 1e9, 1)
+                    for (f, fmt, ax), t in sorted(per.items())},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms, 3)},
+        "gpu_launches": len(runs) * args.steps,
+        "clocks": clocks,
+        "systolic": {"metric": "bit-exact MX systolic-emulated GMAC/s", "value": round(gmacs, 2), "unit": "GMAC/s",
+                     "workload": f"config 3: quantize A, B ({GEMM}x{GEMM} MXFP8_E4M3, block.mxgemmini) + "
+                                 f"systolic MXGEMMINI/HW_FINAL {GEMM}^3 per GPU", "ms_per_gemm": round(gms, 3),
+                     "steps": gsteps},
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------- CPU oracle
+def cpu_sweep_sample(rows, threads):
+    """The sweep on a `rows` x 8192 slice with the CPU oracle; returns (GB/s, seconds, elements)."""
+    import oracle
+    import torch
+    V = synthetic(rows, COLS, 1000).numpy()
+    t0 = time.perf_counter()
+    for f in FAMILIES:
+        for fmt in FORMATS:
+            for ax in (0, 1):
+                oracle.block_quantize(V, f, fmt, ax, threads=threads)
+    dt = time.perf_counter() - t0
+    return BYTES_PER_ELEM * V.size * 30 / dt / 1e9, dt
+
+
+def cpu_baseline(rows):
+    threads = os.cpu_count() or 1
+    gbs, dt = cpu_sweep_sample(rows, threads)
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"the same 30-run sweep on a {rows}x{COLS} row slice ({dt:.1f} s), CPU oracle (C restatement "
+                      "of the reference algorithm), float32, all host threads"}
+
+
+def run_reference(args):
+    """The reference arm: the CPU restatement timed on the host cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_sweep_sample(args.ref_rows, threads)
+    t0 = time.perf_counter()
+    per = []
+    for _ in range(args.steps):
+        gbs, dt = cpu_sweep_sample(args.ref_rows, threads)
+        per.append(dt)
+    total = time.perf_counter() - t0
+    value = BYTES_PER_ELEM * args.ref_rows * COLS * 30 * args.steps / total / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded config-2 distribution)",
+        "config": {"workload": "config 2: block.{mxquant,mxgemmini,ocp}.quantize x 5 MX formats x axis {0,1}",
+                   "rows_per_step": args.ref_rows, "cols": COLS, "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"each step: the 30-run sweep on a {args.ref_rows}x{COLS} row slice with the CPU "
+                                   "oracle (the reference is pure Python/torch and is not installed on the GPU box; "
+                                   "its measured CPU rate is 0.03-1.5 GB/s per quantizer)"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="mxq_b200", choices=["mxq_b200", "reference"])
+    ap.add_argument("--gemm-steps", type=int, default=3)
+    ap.add_argument("--cpu-rows", type=int, default=2048, help="rows of the CPU-baseline slice")
+    ap.add_argument("--ref-rows", type=int, default=256, help="rows per reference-arm step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -564,4 +564,47 @@ MXQ_HD float ar_tile_add(const ArithP& A, float C, float t) {
   return exact_add_rne(lane_round(C, 8, 7), lane_round(t, 8, 7), 8, 7);
 }
 
+// ------------------------------------------------------------------ fast forms for the block quantizer
+// The same results as q_ocp_f / q_microsoft for EVERY float32 input (checked exhaustively on the host against
+// them), with the powers of two built from the exponent field: the scale factors of these grids are always normal
+// float32 numbers, and the two exact power-of-two multiplications of the microxcaling step fold into one.
+MXQ_HD float round_nonneg(float k, int mode) {        // round_int of a value >= 0
+  if (mode == RM_RNE) return rint_f(k);
+  if (mode == RM_TRUNCATE) return trunc_f(k);
+  return floor_f(add_rn(k, 0.5f));
+}
+MXQ_HD float q_ocp_bits(float x, int e, int m, int mode, float max_norm) {
+  uint32_t u = f2u(x), a = u & 0x7fffffffu;
+  int emin_b = 128 - bias_of(e);                       // biased emin; float32 subnormals read biased 0
+  int eb = (int)(a >> 23);
+  eb = eb > emin_b ? eb : emin_b;
+  int sb = eb - m;                                     // biased exponent of the step 2^s (normal)
+  float k = round_nonneg(mul_rn(u2f(a), u2f((uint32_t)(254 - sb) << 23)), mode);
+  float val = fminf(mul_rn(k, u2f((uint32_t)sb << 23)), max_norm);
+  float r = u2f(f2u(val) | (u & 0x80000000u));
+  return a == 0u ? 0.0f : (a >= 0x7f800000u ? x : r);
+}
+// q_microsoft with saturate_normals=True and exp_bits > 0
+MXQ_HD float q_microsoft_sat(float A, int bits, int exp_bits, float max_norm, int round) {
+  uint32_t u = f2u(A), a = u & 0x7fffffffu;
+  if (a >= 0x7f7fffd4u) return q_microsoft(A, bits, exp_bits, max_norm, round, true);  // inf, NaN, log2 -> 128
+  int min_exp = 2 - (1 << (exp_bits - 1));
+  int pe = a ? floor_log2_rn(u2f(a)) : 0;              // floor(log2(|A| + (A == 0)))
+  pe = pe > min_exp ? pe : min_exp;
+  float t = mul_rn(A, u2f((uint32_t)(125 + bits - pe) << 23));          // A / 2^pe * 2^(bits-2)
+  float absA = abs_f(t), r;
+  if (round == MS_FLOOR) {
+    r = floor_f(absA);
+  } else if (round == MS_NEAREST) {
+    r = floor_f(add_rn(absA, 0.5f));
+  } else {
+    float y = sub_rn(absA, 0.5f), h = mul_rn(y, 0.5f);
+    r = sub_rn(floor_f(add_rn(absA, 0.5f)), (y >= 0.0f && floor_f(h) == h) ? 1.0f : 0.0f);
+  }
+  r = u2f(f2u(r) | (u & 0x80000000u));                 // sign(A) * r: -0 for a negative value rounding to zero
+  float out = mul_rn(r, u2f((uint32_t)(129 - bits + pe) << 23));        // / 2^(bits-2) * 2^pe
+  out = fminf(fmaxf(out, -max_norm), max_norm);
+  return a == 0u ? 0.0f : out;
+}
+
 }  // namespace mxq

@@ -5,8 +5,11 @@
 // Kernels (each templated on the quantizer family so the element step is inlined):
 //   k_rows32   inner == 1, block == 32, len % 32 == 0, 16-byte aligned: one float4 per thread, 8 lanes per block,
 //              the block max by three xor-shuffles; fully coalesced 128-bit loads and stores.
-//   k_cols32   inner > 1, block == 32: one thread per (block, column run of VEC columns); the 32 rows of a block
-//              are loaded into registers, so consecutive threads read consecutive columns (coalesced rows).
+//   k_cols_tile  inner % 4 == 0, block == 32, 16-byte aligned: one CTA per 32-row block x 256 columns; each thread
+//              keeps 8 float4 of 4 columns in registers, the four row groups' column maxima meet in shared memory,
+//              and every load and store is a coalesced 128-bit access along the rows.
+//   k_cols32   inner > 1 otherwise, block == 32: one thread per (block, column run of VEC columns); the 32 rows of a
+//              block are loaded into registers, so consecutive threads read consecutive columns (coalesced rows).
 //   k_generic  any block size or alignment: one thread per (outer, block, column), two passes over the block.
 #include "common.cuh"
 #include "numerics.cuh"
@@ -50,9 +53,9 @@ __device__ __forceinline__ float elem(float z, const QParams& q) {
   if (FAM == MXQ_FAMILY_MXQUANT) return q_qtorch(z, q.e, q.m, RM_TIES_AWAY);
   if (FAM == MXQ_FAMILY_MXGEMMINI) {
     if (q.via_e) z = q_ieee(z, q.via_e, q.via_m, q.rounding);
-    return q_ocp_f(z, q.e, q.m, q.rounding, q.max_norm);
+    return q_ocp_bits(z, q.e, q.m, q.rounding, q.max_norm);
   }
-  if (FAM == MXQ_FAMILY_OCP) return q_microsoft(z, q.bits, q.e, q.max_norm, q.rounding, true);
+  if (FAM == MXQ_FAMILY_OCP) return q_microsoft_sat(z, q.bits, q.e, q.max_norm, q.rounding);
   return z;
 }
 
@@ -182,6 +185,71 @@ __global__ void __launch_bounds__(kThreads) k_cols32(const float* __restrict__ V
 }
 
 template <int FAM>
+__global__ void __launch_bounds__(kThreads) k_cols_tile(const float* __restrict__ V, float* __restrict__ P,
+                                                        float* __restrict__ X, int64_t outer, int64_t len,
+                                                        int64_t inner, int64_t nb, QParams q) {
+  __shared__ float part[4][256];                      // column maxima of the four row groups (NaN: a NaN was seen)
+  const int tid = threadIdx.x, c4 = tid & 63, rg = tid >> 6;   // float4 column in the tile, row group 0..3
+  const int64_t inner4 = inner >> 2, ctiles = (inner4 + 63) >> 6, tiles = outer * nb * ctiles;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const int64_t ct = tile % ctiles, ob = tile / ctiles, b = ob % nb, o = ob / nb;
+    const int64_t col4 = ct * 64 + c4, l0 = b * 32;
+    const bool colok = col4 < inner4;
+    const int rows = (int)((len - l0) < 32 ? (len - l0) : 32);
+    const float4* src = reinterpret_cast<const float4*>(V + (o * len + l0) * inner) + col4;
+    float4* dst = reinterpret_cast<float4*>(P + (o * len + l0) * inner) + col4;
+    float4 v[8];
+    float mx[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    bool nan[4] = {false, false, false, false};
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int r = rg + 4 * i;
+      v[i] = (colok && r < rows) ? __ldcs(src + (int64_t)r * inner4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      const float c[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        nan[j] |= isnan_f(c[j]);
+        mx[j] = fmaxf(mx[j], abs_f(c[j]));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) part[rg][c4 * 4 + j] = nan[j] ? qnan_f() : mx[j];
+    __syncthreads();
+    float x[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      float a = 0.0f;
+      bool n = false;
+#pragma unroll
+      for (int g = 0; g < 4; g++) {
+        float p = part[g][c4 * 4 + j];
+        n |= isnan_f(p);
+        a = fmaxf(a, p);
+      }
+      x[j] = (FAM == MXQ_FAMILY_FP32) ? 1.0f : block_scale<FAM>(n ? qnan_f() : a, q);
+    }
+    if (rg == 0 && colok)
+      *reinterpret_cast<float4*>(X + (o * nb + b) * inner + col4 * 4) = make_float4(x[0], x[1], x[2], x[3]);
+    if (FAM != MXQ_FAMILY_FP32) {
+      const Divider d0(x[0]), d1(x[1]), d2(x[2]), d3(x[3]);
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        v[i].x = elem<FAM>(d0.template operator()<FAM>(v[i].x), q);
+        v[i].y = elem<FAM>(d1.template operator()<FAM>(v[i].y), q);
+        v[i].z = elem<FAM>(d2.template operator()<FAM>(v[i].z), q);
+        v[i].w = elem<FAM>(d3.template operator()<FAM>(v[i].w), q);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const int r = rg + 4 * i;
+      if (colok && r < rows) __stcs(dst + (int64_t)r * inner4, v[i]);
+    }
+    __syncthreads();                                   // part[] is rewritten by the next tile
+  }
+}
+
+template <int FAM>
 __global__ void __launch_bounds__(kThreads) k_generic(const float* __restrict__ V, float* __restrict__ P,
                                                       float* __restrict__ X, int64_t outer, int64_t len, int64_t inner,
                                                       int64_t block, int64_t nb, QParams q) {
@@ -214,9 +282,10 @@ int launch_quant(const float* V, float* P, float* X, int64_t outer, int64_t len,
     k_rows32<FAM><<<grid_for(nquads, kThreads, 16), kThreads, 0, st>>>(
         reinterpret_cast<const float4*>(V), reinterpret_cast<float4*>(P), X, nquads, q);
   } else if (block == 32 && inner > 1) {
-    if (inner % 4 == 0 && al16) {
-      int64_t n = outer * nb * (inner / 4);
-      k_cols32<FAM, 4><<<grid_for(n, kThreads, 8), kThreads, 0, st>>>(V, P, X, outer, len, inner, nb, q);
+    if (inner % 4 == 0 && al16 && (uintptr_t)X % 16 == 0) {
+      int64_t tiles = outer * nb * ((inner / 4 + 63) / 64);
+      unsigned grid = (unsigned)(tiles < (int64_t)sm_count() * 6 ? tiles : (int64_t)sm_count() * 6);
+      k_cols_tile<FAM><<<grid, kThreads, 0, st>>>(V, P, X, outer, len, inner, nb, q);
     } else if (inner % 2 == 0 && (uintptr_t)V % 8 == 0 && (uintptr_t)P % 8 == 0) {
       int64_t n = outer * nb * (inner / 2);
       k_cols32<FAM, 2><<<grid_for(n, kThreads, 8), kThreads, 0, st>>>(V, P, X, outer, len, inner, nb, q);

@@ -198,7 +198,7 @@ PLACEMENTS = {"top": 0, "below_top": 1, "no_clip": 2}
 
 
 def block_quantize(V, family, fmt, axis=0, block_size=32, rounding_mode=None, scale_floor=1e-38, via=None,
-                   scale_bits=8, placement="top"):
+                   scale_bits=8, placement="top", threads=None):
     """block.<family>.quantize(V, fmt, axis, block_size, ...) -> (P, X), as mxq/block/_driver.py:45-66 lays them out."""
     V = _f32(V)
     axis = axis % V.ndim
@@ -218,8 +218,27 @@ def block_quantize(V, family, fmt, axis=0, block_size=32, rounding_mode=None, sc
     xshape = list(V.shape)
     xshape[axis] = nb
     X = np.empty(xshape, np.float32)
-    lib().o_block_quantize(_p(V, P_F32), I64(outer), I64(L), I64(inner), I64(block_size), ctypes.byref(spec),
-                           _p(P, P_F32), _p(X, P_F32))
+    f = lib().o_block_quantize
+    if outer > 1:
+        # independent [len, inner] slabs: split them over threads
+        def run(a, b):
+            f(_p(V[a:b] if axis > 0 else V, P_F32), I64(b - a), I64(L), I64(inner), I64(block_size),
+              ctypes.byref(spec), _p(P[a:b] if axis > 0 else P, P_F32), _p(X[a:b] if axis > 0 else X, P_F32))
+        if axis > 0 and V.shape[0] == outer:
+            _run_rows(run, outer, threads)
+            return P, X
+    elif inner > 1 and V.ndim == 2 and axis == 0:
+        # blocks run down the columns: split the columns over threads (strided slabs, copied per thread)
+        def run(a, b):
+            v = np.ascontiguousarray(V[:, a:b])
+            p = np.empty_like(v)
+            x = np.empty((nb, b - a), np.float32)
+            f(_p(v, P_F32), I64(1), I64(L), I64(b - a), I64(block_size), ctypes.byref(spec), _p(p, P_F32), _p(x, P_F32))
+            P[:, a:b] = p
+            X[:, a:b] = x
+        _run_rows(run, inner, threads)
+        return P, X
+    f(_p(V, P_F32), I64(outer), I64(L), I64(inner), I64(block_size), ctypes.byref(spec), _p(P, P_F32), _p(X, P_F32))
     return P, X
 
 

@@ -70,3 +70,17 @@ X void h_log2_thresholds(uint32_t* out) {
     out[k + 149] = lo;
   }
 }
+// the block quantizer's fast element forms against the general ones, over bit patterns lo, lo+stride, ... < hi
+X int64_t h_fast_forms_mismatches(uint64_t lo, uint64_t hi, uint64_t stride, int which, int e, int m, int mode) {
+  int64_t bad = 0;
+  float mn = ocp_max_norm(e, m);
+  for (uint64_t v = lo; v < hi; v += stride) {
+    float x = u2f((uint32_t)v);
+    float a, b;
+    if (which == 0) { a = q_ocp_bits(x, e, m, mode, mn); b = q_ocp_f(x, e, m, mode, mn); }
+    else { a = q_microsoft_sat(x, m + 2, e, mn, mode); b = q_microsoft(x, m + 2, e, mn, mode, true); }
+    bool an = (f2u(a) & 0x7fffffffu) > 0x7f800000u, bn = (f2u(b) & 0x7fffffffu) > 0x7f800000u;
+    if (an != bn || (!an && f2u(a) != f2u(b))) bad++;
+  }
+  return bad;
+}

@@ -98,3 +98,20 @@ def test_log2_exhaustive_vs_libm(shim):
     with ThreadPoolExecutor(8) as ex:
         bad = sum(ex.map(lambda i: f(ctypes.c_uint32(int(cuts[i])), ctypes.c_uint32(int(cuts[i + 1]))), range(8)))
     assert bad == 0
+
+
+@pytest.mark.parametrize("which", [0, 1], ids=["ocp_grid", "microsoft"])
+def test_fast_forms_match_general(shim, which):
+    """The block quantizer's bit-level element forms (q_ocp_bits, q_microsoft_sat) equal the general functions
+    on a dense stride through all 2^32 float32 patterns, for every OCP format and rounding mode."""
+    f = shim.h_fast_forms_mismatches
+    f.restype = ctypes.c_int64
+    f.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                  ctypes.c_int]
+    from concurrent.futures import ThreadPoolExecutor
+    stride, chunk = 4099, 1 << 29                      # 8 chunks of the 2^32 patterns per (format, mode)
+    jobs = [(lo, e, m, mode) for (e, m) in [(4, 3), (5, 2), (3, 2), (2, 3), (2, 1)] for mode in range(3)
+            for lo in range(0, 1 << 32, chunk)]
+    with ThreadPoolExecutor(8) as ex:
+        bad = sum(ex.map(lambda j: f(j[0], j[0] + chunk, stride, which, j[1], j[2], j[3]), jobs))
+    assert bad == 0
