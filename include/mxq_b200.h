@@ -152,6 +152,11 @@ int mxq_anchor_tree(const float* PA, const float* XA, const float* PB, const flo
 int mxq_fp64_accum(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
                    int64_t N, int64_t block, void* stream);
 
+/* ------------------------------------------------------------------------------------------ diagnostics */
+/* No reference counterpart: the number of bounded shared-memory waits (mbarrier) that gave up in the TMA-staged
+ * kernels on the current device since the library was loaded. Always 0 in a correct run; synchronous. */
+int mxq_device_timeouts(uint32_t* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -2,7 +2,8 @@
 // HBM (read V once, write P once, write X once per block). A tensor is viewed as [outer, len, inner] with blocks of
 // `block` along len.
 //
-// Kernels (each templated on the quantizer family so the element step is inlined):
+// Kernels (each templated on the quantizer family so the element step is inlined). The TMA-staged kernel of
+// quantize_tma.cu takes every layout it can map; these register kernels cover the rest:
 //   k_rows32   inner == 1, block == 32, len % 32 == 0, 16-byte aligned: one float4 per thread, 8 lanes per block,
 //              the block max by three xor-shuffles; fully coalesced 128-bit loads and stores.
 //   k_cols_tile  inner % 4 == 0, block == 32, 16-byte aligned: one CTA per 32-row block x 256 columns; each thread
@@ -15,6 +16,11 @@
 #include "numerics.cuh"
 
 using namespace mxq;
+
+namespace mxq {
+int quantize_tma(const float* V, float* P, float* X, int64_t outer, int64_t len, int64_t inner, int64_t block,
+                 const mxq_quant_spec& s, cudaStream_t st);
+}
 
 namespace {
 
@@ -274,7 +280,9 @@ __global__ void __launch_bounds__(kThreads) k_generic(const float* __restrict__ 
 
 template <int FAM>
 int launch_quant(const float* V, float* P, float* X, int64_t outer, int64_t len, int64_t inner, int64_t block,
-                 const QParams& q, cudaStream_t st) {
+                 const QParams& q, const mxq_quant_spec& spec, cudaStream_t st) {
+  int r = quantize_tma(V, P, X, outer, len, inner, block, spec, st);
+  if (r != MXQ_ERR_UNSUPPORTED) return r;
   int64_t nb = (len + block - 1) / block;
   bool al16 = ((uintptr_t)V % 16 == 0) && ((uintptr_t)P % 16 == 0);
   if (block == 32 && inner == 1 && len % 32 == 0 && al16) {
@@ -383,10 +391,10 @@ int mxq_block_quantize(const float* V, float* P, float* X, int64_t outer, int64_
   QParams q = make_params(s);
   cudaStream_t st = as_stream(stream);
   switch (s.family) {
-    case MXQ_FAMILY_FP32: return launch_quant<MXQ_FAMILY_FP32>(V, P, X, outer, len, inner, block, q, st);
-    case MXQ_FAMILY_MXQUANT: return launch_quant<MXQ_FAMILY_MXQUANT>(V, P, X, outer, len, inner, block, q, st);
-    case MXQ_FAMILY_MXGEMMINI: return launch_quant<MXQ_FAMILY_MXGEMMINI>(V, P, X, outer, len, inner, block, q, st);
-    default: return launch_quant<MXQ_FAMILY_OCP>(V, P, X, outer, len, inner, block, q, st);
+    case MXQ_FAMILY_FP32: return launch_quant<MXQ_FAMILY_FP32>(V, P, X, outer, len, inner, block, q, s, st);
+    case MXQ_FAMILY_MXQUANT: return launch_quant<MXQ_FAMILY_MXQUANT>(V, P, X, outer, len, inner, block, q, s, st);
+    case MXQ_FAMILY_MXGEMMINI: return launch_quant<MXQ_FAMILY_MXGEMMINI>(V, P, X, outer, len, inner, block, q, s, st);
+    default: return launch_quant<MXQ_FAMILY_OCP>(V, P, X, outer, len, inner, block, q, s, st);
   }
 }
 

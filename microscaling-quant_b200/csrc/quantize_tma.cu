@@ -1,0 +1,281 @@
+// The block quantizers' main kernel on sm_100a: persistent CTAs stream 32 x 256 float32 tiles of V through shared
+// memory with TMA (cp.async.bulk.tensor, two stages, mbarrier-tracked), so each tile's load overlaps the previous
+// tile's arithmetic, and one pass over HBM reads V once and writes P and X once.
+//
+// Two layouts of the [outer, len, inner] view (blocks of 32 along len):
+//   ROWS (inner == 1): a tile is 32 rows x 256 consecutive values of a row, i.e. 8 blocks per row;
+//   COLS (inner > 1):  a tile is one block of 32 rows (along len) x 256 columns (along inner).
+// Per tile: (1) one thread per block takes the block max from shared memory and computes the block's scale and
+// reciprocal (ROWS: a thread reads its block's 8 float4 in a rotated order, so a quarter-warp hits 32 distinct
+// banks; COLS: a thread walks its column); (2) every thread quantizes 8 float4 of the tile, reading values and
+// scales from shared memory and writing P with coalesced 128-bit streaming stores.
+// The element format is a template parameter, so the grid constants of each format fold into immediates.
+#include "common.cuh"
+#include "numerics.cuh"
+#include "tma.cuh"
+
+using namespace mxq;
+
+namespace {
+
+constexpr int TR = 32, TC = 256, NT = 256, STAGES = 2;
+constexpr unsigned TILE_BYTES = TR * TC * sizeof(float);
+
+struct TParams {
+  int rounding, placement, via_e, via_m;
+  float scale_floor, scale_emax;
+};
+
+template <int E, int M>
+struct Fmt {
+  static constexpr int BIAS = (1 << (E - 1)) - 1;
+  static constexpr float MAX_NORM = (E == 4 && M == 3) ? 448.0f
+                                    : (E == 5 && M == 2) ? 57344.0f
+                                    : (E == 3 && M == 2) ? 28.0f
+                                    : (E == 2 && M == 3) ? 7.5f
+                                                         : 6.0f;
+  static constexpr int EMAX = (E == 5) ? 15 : (E == 4) ? 8 : (E == 3) ? 4 : 2;   // microxcaling emax
+};
+
+// float_em._qtorch ties away (mxq/element_quant/float_em.py:64-84), constants folded
+template <int E, int M>
+__device__ __forceinline__ float qtorch_ties_away(float z) {
+  constexpr uint32_t drop = 23 - M, half = 1u << (drop - 1), mask = ~((1u << drop) - 1u);
+  constexpr uint32_t L = (1u << (E - 1)) - 1u, mins = 127u - L, maxs = 127u + L;
+  constexpr uint32_t MAXMAG = (maxs << 23) | (0x007fffffu & mask), MINMAG = mins << 23;
+  constexpr uint32_t MID = (mins - 1u) << 23, OVF = (maxs + 1u) << 23;
+  const uint32_t u = f2u(z), q = (u + half) & mask, qm = q & 0x7fffffffu, s = u & 0x80000000u;
+  uint32_t r = q;
+  if (qm >= OVF) r = s | MAXMAG;
+  if (qm < MINMAG) r = qm > MID ? (s | MINMAG) : 0u;
+  return u2f(r);
+}
+
+// float_em._ocp (float_em.py:113-134): q_ocp_bits with the format's constants folded
+template <int E, int M>
+__device__ __forceinline__ float ocp_grid(float x, int mode) {
+  constexpr int EMIN_B = 128 - Fmt<E, M>::BIAS;
+  const uint32_t u = f2u(x), a = u & 0x7fffffffu;
+  int eb = (int)(a >> 23);
+  eb = eb > EMIN_B ? eb : EMIN_B;
+  const int sb = eb - M;
+  const float k = round_nonneg(__fmul_rn(u2f(a), u2f((uint32_t)(254 - sb) << 23)), mode);
+  const float val = fminf(__fmul_rn(k, u2f((uint32_t)sb << 23)), Fmt<E, M>::MAX_NORM);
+  const float r = u2f(f2u(val) | (u & 0x80000000u));
+  return a == 0u ? 0.0f : (a >= 0x7f800000u ? x : r);
+}
+
+template <int FAM, int E, int M>
+__device__ __forceinline__ float element(float z, const TParams& p) {
+  if (FAM == MXQ_FAMILY_MXQUANT) return qtorch_ties_away<E, M>(z);
+  if (FAM == MXQ_FAMILY_MXGEMMINI) return ocp_grid<E, M>(z, p.rounding);
+  return q_microsoft_sat(z, M + 2, E, Fmt<E, M>::MAX_NORM, p.rounding);
+}
+
+template <int FAM, int E, int M>
+__device__ __forceinline__ float block_scale(float amax, const TParams& p) {
+  if (FAM == MXQ_FAMILY_MXQUANT || FAM == MXQ_FAMILY_MXGEMMINI) return scale_mxquant(amax, p.scale_floor);
+  if (p.placement == 0) return scale_ocp(amax, Fmt<E, M>::EMAX, p.scale_emax);
+  if (p.placement == 1) return scale_ocp(amax, Fmt<E, M>::EMAX - 1, p.scale_emax);
+  return scale_ocp_no_clip(amax, E, M, p.rounding, p.scale_emax);
+}
+
+// the reciprocal that turns v / X into an exact multiply, or 0 when the division must be a division (X not a
+// normal power of two, or -- for the qtorch family, whose codes see NaN sign bits -- a block holding a NaN)
+template <int FAM>
+__device__ __forceinline__ float reciprocal_of(float x, bool nan_block) {
+  const uint32_t u = f2u(x);
+  const bool pow2 = ((u & 0x807fffffu) == 0u && u >= 0x00800000u && u < 0x7f800000u) || u == 0x00400000u;
+  if (!pow2 || (FAM == MXQ_FAMILY_MXQUANT && nan_block)) return 0.0f;
+  return pow2f(-ilogb_f(x));
+}
+
+template <int FAM>
+__device__ __forceinline__ float divide(float v, float x, float r) {
+  if (r != 0.0f) return __fmul_rn(v, r);
+  return FAM == MXQ_FAMILY_MXQUANT ? x86_div(v, x) : div_rn(v, x);
+}
+
+template <int FAM, int E, int M, bool COLS>
+__global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtensorMap tmap, float* __restrict__ P,
+                                                  float* __restrict__ X, int64_t outer, int64_t len, int64_t inner,
+                                                  TParams prm) {
+  extern __shared__ __align__(128) float tiles[];            // [STAGES][TR][TC]
+  __shared__ __align__(8) uint64_t bars[STAGES];
+  __shared__ float s_x[NT], s_r[NT];
+
+  const int tid = threadIdx.x;
+  // tile grid: ROWS -> (row tiles, column tiles) of the [outer, len] matrix; COLS -> (outer, blocks, column tiles)
+  const int64_t nb = (len + TR - 1) / TR;
+  const int64_t ctiles = COLS ? (inner + TC - 1) / TC : (len + TC - 1) / TC;
+  const int64_t ntiles = COLS ? outer * nb * ctiles : ((outer + TR - 1) / TR) * ctiles;
+
+  auto issue = [&](int64_t tile, int stage) {
+    const int64_t ct = tile % ctiles, rest = tile / ctiles;
+    float* dst = tiles + stage * TR * TC;
+    fence_proxy_async();
+    mbar_expect_tx(&bars[stage], TILE_BYTES);
+    if (COLS) tma_load_3d(dst, &tmap, (int)(ct * TC), (int)((rest % nb) * TR), (int)(rest / nb), &bars[stage]);
+    else tma_load_2d(dst, &tmap, (int)(ct * TC), (int)(rest * TR), &bars[stage]);
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; s++) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int s = 0; s < STAGES; s++)
+      if (blockIdx.x + (int64_t)s * gridDim.x < ntiles) issue(blockIdx.x + (int64_t)s * gridDim.x, s);
+
+  int k = 0;
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, k++) {
+    const int stage = k % STAGES;
+    // every thread waits; the CTA leaves together if the (bounded) wait gave up anywhere
+    if (!__syncthreads_and(mbar_wait(&bars[stage], (unsigned)(k / STAGES) & 1u))) return;
+    const float* T = tiles + stage * TR * TC;
+    const int64_t ct = tile % ctiles, rest = tile / ctiles;
+
+    // (1) block scales
+    if (COLS) {
+      const int64_t b = rest % nb, o = rest / nb, col = ct * TC + tid;
+      float a = 0.0f;
+      bool nan = false;
+#pragma unroll 8
+      for (int r = 0; r < TR; r++) {
+        float v = T[r * TC + tid];
+        nan |= isnan_f(v);
+        a = fmaxf(a, abs_f(v));
+      }
+      const float x = block_scale<FAM, E, M>(nan ? qnan_f() : a, prm);
+      s_x[tid] = x;
+      s_r[tid] = reciprocal_of<FAM>(x, nan);
+      if (col < inner) X[(o * nb + b) * inner + col] = x;
+    } else {
+      const int row = tid >> 3, blk = tid & 7;                // 32 rows x 8 blocks
+      const float4* src = reinterpret_cast<const float4*>(T + row * TC + blk * 32);
+      float a = 0.0f;
+      bool nan = false;
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const float4 v = src[(i + tid) & 7];
+        nan |= isnan_f(v.x) | isnan_f(v.y) | isnan_f(v.z) | isnan_f(v.w);
+        a = fmaxf(a, fmaxf(fmaxf(abs_f(v.x), abs_f(v.y)), fmaxf(abs_f(v.z), abs_f(v.w))));
+      }
+      const float x = block_scale<FAM, E, M>(nan ? qnan_f() : a, prm);
+      s_x[tid] = x;
+      s_r[tid] = reciprocal_of<FAM>(x, nan);
+      const int64_t grow = rest * TR + row, gblk = ct * (TC / 32) + blk;
+      if (grow < outer && gblk < nb) X[grow * nb + gblk] = x;
+    }
+    __syncthreads();
+
+    // (2) elements: float4 q = tid + 256 i of the tile (row q / 64, float4 column q % 64)
+    const int c4 = tid & 63;
+    float4 xs, rs;
+    if (COLS) {
+      xs = *reinterpret_cast<const float4*>(s_x + c4 * 4);
+      rs = *reinterpret_cast<const float4*>(s_r + c4 * 4);
+    }
+#pragma unroll 2
+    for (int i = 0; i < 8; i++) {
+      const int row = (tid >> 6) + 4 * i;
+      float4 v = reinterpret_cast<const float4*>(T + row * TC)[c4];
+      if (!COLS) {
+        const int b = row * 8 + (c4 >> 3);
+        const float x = s_x[b], r = s_r[b];
+        xs = make_float4(x, x, x, x);
+        rs = make_float4(r, r, r, r);
+      }
+      v.x = element<FAM, E, M>(divide<FAM>(v.x, xs.x, rs.x), prm);
+      v.y = element<FAM, E, M>(divide<FAM>(v.y, xs.y, rs.y), prm);
+      v.z = element<FAM, E, M>(divide<FAM>(v.z, xs.z, rs.z), prm);
+      v.w = element<FAM, E, M>(divide<FAM>(v.w, xs.w, rs.w), prm);
+      if (COLS) {
+        const int64_t b = rest % nb, o = rest / nb, l = b * TR + row, col = ct * TC + c4 * 4;
+        if (l < len && col < inner) __stcs(reinterpret_cast<float4*>(P + (o * len + l) * inner + col), v);
+      } else {
+        const int64_t grow = rest * TR + row, col = ct * TC + c4 * 4;
+        if (grow < outer && col < len) __stcs(reinterpret_cast<float4*>(P + grow * len + col), v);
+      }
+    }
+    __syncthreads();                                        // every thread is done with this stage and s_x / s_r
+    if (tid == 0 && tile + (int64_t)STAGES * gridDim.x < ntiles) issue(tile + (int64_t)STAGES * gridDim.x, stage);
+  }
+}
+
+template <int FAM, int E, int M>
+int launch(const CUtensorMap& map, bool cols, float* P, float* X, int64_t outer, int64_t len, int64_t inner,
+           const TParams& prm, cudaStream_t st) {
+  const int64_t nb = (len + TR - 1) / TR;
+  const int64_t ntiles = cols ? outer * nb * ((inner + TC - 1) / TC) : ((outer + TR - 1) / TR) * ((len + TC - 1) / TC);
+  const size_t smem = STAGES * TILE_BYTES;
+  auto kern = cols ? k_quant_tma<FAM, E, M, true> : k_quant_tma<FAM, E, M, false>;
+  if (int r = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                         "block_quantize: shared memory attribute"))
+    return r;
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT, smem);
+  if (per_sm < 1) per_sm = 1;
+  int64_t grid = (int64_t)sm_count() * per_sm;
+  if (grid > ntiles) grid = ntiles;
+  kern<<<(unsigned)grid, NT, smem, st>>>(map, P, X, outer, len, inner, prm);
+  return MXQ_LAUNCH_CHECK("block_quantize");
+}
+
+template <int FAM>
+int launch_fmt(int e, int m, const CUtensorMap& map, bool cols, float* P, float* X, int64_t outer, int64_t len,
+               int64_t inner, const TParams& prm, cudaStream_t st) {
+  if (e == 4 && m == 3) return launch<FAM, 4, 3>(map, cols, P, X, outer, len, inner, prm, st);
+  if (e == 5 && m == 2) return launch<FAM, 5, 2>(map, cols, P, X, outer, len, inner, prm, st);
+  if (e == 3 && m == 2) return launch<FAM, 3, 2>(map, cols, P, X, outer, len, inner, prm, st);
+  if (e == 2 && m == 3) return launch<FAM, 2, 3>(map, cols, P, X, outer, len, inner, prm, st);
+  if (e == 2 && m == 1) return launch<FAM, 2, 1>(map, cols, P, X, outer, len, inner, prm, st);
+  return MXQ_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+namespace mxq {
+
+// The TMA kernel for blocks of 32 when the layout allows a tensor map (16-byte aligned base, rows a multiple of 16
+// bytes, extents below 2^31); MXQ_ERR_UNSUPPORTED otherwise (the caller then takes the register kernels).
+int quantize_tma(const float* V, float* P, float* X, int64_t outer, int64_t len, int64_t inner, int64_t block,
+                 const mxq_quant_spec& s, cudaStream_t st) {
+  if (block != 32 || s.family == MXQ_FAMILY_FP32 || (s.family == MXQ_FAMILY_MXGEMMINI && s.via_e != 0))
+    return MXQ_ERR_UNSUPPORTED;
+  const bool cols = inner > 1;
+  const int64_t rowlen = cols ? inner : len;
+  if ((uintptr_t)V % 16 || (uintptr_t)P % 16 || rowlen % 4 || outer >= (1ll << 31) || len >= (1ll << 31) ||
+      inner >= (1ll << 31))
+    return MXQ_ERR_UNSUPPORTED;
+  CUtensorMap map;
+  if (cols) {
+    const uint64_t dims[3] = {(uint64_t)inner, (uint64_t)len, (uint64_t)outer};
+    const uint64_t strides[2] = {(uint64_t)inner * 4, (uint64_t)(len * inner) * 4};
+    const uint32_t box[3] = {TC, TR, 1};
+    if (encode_tmap_f32(&map, V, 3, dims, strides, box) != MXQ_OK) return MXQ_ERR_UNSUPPORTED;
+  } else {
+    const uint64_t dims[2] = {(uint64_t)len, (uint64_t)outer};
+    const uint64_t strides[1] = {(uint64_t)len * 4};
+    const uint32_t box[2] = {TC, TR};
+    if (encode_tmap_f32(&map, V, 2, dims, strides, box) != MXQ_OK) return MXQ_ERR_UNSUPPORTED;
+  }
+  TParams prm{s.rounding, s.placement, s.via_e, s.via_m, s.scale_floor, s.scale_emax};
+  switch (s.family) {
+    case MXQ_FAMILY_MXQUANT: return launch_fmt<MXQ_FAMILY_MXQUANT>(s.e, s.m, map, cols, P, X, outer, len, inner, prm, st);
+    case MXQ_FAMILY_MXGEMMINI:
+      return launch_fmt<MXQ_FAMILY_MXGEMMINI>(s.e, s.m, map, cols, P, X, outer, len, inner, prm, st);
+    default: return launch_fmt<MXQ_FAMILY_OCP>(s.e, s.m, map, cols, P, X, outer, len, inner, prm, st);
+  }
+}
+
+}  // namespace mxq
+
+// Number of bounded shared-memory waits that gave up in the staged kernels since the library was loaded on the
+// current device (0 in every correct run); synchronous.
+extern "C" int mxq_device_timeouts(uint32_t* out) {
+  if (!out) return mxq::set_error(MXQ_ERR_VALUE, "device_timeouts: null output");
+  *out = mxq::read_wait_timeouts();
+  return MXQ_OK;
+}
