@@ -152,6 +152,33 @@ int mxq_anchor_tree(const float* PA, const float* XA, const float* PB, const flo
 int mxq_fp64_accum(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
                    int64_t N, int64_t block, void* stream);
 
+/* ------------------------------------------------------------------------------------------- LUTs */
+/* MX-Gemmini's look-up tables for the LUT formats (e, m) in {(3,2), (2,3), (5,2), (4,3)}. An operand is K x n,
+ * element (k, j) at P[k * sk + j * sj] (row-major: sk = n, sj = 1; transposed in place: sk = 1, sj = K); one table
+ * of 16 ascending values per 2^group columns. `status` is a device int32 the call zeroes and a kernel sets when an
+ * input is not what the reference accepts (the caller reads it to raise the reference's error). */
+/* mxq/lut/formats.py:83-122 _tables / values: every code's value and fixed point, the finder-safe values (HOST
+ * pointers, any may be NULL; vals/fx hold 2^(1+e+m) entries, safe up to 256); synchronous, no device work */
+int mxq_lut_format_tables(int32_t e, int32_t m, float* vals, int64_t* fx, float* safe, int32_t* nsafe);
+/* mxq/lut/kmeans.py:46-122 tables: T is ceil(n / 2^group) x 16; status 1: a value of P is not a code */
+int mxq_lut_tables(const float* P, float* T, int64_t K, int64_t n, int64_t sk, int64_t sj, int32_t group,
+                   int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream);
+/* mxq/lut/kmeans.py:125-138 pick: I is K x n int64 row-major; T rows of `width` ascending entries */
+int mxq_lut_pick(const float* P, const float* T, int64_t* I, int64_t K, int64_t n, int64_t sk, int64_t sj,
+                 int32_t group, int32_t width, void* stream);
+/* mxq/block/lut.py:33 lookup(pick(P, T), T) in one pass, written in P's own layout */
+int mxq_lut_pick_lookup(const float* P, const float* T, float* out, int64_t K, int64_t n, int64_t sk, int64_t sj,
+                        int32_t group, int32_t width, void* stream);
+/* mxq/lut/kmeans.py:141-146 lookup */
+int mxq_lut_lookup(const int64_t* I, const float* T, float* out, int64_t K, int64_t n, int32_t group, int32_t width,
+                   void* stream);
+/* mxq/lut/formats.py:125-137 encode (status 1: a value is not a code) and :114-117 decode (status 1: bad code) */
+int mxq_lut_encode(const float* V, int64_t* codes, int64_t n, int32_t e, int32_t m, int32_t* status, void* stream);
+int mxq_lut_decode(const int64_t* codes, float* out, int64_t n, int32_t e, int32_t m, int32_t* status, void* stream);
+/* mxq/lut/formats.py:140-159 finder: I is K x n int64 (status 1: bad code, 2: a table value is not a code) */
+int mxq_lut_finder(const int64_t* codes, const float* T, int64_t* I, int64_t K, int64_t n, int32_t group, int32_t e,
+                   int32_t m, int32_t* status, void* stream);
+
 /* ------------------------------------------------------------------------------------------ diagnostics */
 /* No reference counterpart: the number of bounded shared-memory waits (mbarrier) that gave up in the TMA-staged
  * kernels on the current device since the library was loaded. Always 0 in a correct run; synchronous. */

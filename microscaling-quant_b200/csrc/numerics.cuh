@@ -607,4 +607,33 @@ MXQ_HD float q_microsoft_sat(float A, int bits, int exp_bits, float max_norm, in
   return a == 0u ? 0.0f : out;
 }
 
+// The microxcaling step for an OCP element format (exp_bits 2..5, so min_exp >= -14), saturating: q_microsoft's
+// result for every float32 input, cheaper.
+//   * nearest / even: the private exponent may be the exact floor(log2|A|) instead of the reference's rounded-up
+//     log2 -- they differ only within 44 ulps below a power of two 2^k, where both step sizes round to 2^k;
+//     floor mode keeps the reference's rule (there the two steps floor to different values);
+//   * float32 subnormals take the clipped exponent min_exp either way.
+// The rounding itself stays the reference's float32 formula: |t| + 0.5 is rounded before the floor, which is not
+// rint (t = 0.5 - 2^-25 gives 1), so "even" keeps its mask on exact even ties.
+MXQ_HD float q_microsoft_ocp(float A, int bits, int exp_bits, float max_norm, int round) {
+  const uint32_t u = f2u(A), a = u & 0x7fffffffu;
+  if (a >= 0x7f7fffd4u) return q_microsoft(A, bits, exp_bits, max_norm, round, true);  // inf, NaN, log2 -> 128
+  const int min_exp = 2 - (1 << (exp_bits - 1));
+  int pe = (round == MS_FLOOR) ? (a ? floor_log2_rn(u2f(a)) : 0) : (int)(a >> 23) - 127;
+  pe = pe > min_exp ? pe : min_exp;
+  const float t = mul_rn(u2f(a), u2f((uint32_t)(125 + bits - pe) << 23));   // |A| / 2^pe * 2^(bits-2)
+  float r;
+  if (round == MS_FLOOR) {
+    r = floor_f(t);
+  } else {
+    r = floor_f(add_rn(t, 0.5f));
+    if (round == MS_EVEN) {                                    // (|t| - 0.5) % 2 == 0: an exact even tie
+      const float y = sub_rn(t, 0.5f), h = mul_rn(y, 0.5f);
+      r = sub_rn(r, (y >= 0.0f && floor_f(h) == h) ? 1.0f : 0.0f);
+    }
+  }
+  const float val = fminf(mul_rn(r, u2f((uint32_t)(129 - bits + pe) << 23)), max_norm);
+  return a == 0u ? 0.0f : u2f(f2u(val) | (u & 0x80000000u));
+}
+
 }  // namespace mxq

@@ -69,7 +69,7 @@ template <int FAM, int E, int M>
 __device__ __forceinline__ float element(float z, const TParams& p) {
   if (FAM == MXQ_FAMILY_MXQUANT) return qtorch_ties_away<E, M>(z);
   if (FAM == MXQ_FAMILY_MXGEMMINI) return ocp_grid<E, M>(z, p.rounding);
-  return q_microsoft_sat(z, M + 2, E, Fmt<E, M>::MAX_NORM, p.rounding);
+  return q_microsoft_ocp(z, M + 2, E, Fmt<E, M>::MAX_NORM, p.rounding);
 }
 
 template <int FAM, int E, int M>
@@ -139,30 +139,26 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     // (1) block scales
     if (COLS) {
       const int64_t b = rest % nb, o = rest / nb, col = ct * TC + tid;
-      float a = 0.0f;
-      bool nan = false;
+      uint32_t mbits = 0u;                                  // max |v| as bits: a NaN pattern tops every number
 #pragma unroll 8
-      for (int r = 0; r < TR; r++) {
-        float v = T[r * TC + tid];
-        nan |= isnan_f(v);
-        a = fmaxf(a, abs_f(v));
-      }
-      const float x = block_scale<FAM, E, M>(nan ? qnan_f() : a, prm);
+      for (int r = 0; r < TR; r++) mbits = max(mbits, f2u(T[r * TC + tid]) & 0x7fffffffu);
+      const bool nan = mbits > 0x7f800000u;
+      const float x = block_scale<FAM, E, M>(nan ? qnan_f() : u2f(mbits), prm);
       s_x[tid] = x;
       s_r[tid] = reciprocal_of<FAM>(x, nan);
       if (col < inner) X[(o * nb + b) * inner + col] = x;
     } else {
       const int row = tid >> 3, blk = tid & 7;                // 32 rows x 8 blocks
       const float4* src = reinterpret_cast<const float4*>(T + row * TC + blk * 32);
-      float a = 0.0f;
-      bool nan = false;
+      uint32_t mbits = 0u;                                  // max |v| as bits: a NaN pattern tops every number
 #pragma unroll
       for (int i = 0; i < 8; i++) {
         const float4 v = src[(i + tid) & 7];
-        nan |= isnan_f(v.x) | isnan_f(v.y) | isnan_f(v.z) | isnan_f(v.w);
-        a = fmaxf(a, fmaxf(fmaxf(abs_f(v.x), abs_f(v.y)), fmaxf(abs_f(v.z), abs_f(v.w))));
+        mbits = max(max(mbits, f2u(v.x) & 0x7fffffffu), max(f2u(v.y) & 0x7fffffffu, f2u(v.z) & 0x7fffffffu));
+        mbits = max(mbits, f2u(v.w) & 0x7fffffffu);
       }
-      const float x = block_scale<FAM, E, M>(nan ? qnan_f() : a, prm);
+      const bool nan = mbits > 0x7f800000u;
+      const float x = block_scale<FAM, E, M>(nan ? qnan_f() : u2f(mbits), prm);
       s_x[tid] = x;
       s_r[tid] = reciprocal_of<FAM>(x, nan);
       const int64_t grow = rest * TR + row, gblk = ct * (TC / 32) + blk;

@@ -72,6 +72,15 @@ _SIGS = {
     "mxq_anchor_tree": [P, P, P, P, P, I64, I64, I64, I64, I64, ctypes.POINTER(MxqArith), P, P,
                         ctypes.POINTER(MxqAnchorSpec), P, P],
     "mxq_fp64_accum": [P, P, P, P, P, I64, I64, I64, I64, P],
+    "mxq_lut_tables": [P, P, I64, I64, I64, I64, I32, I32, I32, I32, P, P],
+    "mxq_lut_pick": [P, P, P, I64, I64, I64, I64, I32, I32, P],
+    "mxq_lut_pick_lookup": [P, P, P, I64, I64, I64, I64, I32, I32, P],
+    "mxq_lut_lookup": [P, P, P, I64, I64, I32, I32, P],
+    "mxq_lut_encode": [P, P, I64, I32, I32, P, P],
+    "mxq_lut_decode": [P, P, I64, I32, I32, P, P],
+    "mxq_lut_finder": [P, P, P, I64, I64, I32, I32, I32, P, P],
+    "mxq_lut_format_tables": [I32, I32, P, P, P, P],
+    "mxq_device_timeouts": [P],
 }
 
 

@@ -84,3 +84,15 @@ X int64_t h_fast_forms_mismatches(uint64_t lo, uint64_t hi, uint64_t stride, int
   }
   return bad;
 }
+// q_microsoft_ocp against q_microsoft (saturating) over bit patterns lo, lo+stride, ... < hi
+X int64_t h_ms_ocp_mismatches(uint64_t lo, uint64_t hi, uint64_t stride, int e, int m, int mode) {
+  int64_t bad = 0;
+  float mn = ocp_max_norm(e, m);
+  for (uint64_t v = lo; v < hi; v += stride) {
+    float x = u2f((uint32_t)v);
+    float a = q_microsoft_ocp(x, m + 2, e, mn, mode), b = q_microsoft(x, m + 2, e, mn, mode, true);
+    bool an = (f2u(a) & 0x7fffffffu) > 0x7f800000u, bn = (f2u(b) & 0x7fffffffu) > 0x7f800000u;
+    if (an != bn || (!an && f2u(a) != f2u(b))) bad++;
+  }
+  return bad;
+}

@@ -118,3 +118,38 @@ def anchor_tree(P_A, X_A, P_B, X_B, arith, schedule=None, size=16, block_size=32
 
 def fp64_accum(P_A, X_A, P_B, X_B, block_size=32, threads=None):
     return N(mxq.fp64_accum(*_ops(P_A, X_A, P_B, X_B), block_size))
+
+
+# ------------------------------------------------------------------------------------------------------ LUT
+from mxq import lut as _lut  # noqa: E402
+
+
+def lut_format_tables(fmt):
+    v, fx, s = _lut.formats._tables(fmt)
+    return v.numpy(), fx.numpy(), s.numpy()
+
+
+def lut_tables(P, fmt, group, max_iters):
+    return N(_lut.tables(T(np.asarray(P, np.float32)), fmt, group=group, max_iters=max_iters))
+
+
+def lut_pick(P, Tt, group):
+    return N(_lut.pick(T(np.asarray(P, np.float32)), T(np.asarray(Tt, np.float32)), group=group))
+
+
+def lut_lookup(I, Tt, group):
+    return N(_lut.lookup(T(np.asarray(I, np.int64)), T(np.asarray(Tt, np.float32)), group=group))
+
+
+def lut_encode(Tt, fmt):
+    return N(_lut.encode(T(np.asarray(Tt, np.float32)), fmt))
+
+
+def lut_finder(codes, Tt, fmt, group):
+    return N(_lut.finder(T(np.asarray(codes, np.int64)), T(np.asarray(Tt, np.float32)), fmt, group=group))
+
+
+def lut_block_quantize(V, fmt, axis, block_size, rounding_mode, scale_floor, group, max_iters):
+    P, X = block.lut.quantize(T(np.asarray(V, np.float32)), fmt, axis, block_size, rounding_mode=rounding_mode,
+                              scale_floor=scale_floor, group=group, max_iters=max_iters)
+    return N(P), N(X)

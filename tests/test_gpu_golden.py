@@ -52,3 +52,8 @@ def test_config1(prod):
         assert_bits(t, gd[f"config1/{name}"], name)
     Y = mxq.matmul.systolic(P_A, X_A, P_B, X_B, mxq.matmul.MXGEMMINI(), mxq.schedule.HW_FINAL)
     assert_bits(Y, gd["config1/Y"], "config1 Y")
+
+
+@pytest.mark.parametrize("check", [g.test_lut_ops, g.test_lut_block], ids=lambda f: f.__name__[5:])
+def test_lut(prod, check):
+    check(prod)

@@ -107,3 +107,27 @@ def test_systolic_fast_equals_generic(oracle):
     want = oracle.systolic(P_A.cpu().numpy(), X_A.cpu().numpy(), P_B.cpu().numpy(), X_B.cpu().numpy(),
                            oracle.arith_mxgemmini(), hw, 16)
     assert_bits(fast, want, "fast vs oracle")
+
+
+@pytest.mark.parametrize("fmt", ["MXFP6_E3M2", "MXFP8_E4M3", "MXFP6_E2M3", "MXFP8_E5M2"])
+def test_lut_vs_oracle(oracle, fmt):
+    """config 4's distribution (column j ~ N(0, sigma_j^2), sigma_j = 2^U[-8, 8]) at 512 x 384: block.lut on both
+    axes, and tables / pick / finder on the block codes, for G in {0, 1, 3} and a partial last group (G = 7)."""
+    rng = np.random.default_rng(hash(fmt) % 2 ** 32)
+    K, n = 512, 384
+    V = (rng.standard_normal((K, n)) * 2.0 ** rng.uniform(-8, 8, (1, n))).astype(np.float32)
+    for G in (0, 1, 3, 7):
+        for axis in (0, 1):
+            P, X = prod.lut_block_quantize(V, fmt, axis, 32, "rne", 2.0 ** -23, G, 50)
+            Po, Xo = oracle.lut_block_quantize(V, fmt, axis, 32, "rne", 2.0 ** -23, G, 50)
+            assert_bits(P, Po, f"block.lut {fmt} G{G} axis{axis}")
+            assert_bits(X, Xo, f"block.lut X {fmt} G{G} axis{axis}")
+        Pc, _ = oracle.block_quantize(V, "mxgemmini", fmt, 0, 32, "rne", 2.0 ** -23)
+        T = prod.lut_tables(Pc, fmt, G, 50)
+        assert_bits(T, oracle.lut_tables(Pc, fmt, G, 50), f"tables {fmt} G{G}")
+        I = prod.lut_pick(Pc, T, G)
+        assert_bits(I, oracle.lut_pick(Pc, T, G), f"pick {fmt} G{G}")
+        if n % (1 << G) == 0:
+            codes = oracle.lut_encode(Pc, fmt)
+            assert_bits(prod.lut_encode(Pc, fmt), codes, f"encode {fmt}")
+            assert_bits(prod.lut_finder(codes, T, fmt, G), oracle.lut_finder(codes, T, fmt, G), f"finder {fmt} G{G}")

@@ -115,3 +115,29 @@ def test_fast_forms_match_general(shim, which):
     with ThreadPoolExecutor(8) as ex:
         bad = sum(ex.map(lambda j: f(j[0], j[0] + chunk, stride, which, j[1], j[2], j[3]), jobs))
     assert bad == 0
+
+
+def test_microsoft_ocp_form_matches_general(shim):
+    """q_microsoft_ocp (the TMA quantizer's ocp element step) equals q_microsoft on a dense stride through all
+    2^32 patterns for every OCP format and rounding mode; the exhaustive run is in the repository's history."""
+    f = shim.h_ms_ocp_mismatches
+    f.restype = ctypes.c_int64
+    f.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    from concurrent.futures import ThreadPoolExecutor
+    stride, chunk = 4099, 1 << 29
+    jobs = [(lo, e, m, mode) for (e, m) in [(4, 3), (5, 2), (3, 2), (2, 3), (2, 1)] for mode in range(3)
+            for lo in range(0, 1 << 32, chunk)]
+    with ThreadPoolExecutor(8) as ex:
+        bad = sum(ex.map(lambda j: f(j[0], j[0] + chunk, stride, j[1], j[2], j[3]), jobs))
+    assert bad == 0
+
+
+def test_microsoft_even_is_not_rint(shim):
+    """Regression: the reference's even rounding rounds |t| + 0.5 in float32 before the floor, so 2^-10 (1 - 2^-24)
+    in MXFP8_E4M3 (t = 0.5 - 2^-25 after clipping) becomes 2^-9, where round-half-even would give 0."""
+    f = shim.h_ms_ocp_mismatches
+    f.restype = ctypes.c_int64
+    f.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    for base in (0x3A7FFFFF, 0xBA7FFFFF):
+        for e, m in [(4, 3), (5, 2)]:
+            assert f(base - 64, base + 64, 1, e, m, 2) == 0
