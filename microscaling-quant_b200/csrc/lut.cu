@@ -546,6 +546,10 @@ int mxq_lut_tables(const float* P, float* T, int64_t K, int64_t n, int64_t sk, i
   const int gpc = groups_per_cta(group);
   const size_t smem = (size_t)gpc * f->nv * sizeof(int);
   const unsigned grid = (unsigned)((ng + gpc - 1) / gpc);
+  // static (~22 KB) plus the histograms can pass the 48 KB default
+  if (int r = check_cuda(cudaFuncSetAttribute(k_lut_tables, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                         "lut.tables: shared memory attribute"))
+    return r;
   k_lut_tables<<<grid, NT, smem, st>>>(P, K, n, sk, sj, group, max_iters, tp, T, status);
   return MXQ_LAUNCH_CHECK("lut.tables");
 }
