@@ -15,6 +15,7 @@ Fixtures (all numpy .npz, float32 results compared bit for bit, NaN positions on
     reducers.npz      systolic / anchor_tree / adder_tree / fp64_accum variants, and the full config-1 output
     lut.npz           lut.tables / pick / lookup / finder / encode / values and block.lut.quantize
     nn.npz            Scheme.matmul, MXLinear.forward and attend on small shapes
+    model.npz         a small random-init Llama patched as config 5: logits, and every MXLinear's input / output
 """
 import argparse
 import json
@@ -401,6 +402,41 @@ def child(only):
                     out[f"lut/{fmt}/{G}/Tcodes"] = N(lut.encode(Tt, fmt))
         np.savez_compressed(os.path.join(HERE, "lut.npz"), **out)
         print("lut.npz:", len(out), "arrays", flush=True)
+
+    # ------------------------------------------------------------------------------------------- model
+    if want("model"):
+        from functools import partial
+        from mxq import Scheme
+        from mxq.nn import patch
+        from transformers import LlamaConfig, LlamaForCausalLM
+        out = {}
+        cfg = LlamaConfig(hidden_size=128, intermediate_size=352, num_hidden_layers=2, num_attention_heads=4,
+                          num_key_value_heads=4, head_dim=32, vocab_size=256, max_position_embeddings=128,
+                          initializer_range=0.02)
+        torch.manual_seed(0)
+        model = LlamaForCausalLM(cfg).float().eval()
+        ids = torch.randint(0, 256, (2, 40), generator=torch.Generator().manual_seed(1))
+        with torch.no_grad():
+            out["logits_plain"] = N(model(ids).logits)
+        q = partial(block.mxgemmini.quantize, fmt="MXFP8_E4M3", axis=0)
+        s = Scheme("hw_fp8", a=q, b=q, reduce=partial(matmul.systolic, arith=matmul.MXGEMMINI(), schedule=schedule.HW_FINAL))
+        patch(model, [("lm_head", None), ("model.layers.*.self_attn", (s, s)), (torch.nn.Linear, s)])
+        captured = {}
+
+        def hook(name):
+            def f(mod, inp, outp):
+                captured[name + "/x"] = N(inp[0])
+                captured[name + "/y"] = N(outp)
+            return f
+        for name, mod in model.named_modules():
+            if type(mod).__name__ == "MXLinear":
+                mod.register_forward_hook(hook(name))
+        with torch.no_grad():
+            out["logits"] = N(model(ids).logits)
+        out.update(captured)
+        out["ids"] = N(ids)
+        np.savez_compressed(os.path.join(HERE, "model.npz"), **out)
+        print("model.npz:", len(out), "arrays", flush=True)
 
     # ------------------------------------------------------------------------------------------------- nn
     if want("nn"):
