@@ -115,11 +115,91 @@ def compose(V: torch.Tensor, *, scale: Optional[Callable[[torch.Tensor], torch.T
     return _lib.back(P_out, home), _lib.back(X_out, home)
 
 
+STREAM_MIN_BYTES = 8 << 20        # host tensors at least this large are streamed through the device in chunks
+STREAM_CHUNK_BYTES = 16 << 20     # V bytes per chunk
+STREAM_DEPTH = 3                  # chunks in flight: one copying in, one quantizing, one copying out
+_streams = {}
+
+
+def _copy_streams(dev):
+    if dev not in _streams:
+        _streams[dev] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return _streams[dev]
+
+
+def _quantize_streamed(V, spec, axis_, outer, L, inner, nb, block_size, dev):
+    """A host V quantized through the device in independent chunks, copies in, kernels and copies out on three
+    streams so PCIe carries both directions while the device quantizes. Chunks are whole outer slices when
+    outer > 1, else runs of whole blocks along the axis; either way each chunk's V, P and X are contiguous ranges
+    of the host tensors. Returns pinned host P and X after the last copy has landed."""
+    import ctypes
+    src = V.contiguous()
+    if src.dtype != torch.float32:
+        src = src.to(torch.float32)
+    xshape = list(V.shape)
+    xshape[axis_] = nb
+    P = torch.empty(V.shape, dtype=torch.float32, pin_memory=True)
+    X = torch.empty(xshape, dtype=torch.float32, pin_memory=True)
+    vf, pf, xf = src.reshape(-1), P.reshape(-1), X.reshape(-1)
+    chunks = []                        # (v0, v1, x0, x1, (outer, len, inner)) per chunk
+    if outer > 1 and 4 * L * inner <= STREAM_CHUNK_BYTES:       # whole outer slices
+        per = max(1, STREAM_CHUNK_BYTES // (4 * L * inner))
+        for o0 in range(0, outer, per):
+            o1 = min(outer, o0 + per)
+            chunks.append((o0 * L * inner, o1 * L * inner, o0 * nb * inner, o1 * nb * inner, (o1 - o0, L, inner)))
+    else:                              # runs of whole blocks inside each outer slice (the last may be short)
+        per = max(1, STREAM_CHUNK_BYTES // (4 * block_size * inner))
+        for o in range(outer):
+            for b0 in range(0, nb, per):
+                b1 = min(nb, b0 + per)
+                r0, r1 = b0 * block_size, min(L, b1 * block_size)
+                vb, xb = o * L * inner, o * nb * inner
+                chunks.append((vb + r0 * inner, vb + r1 * inner, xb + b0 * inner, xb + b1 * inner, (1, r1 - r0, inner)))
+    cap_v = max(c[1] - c[0] for c in chunks)
+    cap_x = max(c[3] - c[2] for c in chunks)
+    h2d, comp, d2h = _copy_streams(dev)
+    cur = torch.cuda.current_stream(dev)
+    with torch.cuda.device(dev):
+        for s in (h2d, comp, d2h):
+            s.wait_stream(cur)
+        with torch.cuda.stream(comp):
+            dv = [torch.empty(cap_v, dtype=torch.float32, device=dev) for _ in range(STREAM_DEPTH)]
+            dp = [torch.empty(cap_v, dtype=torch.float32, device=dev) for _ in range(STREAM_DEPTH)]
+            dx = [torch.empty(cap_x, dtype=torch.float32, device=dev) for _ in range(STREAM_DEPTH)]
+        free = [None] * STREAM_DEPTH
+        for i, (v0, v1, x0, x1, shape) in enumerate(chunks):
+            s = i % STREAM_DEPTH
+            nv = v1 - v0
+            with torch.cuda.stream(h2d):
+                if free[s] is not None:
+                    h2d.wait_event(free[s])
+                dv[s][:nv].copy_(vf[v0:v1], non_blocking=True)
+                landed = torch.cuda.Event()
+                landed.record(h2d)
+            with torch.cuda.stream(comp):
+                comp.wait_event(landed)
+                _lib.call("mxq_block_quantize", _lib.ptr(dv[s]), _lib.ptr(dp[s]), _lib.ptr(dx[s]), *shape,
+                          block_size, ctypes.byref(spec), ctypes.c_void_p(comp.cuda_stream))
+                done = torch.cuda.Event()
+                done.record(comp)
+            with torch.cuda.stream(d2h):
+                d2h.wait_event(done)
+                pf[v0:v1].copy_(dp[s][:nv], non_blocking=True)
+                xf[x0:x1].copy_(dx[s][:x1 - x0], non_blocking=True)
+                free[s] = torch.cuda.Event()
+                free[s].record(d2h)
+        d2h.synchronize()
+    return P, X
+
+
 def quantize_fused(V: torch.Tensor, spec: "_lib.MxqQuantSpec", axis: int, block_size: int):
-    """A named quantizer's compose as one kernel: P and X from V in one pass (mxq_block_quantize)."""
+    """A named quantizer's compose as one kernel: P and X from V in one pass (mxq_block_quantize). A large host V
+    streams through the device in chunks (_quantize_streamed) and P, X come back as pinned host tensors."""
     axis_, outer, L, inner, nb = _layout(V, axis, block_size)
     home = _lib.home(V)
     dev = _lib.device_for(V)
+    if not V.is_cuda and V.numel() * 4 >= STREAM_MIN_BYTES:
+        return _quantize_streamed(V, spec, axis_, outer, L, inner, nb, block_size, dev)
     v = _lib.on(V, dev)
     P = torch.empty_like(v)
     xshape = list(V.shape)

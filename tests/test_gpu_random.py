@@ -52,6 +52,28 @@ def test_block_layout_paths(oracle):
             assert_bits(X, Xo, f"{shape} {axis} {bs} {family} X")
 
 
+def test_block_host_streamed(monkeypatch):
+    """A host tensor streams through the device in chunks (whole outer slices, or runs of blocks inside a slice,
+    the last one short); the chunked result must equal the one-shot device result bit for bit."""
+    import torch
+    from mxq import block
+    from mxq.block import _driver
+    monkeypatch.setattr(_driver, "STREAM_MIN_BYTES", 1)
+    monkeypatch.setattr(_driver, "STREAM_CHUNK_BYTES", 4 * 32 * 40)
+    rng = np.random.default_rng(9)
+    quant = {"mxquant": block.mxquant.quantize, "mxgemmini": block.mxgemmini.quantize, "ocp": block.ocp.quantize}
+    for shape, axis in (((200, 40), 0), ((200, 40), 1), ((7, 45, 8), 1), ((3, 300, 16), 1), ((4, 5, 33), 0),
+                        ((2, 70, 3), 0)):
+        V = (rng.standard_normal(shape) * 2.0 ** rng.uniform(-8, 8, shape)).astype(np.float32)
+        Vh = torch.from_numpy(V).pin_memory()
+        for family, fmt in (("mxquant", "MXFP8_E4M3"), ("mxgemmini", "MXFP6_E2M3"), ("ocp", "MXFP4")):
+            P, X = quant[family](Vh, fmt, axis=axis)
+            assert not P.is_cuda and not X.is_cuda
+            Pd, Xd = quant[family](Vh.cuda(), fmt, axis=axis)
+            assert_bits(P.numpy(), Pd.cpu().numpy(), f"{shape} {axis} {family} P")
+            assert_bits(X.numpy(), Xd.cpu().numpy(), f"{shape} {axis} {family} X")
+
+
 def _operands(oracle, K, M, N, fmt, seed, special=False):
     rng = np.random.default_rng(seed)
     A = (rng.standard_normal((K, M)) * 2.0 ** rng.uniform(-4, 4, (1, M))).astype(np.float32)
