@@ -148,6 +148,19 @@ MXQ_HD double ddiv_rn(double a, double b) {
 MXQ_HD float floor_f(float x) { return floorf(x); }    // exact operations (no rounding involved)
 MXQ_HD float trunc_f(float x) { return truncf(x); }
 MXQ_HD float rint_f(float x) { return rintf(x); }      // round half to even = torch.round
+// floor / rint of a float32 0 <= s < 2^23 with adds at a fixed exponent, which the device runs on the full-rate
+// FP32 pipe rather than the conversion pipe: s + 2^23 lies in [2^23, 2^24), where float32 values are the integers,
+// so the add's own rounding (toward zero, or to nearest even) is the rounding of s and subtracting 2^23 is exact.
+// Infinities and NaN pass through unchanged, as with floorf / rintf. (Negative s: a defined value that callers
+// discard.)
+MXQ_HD float floor_small(float s) {
+#if defined(__CUDA_ARCH__)
+  return __fsub_rn(__fadd_rz(s, 8388608.0f), 8388608.0f);
+#else
+  return floorf(s);
+#endif
+}
+MXQ_HD float rint_small(float s) { return sub_rn(add_rn(s, 8388608.0f), 8388608.0f); }
 MXQ_HD double floor_d(double x) { return floor(x); }
 MXQ_HD double trunc_d(double x) { return trunc(x); }
 MXQ_HD double rint_d(double x) { return rint(x); }
@@ -568,10 +581,10 @@ MXQ_HD float ar_tile_add(const ArithP& A, float C, float t) {
 // The same results as q_ocp_f / q_microsoft for EVERY float32 input (checked exhaustively on the host against
 // them), with the powers of two built from the exponent field: the scale factors of these grids are always normal
 // float32 numbers, and the two exact power-of-two multiplications of the microxcaling step fold into one.
-MXQ_HD float round_nonneg(float k, int mode) {        // round_int of a value >= 0
-  if (mode == RM_RNE) return rint_f(k);
-  if (mode == RM_TRUNCATE) return trunc_f(k);
-  return floor_f(add_rn(k, 0.5f));
+MXQ_HD float round_nonneg(float k, int mode) {        // round_int of a value 0 <= k < 2^22
+  if (mode == RM_RNE) return rint_small(k);
+  if (mode == RM_TRUNCATE) return floor_small(k);
+  return floor_small(add_rn(k, 0.5f));
 }
 MXQ_HD float q_ocp_bits(float x, int e, int m, int mode, float max_norm) {
   uint32_t u = f2u(x), a = u & 0x7fffffffu;
@@ -593,13 +606,13 @@ MXQ_HD float q_microsoft_sat(float A, int bits, int exp_bits, float max_norm, in
   pe = pe > min_exp ? pe : min_exp;
   float t = mul_rn(A, u2f((uint32_t)(125 + bits - pe) << 23));          // A / 2^pe * 2^(bits-2)
   float absA = abs_f(t), r;
-  if (round == MS_FLOOR) {
-    r = floor_f(absA);
+  if (round == MS_FLOOR) {                             // |t| < 2^(bits-1): the small-value roundings apply
+    r = floor_small(absA);
   } else if (round == MS_NEAREST) {
-    r = floor_f(add_rn(absA, 0.5f));
+    r = floor_small(add_rn(absA, 0.5f));
   } else {
     float y = sub_rn(absA, 0.5f), h = mul_rn(y, 0.5f);
-    r = sub_rn(floor_f(add_rn(absA, 0.5f)), (y >= 0.0f && floor_f(h) == h) ? 1.0f : 0.0f);
+    r = sub_rn(floor_small(add_rn(absA, 0.5f)), (y >= 0.0f && floor_small(h) == h) ? 1.0f : 0.0f);
   }
   r = u2f(f2u(r) | (u & 0x80000000u));                 // sign(A) * r: -0 for a negative value rounding to zero
   float out = mul_rn(r, u2f((uint32_t)(129 - bits + pe) << 23));        // / 2^(bits-2) * 2^pe
@@ -623,13 +636,13 @@ MXQ_HD float q_microsoft_ocp(float A, int bits, int exp_bits, float max_norm, in
   pe = pe > min_exp ? pe : min_exp;
   const float t = mul_rn(u2f(a), u2f((uint32_t)(125 + bits - pe) << 23));   // |A| / 2^pe * 2^(bits-2)
   float r;
-  if (round == MS_FLOOR) {
-    r = floor_f(t);
+  if (round == MS_FLOOR) {                                     // t < 2^(bits-1): small-value roundings apply
+    r = floor_small(t);
   } else {
-    r = floor_f(add_rn(t, 0.5f));
+    r = floor_small(add_rn(t, 0.5f));
     if (round == MS_EVEN) {                                    // (|t| - 0.5) % 2 == 0: an exact even tie
       const float y = sub_rn(t, 0.5f), h = mul_rn(y, 0.5f);
-      r = sub_rn(r, (y >= 0.0f && floor_f(h) == h) ? 1.0f : 0.0f);
+      r = sub_rn(r, (y >= 0.0f && floor_small(h) == h) ? 1.0f : 0.0f);
     }
   }
   const float val = fminf(mul_rn(r, u2f((uint32_t)(129 - bits + pe) << 23)), max_norm);

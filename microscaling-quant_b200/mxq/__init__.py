@@ -7,7 +7,7 @@ a kernel of libmxq_b200.so (microscaling-quant_b200/csrc, C ABI in include/mxq_b
 """
 __version__ = "0.1.0"
 
-from . import rounding, arith, schedule, scale_factor, element_quant, lut, block, matmul, scheme, nn, microxcaling
+from . import rounding, arith, schedule, scale_factor, element_quant, lut, block, matmul, scheme, nn, microxcaling, shard
 from .block import BLOCK
 from ._fp64_accum import fp64_accum
 from .element_quant.formats import Format

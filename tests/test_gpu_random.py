@@ -39,6 +39,25 @@ def test_block_vs_oracle(oracle, family, axis):
         assert_bits(X, Xo, f"{family}/{fmt}/{axis} X")
 
 
+@pytest.mark.parametrize("axis", [0, 1])
+def test_block_random_bits(oracle, axis):
+    """Uniformly random float32 bit patterns (every exponent, subnormals, Inf, NaN payloads) through every family,
+    format and rounding mode the element steps branch on."""
+    rng = np.random.default_rng(31 + axis)
+    V = rng.integers(0, 2 ** 32, (256, 512), dtype=np.uint64).astype(np.uint32).view(np.float32)
+    V = V.copy()
+    V[rng.random(V.shape) < 0.3] *= np.float32(2.0 ** -100)        # more blocks without a NaN or Inf
+    cases = [("mxquant", None), ("mxgemmini", "ties_away"), ("mxgemmini", "rne"), ("mxgemmini", "truncate"),
+             ("ocp", "even"), ("ocp", "nearest"), ("ocp", "floor")]
+    for family, rm in cases:
+        keep = ~nan_block_mask(V, axis) if family == "mxquant" else np.ones(V.shape, bool)
+        for fmt in FMTS:
+            P, X = prod.block_quantize(V, family, fmt, axis, rounding_mode=rm)
+            Po, Xo = oracle.block_quantize(V, family, fmt, axis, rounding_mode=rm)
+            assert_bits_where(P, Po, keep, f"{family}/{rm}/{fmt}/{axis} P")
+            assert_bits(X, Xo, f"{family}/{rm}/{fmt}/{axis} X")
+
+
 def test_block_layout_paths(oracle):
     """The three kernel paths (rows of 32, column runs of 4/2/1, generic) on shapes that force each."""
     rng = np.random.default_rng(5)
