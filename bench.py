@@ -10,7 +10,8 @@ launches. Throughput counts the algorithmic bytes of the reference's contract, 8
 P, write X once per 32 elements). Every rank quantizes its own row shard (weak scaling, no collective).
 
 Beside it, in the same JSON line, `systolic`: config 3's 4096^3 MXFP8_E4M3 systolic GEMM (MXGEMMINI / HW_FINAL,
-operands quantized by block.mxgemmini) in emulated GMAC/s, each rank reducing its own 4096-column panel of B.
+operands quantized by block.mxgemmini) in emulated GMAC/s, each rank reducing its own 4096-column panel of B;
+`reducers`: config 3's reducers (systolic MXGEMMINI and MXQUANT(4,3), adder tree, anchor tree) timed alone.
 
 `e2e` runs the same sweep through the public API with a pinned host V: every call streams V through the device in
 chunks and returns host P and X (copies in, kernels and copies out overlapped on three streams), all inside the
@@ -245,6 +246,32 @@ def run_gpu(args):
     gms = max_over_ranks(g0.elapsed_time(g1)) / gsteps
     gmacs = GEMM ** 3 * world / (gms * 1e-3) / 1e9
 
+    # -- config 3's other reducers on the same quantized operands (reducer kernel only, CUDA events)
+    P_A, X_A = block.mxgemmini.quantize(A, "MXFP8_E4M3", axis=0)
+    P_B, X_B = block.mxgemmini.quantize(B, "MXFP8_E4M3", axis=0)
+    reducers = {
+        "systolic MXGEMMINI/HW_FINAL": lambda: matmul.systolic(P_A, X_A, P_B, X_B, arith, schedule.HW_FINAL),
+        "systolic MXQUANT(4,3)/HW_FINAL": lambda: matmul.systolic(P_A, X_A, P_B, X_B, matmul.MXQUANT(4, 3),
+                                                                  schedule.HW_FINAL),
+        "adder_tree MXGEMMINI [(4,4),(4,5),(4,6),(8,7)]": lambda: matmul.adder_tree(
+            P_A, X_A, P_B, X_B, arith, [(4, 4), (4, 5), (4, 6), (8, 7)]),
+        "anchor_tree MXGEMMINI (defaults)": lambda: matmul.anchor_tree(P_A, X_A, P_B, X_B, arith),
+    }
+    red_out = {}
+    for name, fn in reducers.items():
+        if args.reducer_steps <= 0:
+            break
+        fn()
+        barrier()
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record(stream)
+        for _ in range(args.reducer_steps):
+            fn()
+        r1.record(stream)
+        barrier()
+        rms = max_over_ranks(r0.elapsed_time(r1)) / args.reducer_steps
+        red_out[name] = {"GMAC/s": round(GEMM ** 3 * world / (rms * 1e-3) / 1e9, 1), "ms": round(rms, 3)}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_rows, args.cpu_repeats)
@@ -275,6 +302,8 @@ def run_gpu(args):
                      "workload": f"config 3: quantize A, B ({GEMM}x{GEMM} MXFP8_E4M3, block.mxgemmini) + "
                                  f"systolic MXGEMMINI/HW_FINAL {GEMM}^3 per GPU", "ms_per_gemm": round(gms, 3),
                      "steps": gsteps},
+        "reducers": {"workload": f"config 3: {GEMM}^3 per GPU on MXFP8_E4M3 codes, reducer kernel alone",
+                     "steps": args.reducer_steps, **red_out},
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
@@ -342,6 +371,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mxq_b200", choices=["mxq_b200", "reference"])
     ap.add_argument("--gemm-steps", type=int, default=3)
+    ap.add_argument("--reducer-steps", type=int, default=1, help="timed runs of each other config-3 reducer (0: skip)")
     ap.add_argument("--cpu-rows", type=int, default=ROWS, help="rows of the CPU-baseline matrix")
     ap.add_argument("--cpu-repeats", type=int, default=2, help="sweeps of the CPU-baseline matrix")
     ap.add_argument("--ref-rows", type=int, default=256, help="rows per reference-arm step")

@@ -72,7 +72,11 @@ int mxq_adder_tree(const float* PA, const float* XA, const float* PB, const floa
   LaneTable lv;
   if (int r = fill_lanes(lv, level_e, level_m, levels, "adder_tree")) return r;
   if (M == 0 || N == 0) return MXQ_OK;
-  return adder_generic(PA, XA, PB, XB, Y, K, M, N, block, (int)size, levels, to_arith(arith), lv, as_stream(stream));
+  ArithP A = to_arith(arith);
+  cudaStream_t st = as_stream(stream);
+  int r = adder_fast(PA, XA, PB, XB, Y, K, M, N, block, (int)size, levels, A, lv, st);
+  if (r != MXQ_ERR_UNSUPPORTED) return r;
+  return adder_generic(PA, XA, PB, XB, Y, K, M, N, block, (int)size, levels, A, lv, st);
 }
 
 int mxq_anchor_tree(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K,

@@ -223,6 +223,7 @@ namespace mxq {
 
 int systolic_fast(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
                   int64_t N, int64_t bs, int size, const ArithP& A, const LaneTable& lanes, cudaStream_t st) {
+  if (A.kind == MXQ_ARITH_MXQUANT) return systolic_mxquant_fast(PA, XA, PB, XB, Y, K, M, N, bs, size, A, lanes, st);
   const bool tapeout = A.kind == MXQ_ARITH_MXGEMMINI && A.prod_e == 4 && A.prod_m == 3 && A.has_floor &&
                        A.floor_thr == 1.52587890625e-05f && A.sat_limit == 448.0f && A.sat_value == 448.0f;
   const bool aligned = M % 4 == 0 && N % 4 == 0 && (uintptr_t)PA % 16 == 0 && (uintptr_t)PB % 16 == 0;

@@ -1,0 +1,201 @@
+// The systolic reducer with MXQuant's arithmetic, MXQUANT(prod_e, prod_m) (mxq/matmul/_arithmetic.py:64-73):
+// product = qtorch ties-away of the float32 product onto float(prod_e, prod_m); each lane adds in float32 and rounds
+// the sum with qtorch ties-away onto its own float(e, m); the finished sum times the scale map is added to the
+// output in float32 (mxq/matmul/_systolic.py:45-61). Bit-identical to the generic kernel at ~14 ALU operations per
+// emulated MAC.
+//
+// The operations are the reference's own: float32 multiply, float32 add, the qtorch rounding on the bit pattern
+// ((bits + half) & mask, float_em.py:64-84). Two of qtorch's rules are taken in a short form, valid within a
+// k-block whose codes are finite and max|a| * max|b| <= 8, for lanes with 4 <= e <= 7 (or e = 8) and a product
+// format with 4 <= prod_e <= 7:
+//   * no value reaches a format's top binade (products <= 8, sums of 16 of them <= 128, below 2^7 * (2 - 2^-m)),
+//     so the saturation to max_num never applies and NaN never appears;
+//   * the fake-subnormal binade -- a rounded q with |q| < 2^-L (L = 2^(e-1) - 1) becomes sign * 2^-L when
+//     |q| > 2^-(L+1), else +0 -- is the RNE snap of q onto multiples of 2^-L, (q + C) - C with C = 1.5 * 2^(23-L):
+//     the tie |q| = 2^-(L+1) goes to the even multiple 0, a negative q that snaps to 0 gives +0 as qtorch does, and
+//     -0 gives +0. For e = 8 the binade lies below every value that can occur and is skipped.
+// A k-block outside the domain (or a short last block) runs the generic element code for that block only.
+#include "common.cuh"
+#include "numerics.cuh"
+#include "reduce_common.cuh"
+#include "reduce_tile.cuh"
+
+using namespace mxq;
+using namespace mxq::tile;
+
+namespace {
+
+// qtorch ties-away rounding onto one float(e, m) as the short form uses it
+struct QFmt {
+  uint32_t half, mask;     // (bits + half) & mask rounds to m fraction bits, ties away from zero
+  float thr, magic;        // |q| < thr: the fake-subnormal snap (q + magic) - magic; thr = 0 for e = 8
+};
+struct QLanes {
+  QFmt lane[16];
+};
+
+QFmt qfmt_for(int e, int m) {
+  QFmt f;
+  const uint32_t drop = 23u - (uint32_t)m;
+  f.half = 1u << (drop - 1u);
+  f.mask = ~((1u << drop) - 1u);
+  if (e == 8) {
+    f.thr = 0.0f;
+    f.magic = 1.0f;
+  } else {
+    const int L = (1 << (e - 1)) - 1;
+    f.thr = u2f((uint32_t)(127 - L) << 23);                  // 2^-L
+    f.magic = u2f(((uint32_t)(150 - L) << 23) | 0x00400000u); // 1.5 * 2^(23 - L)
+  }
+  return f;
+}
+
+__device__ __forceinline__ float qround(float x, const QFmt& f) {
+  const float q = u2f((f2u(x) + f.half) & f.mask);
+  const float t = __fsub_rn(__fadd_rn(q, f.magic), f.magic);
+  return fabsf(q) < f.thr ? t : q;
+}
+
+template <int RM, int RN>
+__global__ void __launch_bounds__(256, 2)
+    k_systolic_mxq(const float* __restrict__ PA, const float* __restrict__ XA, const float* __restrict__ PB,
+                   const float* __restrict__ XB, float* __restrict__ Y, int64_t K, int64_t M, int64_t N, ArithP A,
+                   LaneTable lanes, QFmt qp, QLanes ql) {
+  using TT = Tile<RM, RN>;
+  constexpr int NT = TT::NT, BM = TT::BM, BN = TT::BN, HM = TT::HM, HN = TT::HN;
+  extern __shared__ __align__(16) float smem[];
+  __shared__ float red[3][NT / 32];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
+  const int64_t nblocks = (K + BK - 1) / BK;
+  const int ar0 = ty * HM, ar1 = BM / 2 + ty * HM, bc0 = tx * HN, bc1 = BN / 2 + tx * HN;
+  auto row_of = [&](int i) { return i < HM ? ar0 + i : ar1 + (i - HM); };
+  auto col_of = [&](int j) { return j < HN ? bc0 + j : bc1 + (j - HN); };
+
+  float C[RM][RN], S[RM][RN];
+#pragma unroll
+  for (int i = 0; i < RM; i++)
+#pragma unroll
+    for (int j = 0; j < RN; j++) C[i][j] = 0.0f;
+
+  load_stage<BM, BN, NT>(smem, PA, PB, 0, K, M, N, m0, n0);
+  for (int64_t g = 0; g < nblocks; g++) {
+    const int stage = (int)(g & 1);
+    if (g + 1 < nblocks) {
+      load_stage<BM, BN, NT>(smem + (stage ^ 1) * TT::STAGE, PA, PB, g + 1, K, M, N, m0, n0);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float* As = smem + stage * TT::STAGE;
+    const float* Bs = As + BK * BM;
+    const bool domain = in_domain<BM, BN, NT>(As, red);
+    const int64_t kcount = (K - g * BK) < BK ? (K - g * BK) : BK;
+
+    float xa[RM], xb[RN];
+#pragma unroll
+    for (int i = 0; i < RM; i++) {
+      int64_t r = m0 + row_of(i);
+      xa[i] = r < M ? XA[g * M + r] : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < RN; j++) {
+      int64_t c = n0 + col_of(j);
+      xb[j] = c < N ? XB[g * N + c] : 0.0f;
+    }
+
+    if (domain && kcount == BK) {
+#pragma unroll 1
+      for (int half = 0; half < 2; half++) {
+        const float* Ak = As + half * 16 * BM;
+        const float* Bk = Bs + half * 16 * BN;
+        float a[RM], b[RN];
+        // lane 0: the sum starts at +0, S = q(+0 + p)
+        lds<HM>(a, Ak + ar0);
+        lds<HM>(a + HM, Ak + ar1);
+        lds<HN>(b, Bk + bc0);
+        lds<HN>(b + HN, Bk + bc1);
+        {
+          const QFmt l = ql.lane[0];
+#pragma unroll
+          for (int i = 0; i < RM; i++)
+#pragma unroll
+            for (int j = 0; j < RN; j++) S[i][j] = qround(__fadd_rn(0.0f, qround(__fmul_rn(a[i], b[j]), qp)), l);
+        }
+#pragma unroll 1
+        for (int p = 1; p < 16; p++) {
+          const QFmt l = ql.lane[p];
+          lds<HM>(a, Ak + p * BM + ar0);
+          lds<HM>(a + HM, Ak + p * BM + ar1);
+          lds<HN>(b, Bk + p * BN + bc0);
+          lds<HN>(b + HN, Bk + p * BN + bc1);
+#pragma unroll
+          for (int i = 0; i < RM; i++)
+#pragma unroll
+            for (int j = 0; j < RN; j++) S[i][j] = qround(__fadd_rn(S[i][j], qround(__fmul_rn(a[i], b[j]), qp)), l);
+        }
+        // tile add: C = C + S * (xa * xb), float32
+#pragma unroll
+        for (int i = 0; i < RM; i++)
+#pragma unroll
+          for (int j = 0; j < RN; j++) C[i][j] = __fadd_rn(C[i][j], __fmul_rn(S[i][j], __fmul_rn(xa[i], xb[j])));
+      }
+    } else {
+      for (int kk = 0; kk < kcount; kk++) {
+        const int p = kk & 15;
+        const int e = lanes.e[p], m = lanes.m[p];
+        const bool last = (p == 15) || (kk == kcount - 1);
+#pragma unroll
+        for (int i = 0; i < RM; i++) {
+          const float a = As[kk * BM + row_of(i)];
+#pragma unroll
+          for (int j = 0; j < RN; j++) {
+            float prod = ar_product(A, a, Bs[kk * BN + col_of(j)]);
+            S[i][j] = ar_acc_add(A, p == 0 ? 0.0f : S[i][j], prod, e, m);
+            if (last) C[i][j] = ar_tile_add(A, C[i][j], __fmul_rn(S[i][j], __fmul_rn(xa[i], xb[j])));
+          }
+        }
+      }
+    }
+    __syncthreads();                                   // the stage is refilled next iteration
+  }
+#pragma unroll
+  for (int i = 0; i < RM; i++) {
+    int64_t r = m0 + row_of(i);
+    if (r >= M) continue;
+#pragma unroll
+    for (int j = 0; j < RN; j++) {
+      int64_t c = n0 + col_of(j);
+      if (c < N) Y[r * N + c] = C[i][j];
+    }
+  }
+}
+
+}  // namespace
+
+namespace mxq {
+
+int systolic_mxquant_fast(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K,
+                          int64_t M, int64_t N, int64_t bs, int size, const ArithP& A, const LaneTable& lanes,
+                          cudaStream_t st) {
+  bool ok = A.kind == MXQ_ARITH_MXQUANT && A.prod_e >= 4 && A.prod_e <= 7 && A.prod_m >= 1 && A.prod_m <= 22 &&
+            bs == 32 && size == 16 && M % 4 == 0 && N % 4 == 0 && (uintptr_t)PA % 16 == 0 &&
+            (uintptr_t)PB % 16 == 0 && K > 0;
+  for (int p = 0; ok && p < 16; p++) ok = lanes.e[p] >= 4 && lanes.e[p] <= 8 && lanes.m[p] >= 1 && lanes.m[p] <= 22;
+  if (!ok) return MXQ_ERR_UNSUPPORTED;
+  QLanes ql;
+  for (int p = 0; p < 16; p++) ql.lane[p] = qfmt_for(lanes.e[p], lanes.m[p]);
+  const QFmt qp = qfmt_for(A.prod_e, A.prod_m);
+  constexpr int RM = 4, RN = 8;
+  using TT = Tile<RM, RN>;
+  if (int r = check_cuda(cudaFuncSetAttribute(k_systolic_mxq<RM, RN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)TT::SMEM),
+                         "systolic: shared memory attribute"))
+    return r;
+  dim3 grid((unsigned)((N + TT::BN - 1) / TT::BN), (unsigned)((M + TT::BM - 1) / TT::BM));
+  k_systolic_mxq<RM, RN><<<grid, TT::NT, TT::SMEM, st>>>(PA, XA, PB, XB, Y, K, M, N, A, lanes, qp, ql);
+  return MXQ_LAUNCH_CHECK("systolic");
+}
+
+}  // namespace mxq

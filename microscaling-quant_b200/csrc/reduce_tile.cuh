@@ -22,7 +22,7 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // product truncated to 3 fraction bits (normal or not: anything a mask changes below 2^-126 rounds to 0 later)
 __device__ __forceinline__ float trunc3(float a, float b) { return u2f(f2u(__fmul_rn(a, b)) & 0xfff00000u); }
 
-// One float(4, m) lane, 3 <= m <= 8:
+// One float(4, m) lane, 3 <= m <= 8 (a caller may need a tighter bound):
 //   magic: 1.5 * 2^(17 - m), whose ulp is the lane's subnormal step 2^(-6 - m): (p + magic) - magic is the lane's
 //          RNE of a product |p| <= 8 with 4 significant bits (exact above 2^-6, the snap to the step below it, and
 //          0 for anything under the 2^-16 product flush, which is below half a step)
