@@ -628,9 +628,9 @@ MXQ_HD float q_microsoft_sat(float A, int bits, int exp_bits, float max_norm, in
 //   * float32 subnormals take the clipped exponent min_exp either way.
 // The rounding itself stays the reference's float32 formula: |t| + 0.5 is rounded before the floor, which is not
 // rint (t = 0.5 - 2^-25 gives 1), so "even" keeps its mask on exact even ties.
-MXQ_HD float q_microsoft_ocp(float A, int bits, int exp_bits, float max_norm, int round) {
+// q_microsoft_ocp_core is the part for |A| < 0x7f7fffd4 (finite, log2 below 128); q_microsoft_ocp adds the rest.
+MXQ_HD float q_microsoft_ocp_core(float A, int bits, int exp_bits, float max_norm, int round) {
   const uint32_t u = f2u(A), a = u & 0x7fffffffu;
-  if (a >= 0x7f7fffd4u) return q_microsoft(A, bits, exp_bits, max_norm, round, true);  // inf, NaN, log2 -> 128
   const int min_exp = 2 - (1 << (exp_bits - 1));
   int pe = (round == MS_FLOOR) ? (a ? floor_log2_rn(u2f(a)) : 0) : (int)(a >> 23) - 127;
   pe = pe > min_exp ? pe : min_exp;
@@ -647,6 +647,10 @@ MXQ_HD float q_microsoft_ocp(float A, int bits, int exp_bits, float max_norm, in
   }
   const float val = fminf(mul_rn(r, u2f((uint32_t)(129 - bits + pe) << 23)), max_norm);
   return a == 0u ? 0.0f : u2f(f2u(val) | (u & 0x80000000u));
+}
+MXQ_HD float q_microsoft_ocp(float A, int bits, int exp_bits, float max_norm, int round) {
+  if ((f2u(A) & 0x7fffffffu) >= 0x7f7fffd4u) return q_microsoft(A, bits, exp_bits, max_norm, round, true);
+  return q_microsoft_ocp_core(A, bits, exp_bits, max_norm, round);
 }
 
 }  // namespace mxq

@@ -51,9 +51,9 @@ __device__ __forceinline__ float qtorch_ties_away(float z) {
   return u2f(r);
 }
 
-// float_em._ocp (float_em.py:113-134): q_ocp_bits with the format's constants folded
+// float_em._ocp (float_em.py:113-134): q_ocp_bits with the format's constants folded; the core for finite x
 template <int E, int M>
-__device__ __forceinline__ float ocp_grid(float x, int mode) {
+__device__ __forceinline__ float ocp_grid_core(float x, int mode) {
   constexpr int EMIN_B = 128 - Fmt<E, M>::BIAS;
   const uint32_t u = f2u(x), a = u & 0x7fffffffu;
   int eb = (int)(a >> 23);
@@ -62,7 +62,11 @@ __device__ __forceinline__ float ocp_grid(float x, int mode) {
   const float k = round_nonneg(__fmul_rn(u2f(a), u2f((uint32_t)(254 - sb) << 23)), mode);
   const float val = fminf(__fmul_rn(k, u2f((uint32_t)sb << 23)), Fmt<E, M>::MAX_NORM);
   const float r = u2f(f2u(val) | (u & 0x80000000u));
-  return a == 0u ? 0.0f : (a >= 0x7f800000u ? x : r);
+  return a == 0u ? 0.0f : r;
+}
+template <int E, int M>
+__device__ __forceinline__ float ocp_grid(float x, int mode) {
+  return (f2u(x) & 0x7fffffffu) >= 0x7f800000u ? x : ocp_grid_core<E, M>(x, mode);
 }
 
 template <int FAM, int E, int M>
@@ -70,6 +74,16 @@ __device__ __forceinline__ float element(float z, const TParams& p) {
   if (FAM == MXQ_FAMILY_MXQUANT) return qtorch_ties_away<E, M>(z);
   if (FAM == MXQ_FAMILY_MXGEMMINI) return ocp_grid<E, M>(z, p.rounding);
   return q_microsoft_ocp(z, M + 2, E, Fmt<E, M>::MAX_NORM, p.rounding);
+}
+
+// The element step of a clean tile (every block finite, every scale a power of two with an exact reciprocal): z is
+// then finite and |z| < 2^17, so the Inf / NaN / huge-value branches cannot be taken, and the rounding mode is a
+// template argument.
+template <int FAM, int E, int M, int MODE>
+__device__ __forceinline__ float element_clean(float z) {
+  if (FAM == MXQ_FAMILY_MXQUANT) return qtorch_ties_away<E, M>(z);
+  if (FAM == MXQ_FAMILY_MXGEMMINI) return ocp_grid_core<E, M>(z, MODE);
+  return q_microsoft_ocp_core(z, M + 2, E, Fmt<E, M>::MAX_NORM, MODE);
 }
 
 template <int FAM, int E, int M>
@@ -94,6 +108,35 @@ template <int FAM>
 __device__ __forceinline__ float divide(float v, float x, float r) {
   if (r != 0.0f) return __fmul_rn(v, r);
   return FAM == MXQ_FAMILY_MXQUANT ? x86_div(v, x) : div_rn(v, x);
+}
+
+// (2) for a clean tile: every thread quantizes 8 float4 (float4 q = tid + 256 i: row q / 64, float4 column q % 64)
+template <int FAM, int E, int M, bool COLS, int MODE>
+__device__ __forceinline__ void pass_clean(const float* T, const float* s_r, float* __restrict__ P, int64_t rest,
+                                           int64_t ct, int64_t nb, int64_t outer, int64_t len, int64_t inner) {
+  const int tid = threadIdx.x, c4 = tid & 63;
+  float4 rs;
+  if (COLS) rs = *reinterpret_cast<const float4*>(s_r + c4 * 4);
+#pragma unroll 2
+  for (int i = 0; i < 8; i++) {
+    const int row = (tid >> 6) + 4 * i;
+    float4 v = reinterpret_cast<const float4*>(T + row * TC)[c4];
+    if (!COLS) {
+      const float r = s_r[row * 8 + (c4 >> 3)];
+      rs = make_float4(r, r, r, r);
+    }
+    v.x = element_clean<FAM, E, M, MODE>(__fmul_rn(v.x, rs.x));
+    v.y = element_clean<FAM, E, M, MODE>(__fmul_rn(v.y, rs.y));
+    v.z = element_clean<FAM, E, M, MODE>(__fmul_rn(v.z, rs.z));
+    v.w = element_clean<FAM, E, M, MODE>(__fmul_rn(v.w, rs.w));
+    if (COLS) {
+      const int64_t b = rest % nb, o = rest / nb, l = b * TR + row, col = ct * TC + c4 * 4;
+      if (l < len && col < inner) __stcs(reinterpret_cast<float4*>(P + (o * len + l) * inner + col), v);
+    } else {
+      const int64_t grow = rest * TR + row, col = ct * TC + c4 * 4;
+      if (grow < outer && col < len) __stcs(reinterpret_cast<float4*>(P + grow * len + col), v);
+    }
+  }
 }
 
 template <int FAM, int E, int M, bool COLS>
@@ -137,6 +180,7 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     const int64_t ct = tile % ctiles, rest = tile / ctiles;
 
     // (1) block scales
+    bool bad;
     if (COLS) {
       const int64_t b = rest % nb, o = rest / nb, col = ct * TC + tid;
       uint32_t mbits = 0u;                                  // max |v| as bits: a NaN pattern tops every number
@@ -144,8 +188,10 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
       for (int r = 0; r < TR; r++) mbits = max(mbits, f2u(T[r * TC + tid]) & 0x7fffffffu);
       const bool nan = mbits > 0x7f800000u;
       const float x = block_scale<FAM, E, M>(nan ? qnan_f() : u2f(mbits), prm);
+      const float r = reciprocal_of<FAM>(x, nan);
       s_x[tid] = x;
-      s_r[tid] = reciprocal_of<FAM>(x, nan);
+      s_r[tid] = r;
+      bad = col < inner && (mbits >= 0x7f800000u || r == 0.0f);     // padding columns do not vote
       if (col < inner) X[(o * nb + b) * inner + col] = x;
     } else {
       const int row = tid >> 3, blk = tid & 7;                // 32 rows x 8 blocks
@@ -159,12 +205,26 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
       }
       const bool nan = mbits > 0x7f800000u;
       const float x = block_scale<FAM, E, M>(nan ? qnan_f() : u2f(mbits), prm);
+      const float r = reciprocal_of<FAM>(x, nan);
       s_x[tid] = x;
-      s_r[tid] = reciprocal_of<FAM>(x, nan);
+      s_r[tid] = r;
       const int64_t grow = rest * TR + row, gblk = ct * (TC / 32) + blk;
+      bad = grow < outer && gblk < nb && (mbits >= 0x7f800000u || r == 0.0f);   // padding blocks do not vote
       if (grow < outer && gblk < nb) X[grow * nb + gblk] = x;
     }
-    __syncthreads();
+    const bool clean = !__syncthreads_or(bad);              // the whole tile takes the short element step
+
+    if (clean) {
+      if (FAM == MXQ_FAMILY_MXQUANT || prm.rounding == 0)
+        pass_clean<FAM, E, M, COLS, 0>(T, s_r, P, rest, ct, nb, outer, len, inner);
+      else if (prm.rounding == 1)
+        pass_clean<FAM, E, M, COLS, 1>(T, s_r, P, rest, ct, nb, outer, len, inner);
+      else
+        pass_clean<FAM, E, M, COLS, 2>(T, s_r, P, rest, ct, nb, outer, len, inner);
+      __syncthreads();                                      // every thread is done with this stage and s_x / s_r
+      if (tid == 0 && tile + (int64_t)STAGES * gridDim.x < ntiles) issue(tile + (int64_t)STAGES * gridDim.x, stage);
+      continue;
+    }
 
     // (2) elements: float4 q = tid + 256 i of the tile (row q / 64, float4 column q % 64)
     const int c4 = tid & 63;

@@ -113,7 +113,11 @@ int mxq_anchor_tree(const float* PA, const float* XA, const float* PB, const flo
     }
   }
   if (M == 0 || N == 0) return MXQ_OK;
-  return anchor_generic(PA, XA, PB, XB, Y, K, M, N, block, (int)size, to_arith(arith), at, as_stream(stream));
+  ArithP A = to_arith(arith);
+  cudaStream_t st = as_stream(stream);
+  int r = anchor_fast(PA, XA, PB, XB, Y, K, M, N, block, (int)size, A, at, st);
+  if (r != MXQ_ERR_UNSUPPORTED) return r;
+  return anchor_generic(PA, XA, PB, XB, Y, K, M, N, block, (int)size, A, at, st);
 }
 
 int mxq_fp64_accum(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,

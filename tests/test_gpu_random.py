@@ -175,6 +175,36 @@ def test_systolic_mxquant_fast_equals_generic(oracle, prod, lanes):
     assert_bits(fast, want, "fast vs oracle")
 
 
+@pytest.mark.parametrize("kw", [{}, {"drop": "rne"}, {"bits": [16] * 6, "headroom": 6},
+                                {"bits": [20, 20, 19, 19, 18, 18]}, {"emin": -6}])
+def test_anchor_fast_equals_generic(oracle, kw):
+    """The one-tree anchor kernel (M, N multiples of 4) against the generic kernel (M = 127) and the oracle, on
+    defaults, RNE drops and narrower levels; unequal level widths and emin are outside it (generic route). The
+    operands hold a k-block over the fast bound, an Inf code, a short last block, output columns whose products are
+    all tiny (the anchor from the products one by one) and small ones that need the 2^-16 flush."""
+    import torch
+    import mxq
+    rng = np.random.default_rng(80)
+    K, M, N = 330, 128, 96
+    A = (rng.standard_normal((K, M)) * 2.0 ** rng.uniform(-12, 12, (1, M))).astype(np.float32)
+    B = (rng.standard_normal((K, N)) * 2.0 ** rng.uniform(-12, 12, (1, N))).astype(np.float32)
+    P_A, X_A = mxq.block.mxgemmini.quantize(torch.from_numpy(A).cuda(), "MXFP8_E4M3", axis=0)
+    P_B, X_B = mxq.block.mxgemmini.quantize(torch.from_numpy(B).cuda(), "MXFP8_E4M3", axis=0)
+    P_A[40:72, 5] *= 3.0                                   # a block whose products exceed the fast bound
+    P_B[200, 7] = float("inf")
+    P_A[:, 10] *= 2.0 ** -9                                # every product of row 10 tiny: below 2^-16 with small b
+    P_B[:, 11] *= 2.0 ** -9
+    P_A[:, 12] *= 2.0 ** -4                                # labels around -5: the grid falls below 2^-16
+    P_B[:, 13] *= 2.0 ** -4
+    ar = mxq.matmul.MXGEMMINI()
+    fast = mxq.matmul.anchor_tree(P_A, X_A, P_B, X_B, ar, **kw)
+    generic = mxq.matmul.anchor_tree(P_A[:, :127].contiguous(), X_A[:, :127].contiguous(), P_B, X_B, ar, **kw)
+    assert_bits(fast[:127], generic, "fast vs generic")
+    want = oracle.anchor_tree(P_A.cpu().numpy(), X_A.cpu().numpy(), P_B.cpu().numpy(), X_B.cpu().numpy(),
+                              oracle.arith_mxgemmini(), **kw)
+    assert_bits(fast, want, "fast vs oracle")
+
+
 @pytest.mark.parametrize("levels", [[(4, 4), (4, 5), (4, 6), (8, 7)], [(4, 3), (4, 3), (4, 7), (8, 7)],
                                     [(4, 3), (4, 4), (4, 8), (8, 7)]])
 def test_adder_fast_equals_generic(oracle, levels):
