@@ -179,6 +179,17 @@ int mxq_lut_decode(const int64_t* codes, float* out, int64_t n, int32_t e, int32
 int mxq_lut_finder(const int64_t* codes, const float* T, int64_t* I, int64_t K, int64_t n, int32_t group, int32_t e,
                    int32_t m, int32_t* status, void* stream);
 
+/* mxq/block/lut.py:23-34 quantize in one call: block.mxgemmini codes of the 2-D V (rows x cols, blocks along
+ * `axis`), the tables of the K x n operand (axis 0: V itself; axis 1: V's transpose, read in place), every code
+ * replaced by its table entry. P_lut has V's layout; X is the scales (as mxq_block_quantize writes them). spec must be
+ * the mxgemmini family without `via` and a LUT format. The codes and the tables live in `workspace`, at least
+ * mxq_block_lut_workspace(rows, cols, axis, group) bytes, 256-byte aligned (-1 for bad sizes). `status` as for
+ * mxq_lut_tables (1: a code is not on the format's grid, e.g. from a NaN or Inf in V). Asynchronous. */
+int64_t mxq_block_lut_workspace(int64_t rows, int64_t cols, int32_t axis, int32_t group);
+int mxq_block_lut_quantize(const float* V, float* P_lut, float* X, int64_t rows, int64_t cols, int32_t axis,
+                           int64_t block, const mxq_quant_spec* spec, int32_t group, int32_t max_iters,
+                           void* workspace, int64_t workspace_bytes, int32_t* status, void* stream);
+
 /* ------------------------------------------------------------------------------------------ diagnostics */
 /* No reference counterpart: the number of bounded shared-memory waits (mbarrier) that gave up in the TMA-staged
  * kernels on the current device since the library was loaded. Always 0 in a correct run; synchronous. */

@@ -1,0 +1,55 @@
+// block.lut.quantize (mxq/block/lut.py:23-34) as one C-ABI call: the fused mxgemmini quantizer writes V's codes
+// into a workspace, the table fit reads them as the K x n operand (axis 0: V itself; axis 1: V read transposed in
+// place) and writes its tables into the same workspace, and pick with lookup replaces every code by its table
+// entry in V's layout. Three kernels on one stream; nothing is allocated and nothing waits on the host.
+#include "common.cuh"
+
+namespace {
+
+constexpr int64_t kAlign = 256;
+constexpr int kTableWidth = 16;        // mxq/lut/__init__.py SIZE
+
+int64_t round_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+bool lut_format(int e, int m) { return (e == 3 && m == 2) || (e == 2 && m == 3) || (e == 5 && m == 2) || (e == 4 && m == 3); }
+
+}  // namespace
+
+extern "C" {
+
+int64_t mxq_block_lut_workspace(int64_t rows, int64_t cols, int32_t axis, int32_t group) {
+  if (rows < 0 || cols < 0 || group < 0 || group >= 31) return -1;
+  const int64_t n = (axis % 2 == 0) ? cols : rows;
+  const int64_t ng = (n + ((int64_t)1 << group) - 1) >> group;
+  return round_up(rows * cols * (int64_t)sizeof(float)) + round_up(ng * kTableWidth * (int64_t)sizeof(float));
+}
+
+int mxq_block_lut_quantize(const float* V, float* P_lut, float* X, int64_t rows, int64_t cols, int32_t axis,
+                           int64_t block, const mxq_quant_spec* spec, int32_t group, int32_t max_iters,
+                           void* workspace, int64_t workspace_bytes, int32_t* status, void* stream) {
+  MXQ_REQUIRE(spec != nullptr, MXQ_ERR_VALUE, "block.lut: no spec");
+  MXQ_REQUIRE(axis >= -2 && axis <= 1, MXQ_ERR_VALUE, "block.lut: V must be 2-D with axis 0 or 1, got axis %d", axis);
+  MXQ_REQUIRE(spec->family == MXQ_FAMILY_MXGEMMINI && spec->via_e == 0, MXQ_ERR_VALUE,
+              "block.lut: the codes come from block.mxgemmini without via");
+  MXQ_REQUIRE(lut_format(spec->e, spec->m), MXQ_ERR_VALUE, "mxq.lut: no LUT format (e=%d, m=%d)", spec->e, spec->m);
+  MXQ_REQUIRE(status != nullptr, MXQ_ERR_VALUE, "block.lut: no status word");
+  const int64_t need = mxq_block_lut_workspace(rows, cols, axis, group);
+  MXQ_REQUIRE(need >= 0, MXQ_ERR_VALUE, "block.lut: bad sizes (%lld x %lld, group %d)", (long long)rows,
+              (long long)cols, group);
+  MXQ_REQUIRE(need == 0 || (workspace != nullptr && workspace_bytes >= need && (uintptr_t)workspace % kAlign == 0),
+              MXQ_ERR_VALUE,
+              "block.lut: the workspace needs %lld bytes, 256-byte aligned (got %lld)", (long long)need,
+              (long long)workspace_bytes);
+  const bool ax0 = axis % 2 == 0;
+  float* P = static_cast<float*>(workspace);
+  float* T = reinterpret_cast<float*>(static_cast<char*>(workspace) + round_up(rows * cols * (int64_t)sizeof(float)));
+  // the codes: V viewed as [outer, len, inner] with blocks along `axis`
+  const int64_t outer = ax0 ? 1 : rows, len = ax0 ? rows : cols, inner = ax0 ? cols : 1;
+  if (int r = mxq_block_quantize(V, P, X, outer, len, inner, block, spec, stream)) return r;
+  // the K x n operand: axis 0 is V's own layout; axis 1 reads V's transpose in place
+  const int64_t K = ax0 ? rows : cols, n = ax0 ? cols : rows, sk = ax0 ? cols : 1, sj = ax0 ? 1 : cols;
+  if (int r = mxq_lut_tables(P, T, K, n, sk, sj, group, max_iters, spec->e, spec->m, status, stream)) return r;
+  return mxq_lut_pick_lookup(P, T, P_lut, K, n, sk, sj, group, kTableWidth, stream);
+}
+
+}  // extern "C"

@@ -75,6 +75,7 @@ _SIGS = {
     "mxq_lut_tables": [P, P, I64, I64, I64, I64, I32, I32, I32, I32, P, P],
     "mxq_lut_pick": [P, P, P, I64, I64, I64, I64, I32, I32, P],
     "mxq_lut_pick_lookup": [P, P, P, I64, I64, I64, I64, I32, I32, P],
+    "mxq_block_lut_quantize": [P, P, P, I64, I64, I32, I64, ctypes.POINTER(MxqQuantSpec), I32, I32, P, I64, P, P],
     "mxq_lut_lookup": [P, P, P, I64, I64, I32, I32, P],
     "mxq_lut_encode": [P, P, I64, I32, I32, P, P],
     "mxq_lut_decode": [P, P, I64, I32, I32, P, P],
@@ -98,6 +99,8 @@ def lib():
                     f = getattr(L, name)
                     f.argtypes = args
                     f.restype = I32
+                L.mxq_block_lut_workspace.argtypes = [I64, I64, I32, I32]
+                L.mxq_block_lut_workspace.restype = I64
                 L.mxq_last_error.restype = ctypes.c_char_p
                 L.mxq_version.restype = ctypes.c_char_p
                 _lib = L

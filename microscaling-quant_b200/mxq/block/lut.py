@@ -5,13 +5,15 @@ keyword-required, as in the reference.
     P, X = quantize(V, "MXFP6_E3M2", axis=0, block_size=32, rounding_mode="rne", scale_floor=2**-23,
                     group=1, max_iters=50)                                V_hat = P * expand(X)
 
-Three kernels: the fused block quantizer, the table fit, and pick with lookup fused; an axis-1 operand is read
-transposed in place, never copied.
+One C call (mxq_block_lut_quantize): the fused block quantizer, the table fit and pick with lookup fused, the
+codes and tables in a workspace; an axis-1 operand is read transposed in place, never copied.
 """
+import ctypes
+
 import torch
 
 from . import _driver, mxgemmini
-from .. import lut
+from .. import _lib, lut
 
 __all__ = ["quantize", "dequantize"]
 
@@ -21,13 +23,29 @@ def quantize(V: torch.Tensor, fmt, axis: int, block_size: int, *, rounding_mode:
     """block.mxgemmini.quantize, then each code replaced by its table entry. Returns (P, X), float32."""
     if V.ndim != 2 or axis not in (0, 1, -1, -2):
         raise ValueError(f"block.lut: V must be 2-D with axis 0 or 1, got shape {tuple(V.shape)}, axis {axis}")
-    lut.formats._format(fmt)                                   # refuse a non-LUT format first
-    P, X = mxgemmini.quantize(V, fmt, axis=axis, block_size=block_size, rounding_mode=rounding_mode,
-                              scale_floor=scale_floor)
-    Pk = P if axis % 2 == 0 else P.t()                         # K×n (a view for axis 1)
-    T = lut.tables(Pk, fmt, group=group, max_iters=max_iters)
-    P_lut = lut.kmeans.pick_lookup(Pk, T, group=group)
-    return (P_lut if axis % 2 == 0 else P_lut.t()).contiguous(), X
+    f = lut.formats._format(fmt)                               # refuse a non-LUT format first
+    spec = mxgemmini.spec(fmt, rounding_mode, scale_floor)     # then what block.mxgemmini refuses
+    _driver._layout(V, axis, block_size)
+    lut.kmeans._check(V if axis % 2 == 0 else V.t(), group)    # then what lut.tables refuses
+    if not isinstance(max_iters, int) or isinstance(max_iters, bool) or max_iters < 0:
+        raise ValueError(f"mxq.lut: max_iters {max_iters!r} must be a non-negative integer")
+    home = _lib.home(V)
+    dev = _lib.device_for(V)
+    v = _lib.on(V, dev)
+    rows, cols = v.shape
+    ax = axis % 2
+    P = torch.empty_like(v)
+    xshape = [rows, cols]
+    xshape[ax] = (xshape[ax] + block_size - 1) // block_size
+    X = torch.empty(xshape, dtype=torch.float32, device=dev)
+    ws = torch.empty(max(1, _lib.lib().mxq_block_lut_workspace(rows, cols, ax, group)), dtype=torch.uint8,
+                     device=dev)
+    st = torch.empty(1, dtype=torch.int32, device=dev)
+    _lib.run("mxq_block_lut_quantize", dev, _lib.ptr(v), _lib.ptr(P), _lib.ptr(X), rows, cols, ax, block_size,
+             ctypes.byref(spec), group, max_iters, _lib.ptr(ws), ws.numel(), _lib.ptr(st))
+    if int(st.item()):
+        raise ValueError(f"mxq.lut: P holds a value that is not a {f.name} code; quantize it first")
+    return _lib.back(P, home), _lib.back(X, home)
 
 
 def dequantize(P: torch.Tensor, X: torch.Tensor, axis: int = 0, block_size: int = _driver.BLOCK) -> torch.Tensor:
