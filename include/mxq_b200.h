@@ -189,6 +189,14 @@ int64_t mxq_block_lut_workspace(int64_t rows, int64_t cols, int32_t axis, int32_
 int mxq_block_lut_quantize(const float* V, float* P_lut, float* X, int64_t rows, int64_t cols, int32_t axis,
                            int64_t block, const mxq_quant_spec* spec, int32_t group, int32_t max_iters,
                            void* workspace, int64_t workspace_bytes, int32_t* status, void* stream);
+/* No counterpart in the reference: mxq_block_lut_quantize with its workspace taken from a static device array of
+ * 16 MiB (one per device) instead of the caller, so the call allocates nothing. Sizes whose workspace
+ * (mxq_block_lut_workspace) exceeds 16 MiB are rejected with MXQ_ERR_VALUE. Every call on a device shares the
+ * array: calls whose work overlaps on the GPU (other streams, or other host threads, without ordering between
+ * them) race on it. Nothing in the array needs to start at zero. */
+int mxq_block_lut_quantize_static(const float* V, float* P_lut, float* X, int64_t rows, int64_t cols, int32_t axis,
+                                  int64_t block, const mxq_quant_spec* spec, int32_t group, int32_t max_iters,
+                                  int32_t* status, void* stream);
 
 /* ------------------------------------------------------------------------------------------ diagnostics */
 /* No reference counterpart: the number of bounded shared-memory waits (mbarrier) that gave up in the TMA-staged

@@ -4,6 +4,14 @@
 // entry in V's layout. Three kernels on one stream; nothing is allocated and nothing waits on the host.
 #include "common.cuh"
 
+#include <mutex>
+
+using namespace mxq;
+
+// The scratch of mxq_block_lut_quantize_static: one array per device, shared by every call on that device.
+constexpr int64_t kStaticScratchBytes = (int64_t)16 << 20;
+static __device__ __align__(256) unsigned char g_block_lut_scratch[kStaticScratchBytes];
+
 namespace {
 
 constexpr int64_t kAlign = 256;
@@ -12,6 +20,26 @@ constexpr int kTableWidth = 16;        // mxq/lut/__init__.py SIZE
 int64_t round_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 bool lut_format(int e, int m) { return (e == 3 && m == 2) || (e == 2 && m == 3) || (e == 5 && m == 2) || (e == 4 && m == 3); }
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+// The current device's address of g_block_lut_scratch, looked up once per device with that device current.
+int static_scratch(void** out) {
+  int dev = 0;
+  if (int r = check_cuda(cudaGetDevice(&dev), "block.lut static scratch: current device")) return r;
+  MXQ_REQUIRE(dev >= 0 && dev < kMaxDevices, MXQ_ERR_UNSUPPORTED, "block.lut static scratch: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (int r = check_cuda(cudaGetSymbolAddress(&p, g_block_lut_scratch), "block.lut static scratch: address"))
+      return r;
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return MXQ_OK;
+}
 
 }  // namespace
 
@@ -50,6 +78,22 @@ int mxq_block_lut_quantize(const float* V, float* P_lut, float* X, int64_t rows,
   const int64_t K = ax0 ? rows : cols, n = ax0 ? cols : rows, sk = ax0 ? cols : 1, sj = ax0 ? 1 : cols;
   if (int r = mxq_lut_tables(P, T, K, n, sk, sj, group, max_iters, spec->e, spec->m, status, stream)) return r;
   return mxq_lut_pick_lookup(P, T, P_lut, K, n, sk, sj, group, kTableWidth, stream);
+}
+
+int mxq_block_lut_quantize_static(const float* V, float* P_lut, float* X, int64_t rows, int64_t cols, int32_t axis,
+                                  int64_t block, const mxq_quant_spec* spec, int32_t group, int32_t max_iters,
+                                  int32_t* status, void* stream) {
+  const int64_t need = mxq_block_lut_workspace(rows, cols, axis, group);
+  MXQ_REQUIRE(need >= 0, MXQ_ERR_VALUE, "block.lut: bad sizes (%lld x %lld, group %d)", (long long)rows,
+              (long long)cols, group);
+  MXQ_REQUIRE(need <= kStaticScratchBytes, MXQ_ERR_VALUE,
+              "block.lut static scratch: %lld x %lld at group %d needs %lld bytes of scratch, above the %lld-byte "
+              "maximum (call mxq_block_lut_quantize with a workspace instead)",
+              (long long)rows, (long long)cols, group, (long long)need, (long long)kStaticScratchBytes);
+  void* scratch = nullptr;
+  if (int r = static_scratch(&scratch)) return r;
+  return mxq_block_lut_quantize(V, P_lut, X, rows, cols, axis, block, spec, group, max_iters, scratch,
+                                kStaticScratchBytes, status, stream);
 }
 
 }  // extern "C"

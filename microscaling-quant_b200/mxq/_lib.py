@@ -76,6 +76,7 @@ _SIGS = {
     "mxq_lut_pick": [P, P, P, I64, I64, I64, I64, I32, I32, P],
     "mxq_lut_pick_lookup": [P, P, P, I64, I64, I64, I64, I32, I32, P],
     "mxq_block_lut_quantize": [P, P, P, I64, I64, I32, I64, ctypes.POINTER(MxqQuantSpec), I32, I32, P, I64, P, P],
+    "mxq_block_lut_quantize_static": [P, P, P, I64, I64, I32, I64, ctypes.POINTER(MxqQuantSpec), I32, I32, P, P],
     "mxq_lut_lookup": [P, P, P, I64, I64, I32, I32, P],
     "mxq_lut_encode": [P, P, I64, I32, I32, P, P],
     "mxq_lut_decode": [P, P, I64, I32, I32, P, P],
