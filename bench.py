@@ -166,25 +166,28 @@ def run_gpu(args):
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
         step()
-    per = {}
-    for f, fmt, ax in runs:                                 # per-kernel launch durations (after warm-up)
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * 3)]
-        for i in range(3):
-            ev[2 * i].record(stream)
-            quant[f](V, fmt, axis=ax)
-            ev[2 * i + 1].record(stream)
-        torch.cuda.synchronize()
-        per[(f, fmt, ax)] = sum(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(3)) / 3
+    # per-launch durations: events around every launch of the first `nev` timed steps, on the launching stream
+    nev = min(args.steps, 20)
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in runs]
+           for _ in range(nev)]
     barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
         barrier()
         start.record(stream)
-        for _ in range(args.steps):
-            step()
+        for s in range(args.steps):
+            if s < nev:
+                for (f, fmt, ax), (e0, e1) in zip(runs, evs[s]):
+                    e0.record(stream)
+                    quant[f](V, fmt, axis=ax)
+                    e1.record(stream)
+            else:
+                step()
         end.record(stream)
         barrier()
     ms = max_over_ranks(start.elapsed_time(end))
+    per = {run: sum(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(nev)) / nev
+           for i, run in enumerate(runs)}
     ms_step = ms / args.steps
     elems = ROWS * COLS
     total_bytes = BYTES_PER_ELEM * elems * len(runs) * world
@@ -219,8 +222,8 @@ def run_gpu(args):
     barrier()
     e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3) / e2e_steps
     e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
-    h2d = 4 * elems * len(runs)
-    d2h = (4 * elems + 4 * elems // 32) * len(runs)
+    h2d = 4 * elems * len(runs) * world                     # whole job, like value
+    d2h = (4 * elems + 4 * elems // 32) * len(runs) * world
 
     # -- config 3: the systolic GEMM, one 4096-column panel per rank
     gsteps = max(1, args.gemm_steps)

@@ -588,12 +588,12 @@ MXQ_HD float round_nonneg(float k, int mode) {        // round_int of a value 0 
 }
 MXQ_HD float q_ocp_bits(float x, int e, int m, int mode, float max_norm) {
   uint32_t u = f2u(x), a = u & 0x7fffffffu;
-  int emin_b = 128 - bias_of(e);                       // biased emin; float32 subnormals read biased 0
-  int eb = (int)(a >> 23);
-  eb = eb > emin_b ? eb : emin_b;
-  int sb = eb - m;                                     // biased exponent of the step 2^s (normal)
-  float k = round_nonneg(mul_rn(u2f(a), u2f((uint32_t)(254 - sb) << 23)), mode);
-  float val = fminf(mul_rn(k, u2f((uint32_t)sb << 23)), max_norm);
+  // the binade's biased exponent field in place, clipped below at emin (float32 subnormals read biased 0); the
+  // step is 2^s with biased field sb = eb - m (normal)
+  const uint32_t lo = (uint32_t)(128 - bias_of(e)) << 23;
+  const uint32_t e23 = (a & 0x7f800000u) > lo ? (a & 0x7f800000u) : lo;
+  float k = round_nonneg(mul_rn(u2f(a), u2f(((uint32_t)(254 + m) << 23) - e23)), mode);     // |x| / 2^s
+  float val = fminf(mul_rn(k, u2f(e23 - ((uint32_t)m << 23))), max_norm);                   // k * 2^s
   float r = u2f(f2u(val) | (u & 0x80000000u));
   return a == 0u ? 0.0f : (a >= 0x7f800000u ? x : r);
 }
@@ -632,20 +632,27 @@ MXQ_HD float q_microsoft_sat(float A, int bits, int exp_bits, float max_norm, in
 MXQ_HD float q_microsoft_ocp_core(float A, int bits, int exp_bits, float max_norm, int round) {
   const uint32_t u = f2u(A), a = u & 0x7fffffffu;
   const int min_exp = 2 - (1 << (exp_bits - 1));
-  int pe = (round == MS_FLOOR) ? (a ? floor_log2_rn(u2f(a)) : 0) : (int)(a >> 23) - 127;
-  pe = pe > min_exp ? pe : min_exp;
-  const float t = mul_rn(u2f(a), u2f((uint32_t)(125 + bits - pe) << 23));   // |A| / 2^pe * 2^(bits-2)
-  float r;
-  if (round == MS_FLOOR) {                                     // t < 2^(bits-1): small-value roundings apply
-    r = floor_small(t);
+  // e23: the private exponent's biased field in place, E << 23 with E = pe + 127 (pe clipped below at min_exp)
+  uint32_t e23;
+  if (round == MS_FLOOR) {
+    int pe = a ? floor_log2_rn(u2f(a)) : 0;
+    e23 = (uint32_t)((pe > min_exp ? pe : min_exp) + 127) << 23;
   } else {
-    r = floor_small(add_rn(t, 0.5f));
-    if (round == MS_EVEN) {                                    // (|t| - 0.5) % 2 == 0: an exact even tie
-      const float y = sub_rn(t, 0.5f), h = mul_rn(y, 0.5f);
-      r = sub_rn(r, (y >= 0.0f && floor_small(h) == h) ? 1.0f : 0.0f);
-    }
+    const uint32_t lo = (uint32_t)(min_exp + 127) << 23;
+    e23 = (a & 0x7f800000u) > lo ? (a & 0x7f800000u) : lo;
   }
-  const float val = fminf(mul_rn(r, u2f((uint32_t)(129 - bits + pe) << 23)), max_norm);
+  const float t = mul_rn(u2f(a), u2f(((uint32_t)(252 + bits) << 23) - e23));  // |A| / 2^pe * 2^(bits-2), < 2^(bits-1)
+  float r;
+  if (round == MS_FLOOR) {
+    r = floor_small(t);
+  } else if (round == MS_NEAREST) {
+    r = floor_small(add_rn(t, 0.5f));
+  } else {
+    // floor(fl(t + 0.5)) minus 1 when t - 0.5 is an even integer: for every t >= 0 that is rint(t) (ties to even),
+    // except t = 0.5 - 2^-25, the one value whose float32 sum with 0.5 ties up to 1.0
+    r = add_rn(rint_small(t), f2u(t) == 0x3effffffu ? 1.0f : 0.0f);
+  }
+  const float val = fminf(mul_rn(r, u2f(e23 - ((uint32_t)(bits - 2) << 23))), max_norm);   // r * 2^(pe-bits+2)
   return a == 0u ? 0.0f : u2f(f2u(val) | (u & 0x80000000u));
 }
 MXQ_HD float q_microsoft_ocp(float A, int bits, int exp_bits, float max_norm, int round) {

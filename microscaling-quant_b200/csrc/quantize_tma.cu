@@ -1,15 +1,19 @@
-// The block quantizers' main kernel on sm_100a: persistent CTAs stream 32 x 256 float32 tiles of V through shared
-// memory with TMA (cp.async.bulk.tensor, two stages, mbarrier-tracked), so each tile's load overlaps the previous
-// tile's arithmetic, and one pass over HBM reads V once and writes P and X once.
+// The block quantizers' main kernel on sm_100a: persistent CTAs stream 32 x TC float32 tiles of V (TC = 256) through
+// shared memory with TMA (cp.async.bulk.tensor, two stages, mbarrier-tracked), so each tile's load overlaps the
+// previous tile's arithmetic, and one pass over HBM reads V once and writes P and X once. (32 x 128 tiles, five
+// CTAs per SM instead of three, measured slower: the per-tile work no longer covers the per-tile synchronisation.)
 //
 // Two layouts of the [outer, len, inner] view (blocks of 32 along len):
-//   ROWS (inner == 1): a tile is 32 rows x 256 consecutive values of a row, i.e. 8 blocks per row;
-//   COLS (inner > 1):  a tile is one block of 32 rows (along len) x 256 columns (along inner).
+//   ROWS (inner == 1): a tile is 32 rows x TC consecutive values of a row, i.e. TC / 32 blocks per row;
+//   COLS (inner > 1):  a tile is one block of 32 rows (along len) x TC columns (along inner).
 // Per tile: (1) one thread per block takes the block max from shared memory and computes the block's scale and
 // reciprocal (ROWS: a thread reads its block's 8 float4 in a rotated order, so a quarter-warp hits 32 distinct
-// banks; COLS: a thread walks its column); (2) every thread quantizes 8 float4 of the tile, reading values and
-// scales from shared memory and writing P with coalesced 128-bit streaming stores.
+// banks; COLS: a thread walks its column), and the CTA votes whether every block is clean (finite, with a
+// power-of-two scale); (2) every thread quantizes its float4 of the tile, reading values and scales from shared
+// memory and writing P with coalesced 128-bit streaming stores -- a clean tile with the short element step.
 // The element format is a template parameter, so the grid constants of each format fold into immediates.
+#include <atomic>
+
 #include "common.cuh"
 #include "numerics.cuh"
 #include "tma.cuh"
@@ -19,6 +23,11 @@ using namespace mxq;
 namespace {
 
 constexpr int TR = 32, TC = 256, NT = 256, STAGES = 2;
+constexpr int C4 = TC / 4;              // float4 per tile row
+constexpr int BPR = TC / 32;            // blocks per tile row (ROWS layout)
+constexpr int RPI = NT / C4;            // tile rows per pass of the CTA in the element step
+static_assert(TC % 32 == 0 && TC <= NT && NT % C4 == 0 && TR % RPI == 0, "tile shape");
+constexpr int kMaxDevices = 64;
 constexpr unsigned TILE_BYTES = TR * TC * sizeof(float);
 
 struct TParams {
@@ -54,13 +63,11 @@ __device__ __forceinline__ float qtorch_ties_away(float z) {
 // float_em._ocp (float_em.py:113-134): q_ocp_bits with the format's constants folded; the core for finite x
 template <int E, int M>
 __device__ __forceinline__ float ocp_grid_core(float x, int mode) {
-  constexpr int EMIN_B = 128 - Fmt<E, M>::BIAS;
+  constexpr uint32_t LO = (uint32_t)(128 - Fmt<E, M>::BIAS) << 23;     // biased emin in place
   const uint32_t u = f2u(x), a = u & 0x7fffffffu;
-  int eb = (int)(a >> 23);
-  eb = eb > EMIN_B ? eb : EMIN_B;
-  const int sb = eb - M;
-  const float k = round_nonneg(__fmul_rn(u2f(a), u2f((uint32_t)(254 - sb) << 23)), mode);
-  const float val = fminf(__fmul_rn(k, u2f((uint32_t)sb << 23)), Fmt<E, M>::MAX_NORM);
+  const uint32_t e23 = (a & 0x7f800000u) > LO ? (a & 0x7f800000u) : LO;
+  const float k = round_nonneg(__fmul_rn(u2f(a), u2f(((uint32_t)(254 + M) << 23) - e23)), mode);
+  const float val = fminf(__fmul_rn(k, u2f(e23 - ((uint32_t)M << 23))), Fmt<E, M>::MAX_NORM);
   const float r = u2f(f2u(val) | (u & 0x80000000u));
   return a == 0u ? 0.0f : r;
 }
@@ -110,19 +117,19 @@ __device__ __forceinline__ float divide(float v, float x, float r) {
   return FAM == MXQ_FAMILY_MXQUANT ? x86_div(v, x) : div_rn(v, x);
 }
 
-// (2) for a clean tile: every thread quantizes 8 float4 (float4 q = tid + 256 i: row q / 64, float4 column q % 64)
+// (2) for a clean tile: every thread quantizes TR / RPI float4 (float4 q = tid + NT i: row q / C4, column q % C4)
 template <int FAM, int E, int M, bool COLS, int MODE>
 __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, float* __restrict__ P, int64_t rest,
                                            int64_t ct, int64_t nb, int64_t outer, int64_t len, int64_t inner) {
-  const int tid = threadIdx.x, c4 = tid & 63;
+  const int tid = threadIdx.x, c4 = tid % C4;
   float4 rs;
   if (COLS) rs = *reinterpret_cast<const float4*>(s_r + c4 * 4);
 #pragma unroll 2
-  for (int i = 0; i < 8; i++) {
-    const int row = (tid >> 6) + 4 * i;
+  for (int i = 0; i < TR / RPI; i++) {
+    const int row = tid / C4 + RPI * i;
     float4 v = reinterpret_cast<const float4*>(T + row * TC)[c4];
     if (!COLS) {
-      const float r = s_r[row * 8 + (c4 >> 3)];
+      const float r = s_r[row * BPR + (c4 >> 3)];
       rs = make_float4(r, r, r, r);
     }
     v.x = element_clean<FAM, E, M, MODE>(__fmul_rn(v.x, rs.x));
@@ -145,7 +152,7 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
                                                   TParams prm) {
   extern __shared__ __align__(128) float tiles[];            // [STAGES][TR][TC]
   __shared__ __align__(8) uint64_t bars[STAGES];
-  __shared__ float s_x[NT], s_r[NT];
+  __shared__ float s_x[TC], s_r[TC];
 
   const int tid = threadIdx.x;
   // tile grid: ROWS -> (row tiles, column tiles) of the [outer, len] matrix; COLS -> (outer, blocks, column tiles)
@@ -179,9 +186,10 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     const float* T = tiles + stage * TR * TC;
     const int64_t ct = tile % ctiles, rest = tile / ctiles;
 
-    // (1) block scales
-    bool bad;
-    if (COLS) {
+    // (1) block scales: one thread per block of the tile (TC of them)
+    bool bad = false;
+    if (tid >= TC) {
+    } else if (COLS) {
       const int64_t b = rest % nb, o = rest / nb, col = ct * TC + tid;
       uint32_t mbits = 0u;                                  // max |v| as bits: a NaN pattern tops every number
 #pragma unroll 8
@@ -194,7 +202,7 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
       bad = col < inner && (mbits >= 0x7f800000u || r == 0.0f);     // padding columns do not vote
       if (col < inner) X[(o * nb + b) * inner + col] = x;
     } else {
-      const int row = tid >> 3, blk = tid & 7;                // 32 rows x 8 blocks
+      const int row = tid / BPR, blk = tid % BPR;            // TR rows x BPR blocks
       const float4* src = reinterpret_cast<const float4*>(T + row * TC + blk * 32);
       uint32_t mbits = 0u;                                  // max |v| as bits: a NaN pattern tops every number
 #pragma unroll
@@ -226,19 +234,19 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
       continue;
     }
 
-    // (2) elements: float4 q = tid + 256 i of the tile (row q / 64, float4 column q % 64)
-    const int c4 = tid & 63;
+    // (2) elements: float4 q = tid + NT i of the tile (row q / C4, float4 column q % C4)
+    const int c4 = tid % C4;
     float4 xs, rs;
     if (COLS) {
       xs = *reinterpret_cast<const float4*>(s_x + c4 * 4);
       rs = *reinterpret_cast<const float4*>(s_r + c4 * 4);
     }
 #pragma unroll 2
-    for (int i = 0; i < 8; i++) {
-      const int row = (tid >> 6) + 4 * i;
+    for (int i = 0; i < TR / RPI; i++) {
+      const int row = tid / C4 + RPI * i;
       float4 v = reinterpret_cast<const float4*>(T + row * TC)[c4];
       if (!COLS) {
-        const int b = row * 8 + (c4 >> 3);
+        const int b = row * BPR + (c4 >> 3);
         const float x = s_x[b], r = s_r[b];
         xs = make_float4(x, x, x, x);
         rs = make_float4(r, r, r, r);
@@ -260,6 +268,28 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
   }
 }
 
+// CTAs per SM of one kernel on the current device, with its shared-memory attribute set: done once per kernel and
+// device (the attribute is per device), then read from the cache.
+template <int FAM, int E, int M, bool COLS>
+int ctas_per_sm(size_t smem) {
+  static std::atomic<int> cache[kMaxDevices];
+  int dev = 0;
+  if (int r = check_cuda(cudaGetDevice(&dev), "block_quantize: current device")) return -r;
+  if (dev < 0 || dev >= kMaxDevices) return -set_error(MXQ_ERR_UNSUPPORTED, "block_quantize: device %d", dev);
+  int per_sm = cache[dev].load(std::memory_order_relaxed);
+  if (per_sm > 0) return per_sm;
+  auto kern = k_quant_tma<FAM, E, M, COLS>;
+  if (int r = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                         "block_quantize: shared memory attribute"))
+    return -r;
+  if (int r = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT, smem),
+                         "block_quantize: occupancy"))
+    return -r;
+  if (per_sm < 1) per_sm = 1;
+  cache[dev].store(per_sm, std::memory_order_relaxed);
+  return per_sm;
+}
+
 template <int FAM, int E, int M>
 int launch(const CUtensorMap& map, bool cols, float* P, float* X, int64_t outer, int64_t len, int64_t inner,
            const TParams& prm, cudaStream_t st) {
@@ -267,12 +297,8 @@ int launch(const CUtensorMap& map, bool cols, float* P, float* X, int64_t outer,
   const int64_t ntiles = cols ? outer * nb * ((inner + TC - 1) / TC) : ((outer + TR - 1) / TR) * ((len + TC - 1) / TC);
   const size_t smem = STAGES * TILE_BYTES;
   auto kern = cols ? k_quant_tma<FAM, E, M, true> : k_quant_tma<FAM, E, M, false>;
-  if (int r = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                         "block_quantize: shared memory attribute"))
-    return r;
-  int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT, smem);
-  if (per_sm < 1) per_sm = 1;
+  const int per_sm = cols ? ctas_per_sm<FAM, E, M, true>(smem) : ctas_per_sm<FAM, E, M, false>(smem);
+  if (per_sm < 0) return -per_sm;
   int64_t grid = (int64_t)sm_count() * per_sm;
   if (grid > ntiles) grid = ntiles;
   kern<<<(unsigned)grid, NT, smem, st>>>(map, P, X, outer, len, inner, prm);
