@@ -249,31 +249,104 @@ def run_gpu(args):
     gms = max_over_ranks(g0.elapsed_time(g1)) / gsteps
     gmacs = GEMM ** 3 * world / (gms * 1e-3) / 1e9
 
-    # -- config 3's other reducers on the same quantized operands (reducer kernel only, CUDA events)
-    P_A, X_A = block.mxgemmini.quantize(A, "MXFP8_E4M3", axis=0)
-    P_B, X_B = block.mxgemmini.quantize(B, "MXFP8_E4M3", axis=0)
-    reducers = {
-        "systolic MXGEMMINI/HW_FINAL": lambda: matmul.systolic(P_A, X_A, P_B, X_B, arith, schedule.HW_FINAL),
-        "systolic MXQUANT(4,3)/HW_FINAL": lambda: matmul.systolic(P_A, X_A, P_B, X_B, matmul.MXQUANT(4, 3),
-                                                                  schedule.HW_FINAL),
-        "adder_tree MXGEMMINI [(4,4),(4,5),(4,6),(8,7)]": lambda: matmul.adder_tree(
-            P_A, X_A, P_B, X_B, arith, [(4, 4), (4, 5), (4, 6), (8, 7)]),
-        "anchor_tree MXGEMMINI (defaults)": lambda: matmul.anchor_tree(P_A, X_A, P_B, X_B, arith),
-    }
-    red_out = {}
-    for name, fn in reducers.items():
-        if args.reducer_steps <= 0:
-            break
+    # -- config 3's reducers on both operand formats (reducer kernel alone, CUDA events)
+    def timed(fn, steps):
         fn()
         barrier()
-        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        r0.record(stream)
-        for _ in range(args.reducer_steps):
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(steps):
             fn()
-        r1.record(stream)
+        t1.record(stream)
         barrier()
-        rms = max_over_ranks(r0.elapsed_time(r1)) / args.reducer_steps
-        red_out[name] = {"GMAC/s": round(GEMM ** 3 * world / (rms * 1e-3) / 1e9, 1), "ms": round(rms, 3)}
+        return max_over_ranks(t0.elapsed_time(t1)) / steps
+
+    red_out = {}
+    for fmt in ("MXFP8_E4M3", "MXFP6_E2M3") if args.reducer_steps > 0 else ():
+        P_A, X_A = block.mxgemmini.quantize(A, fmt, axis=0)
+        P_B, X_B = block.mxgemmini.quantize(B, fmt, axis=0)
+        reducers = {
+            "systolic MXGEMMINI/HW_FINAL": lambda: matmul.systolic(P_A, X_A, P_B, X_B, arith, schedule.HW_FINAL),
+            "systolic MXQUANT(4,3)/HW_FINAL": lambda: matmul.systolic(P_A, X_A, P_B, X_B, matmul.MXQUANT(4, 3),
+                                                                      schedule.HW_FINAL),
+            "adder_tree MXGEMMINI [(4,4),(4,5),(4,6),(8,7)]": lambda: matmul.adder_tree(
+                P_A, X_A, P_B, X_B, arith, [(4, 4), (4, 5), (4, 6), (8, 7)]),
+            "anchor_tree MXGEMMINI (defaults)": lambda: matmul.anchor_tree(P_A, X_A, P_B, X_B, arith),
+        }
+        for name, fn in reducers.items():
+            rms = timed(fn, args.reducer_steps)
+            red_out[f"{fmt} {name}"] = {"GMAC/s": round(GEMM ** 3 * world / (rms * 1e-3) / 1e9, 1),
+                                        "ms": round(rms, 3)}
+        del P_A, X_A, P_B, X_B
+
+    # -- config 1: the PR1 systolic GEMM (quantize x^T and W^T, systolic), 256 x 512 x 512
+    extra = {}
+    if args.extra_steps > 0:
+        x = torch.randn(256, 512, generator=torch.Generator(device=dev).manual_seed(11), device=dev)
+        W = torch.randn(512, 512, generator=torch.Generator(device=dev).manual_seed(12), device=dev)
+
+        def pr1():
+            PA1, XA1 = block.mxgemmini.quantize(x.t().contiguous(), "MXFP8_E4M3", axis=0)
+            PB1, XB1 = block.mxgemmini.quantize(W.t().contiguous(), "MXFP8_E4M3", axis=0)
+            return matmul.systolic(PA1, XA1, PB1, XB1, arith, schedule.HW_FINAL)
+
+        ms1 = timed(pr1, 20 * args.extra_steps)
+        extra["config 1: PR1 systolic 256x512x512 (quantize x^T, W^T + systolic)"] = {
+            "GMAC/s": round(256 * 512 * 512 * world / (ms1 * 1e-3) / 1e9, 1), "us": round(ms1 * 1e3, 1)}
+
+        # -- config 4: the LUT path on a 4096 x 4096 operand, column j ~ N(0, sigma_j^2), sigma_j = 2^U[-8, 8]
+        from mxq import lut
+        g4 = torch.Generator(device=dev).manual_seed(13 + rank)
+        V4 = torch.randn(4096, 4096, generator=g4, device=dev) * torch.exp2(
+            torch.rand(1, 4096, generator=g4, device=dev) * 16 - 8)
+        n4 = V4.numel()
+        for fmt in ("MXFP6_E3M2", "MXFP8_E4M3"):
+            for G in (1, 3):
+                ms4 = timed(lambda: block.lut.quantize(V4, fmt, 0, 32, rounding_mode="rne", scale_floor=2.0 ** -23,
+                                                       group=G, max_iters=50), args.extra_steps)
+                extra[f"config 4: block.lut {fmt} G={G}"] = {
+                    "GB/s": round(BYTES_PER_ELEM * n4 * world / (ms4 * 1e-3) / 1e9, 1), "ms": round(ms4, 3)}
+        P4 = block.mxgemmini.quantize(V4, "MXFP6_E3M2", 0, 32, rounding_mode="rne", scale_floor=2.0 ** -23)[0]
+        T4 = lut.tables(P4, "MXFP6_E3M2", group=1, max_iters=50)
+        C4 = lut.encode(P4, "MXFP6_E3M2")
+        for name, fn, bpe in (("lut.tables", lambda: lut.tables(P4, "MXFP6_E3M2", group=1, max_iters=50), 4),
+                              ("lut.pick", lambda: lut.pick(P4, T4, group=1), 12),
+                              ("lut.finder", lambda: lut.finder(C4, T4, "MXFP6_E3M2", group=1), 16)):
+            ms4 = timed(fn, args.extra_steps)
+            extra[f"config 4: {name} MXFP6_E3M2 G=1"] = {
+                "GB/s": round(bpe * n4 * world / (ms4 * 1e-3) / 1e9, 1), "ms": round(ms4, 3)}
+        del V4, P4, T4, C4
+
+    # -- config 5: the MXLinear-patched Llama decoder (random init, std 0.02), 8 x 1024 tokens per GPU, one forward
+    model_out = None
+    if args.model_steps > 0:
+        from functools import partial
+        from transformers import LlamaConfig, LlamaForCausalLM
+        from mxq import Scheme
+        from mxq.nn import patch
+        cfg = LlamaConfig(hidden_size=2048, intermediate_size=5632, num_hidden_layers=16, num_attention_heads=16,
+                          num_key_value_heads=16, head_dim=128, vocab_size=32000, max_position_embeddings=1024,
+                          initializer_range=0.02)
+        torch.manual_seed(0)
+        with torch.device(dev):
+            model = LlamaForCausalLM(cfg).float().eval()
+        q8 = partial(block.mxgemmini.quantize, fmt="MXFP8_E4M3", axis=0)
+        sch = Scheme("hw_fp8", a=q8, b=q8, reduce=partial(matmul.systolic, arith=arith, schedule=schedule.HW_FINAL))
+        handle = patch(model, [("lm_head", None), ("model.layers.*.self_attn", (sch, sch)), (torch.nn.Linear, sch)])
+        ids = torch.randint(0, 32000, (8, 1024), generator=torch.Generator(device=dev).manual_seed(14 + rank),
+                            device=dev)
+        with torch.no_grad():
+            msm = timed(lambda: model(ids).logits, args.model_steps)
+        macs = 8 * 1024 * 16 * (4 * 2048 * 2048 + 3 * 2048 * 5632) + 8 * 16 * 16 * 2 * 1024 * 1024 * 128
+        model_out = {"workload": "config 5: MXLinear-patched Llama (16 layers, hidden 2048, 16 heads x 128, FFN 5632, "
+                                 "vocab 32000), batch 8 x 1024 tokens per GPU, one forward, every Linear but lm_head "
+                                 "and the attention core through mxgemmini MXFP8_E4M3 + systolic MXGEMMINI/HW_FINAL",
+                     "tokens/s": round(8 * 1024 * world / (msm * 1e-3), 1),
+                     "emulated GMAC/s": round(macs * world / (msm * 1e-3) / 1e9, 1), "s_per_forward": round(msm / 1e3, 3),
+                     "steps": args.model_steps}
+        handle.revert()
+        del model, handle, ids
+        torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -305,8 +378,12 @@ def run_gpu(args):
                      "workload": f"config 3: quantize A, B ({GEMM}x{GEMM} MXFP8_E4M3, block.mxgemmini) + "
                                  f"systolic MXGEMMINI/HW_FINAL {GEMM}^3 per GPU", "ms_per_gemm": round(gms, 3),
                      "steps": gsteps},
-        "reducers": {"workload": f"config 3: {GEMM}^3 per GPU on MXFP8_E4M3 codes, reducer kernel alone",
+        "reducers": {"workload": f"config 3: {GEMM}^3 per GPU on MXFP8_E4M3 and MXFP6_E2M3 codes, reducer alone",
                      "steps": args.reducer_steps, **red_out},
+        "configs_1_4": {"workload": "config 1 (PR1 GEMM, whole call) and config 4 (LUT path, 4096 x 4096 per GPU); "
+                                    "GB/s counts 8.125 B/element for block.lut, 4 tables, 12 pick, 16 finder",
+                        "steps": args.extra_steps, **extra},
+        "model": model_out,
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
@@ -374,7 +451,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mxq_b200", choices=["mxq_b200", "reference"])
     ap.add_argument("--gemm-steps", type=int, default=3)
-    ap.add_argument("--reducer-steps", type=int, default=1, help="timed runs of each other config-3 reducer (0: skip)")
+    ap.add_argument("--reducer-steps", type=int, default=1, help="timed runs of each config-3 reducer (0: skip)")
+    ap.add_argument("--extra-steps", type=int, default=3, help="timed runs of configs 1 and 4 (0: skip)")
+    ap.add_argument("--model-steps", type=int, default=1, help="timed forwards of the config-5 model (0: skip)")
     ap.add_argument("--cpu-rows", type=int, default=ROWS, help="rows of the CPU-baseline matrix")
     ap.add_argument("--cpu-repeats", type=int, default=2, help="sweeps of the CPU-baseline matrix")
     ap.add_argument("--ref-rows", type=int, default=256, help="rows per reference-arm step")
