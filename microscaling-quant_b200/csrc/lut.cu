@@ -5,12 +5,10 @@
 // Layout: an operand is addressed as element (k, j) = P[k * sk + j * sj], so the row-major K x n operand (sk = n,
 // sj = 1) and the transposed one of an axis-1 quantization (sk = 1, sj = K) are read in place.
 //
-// tables: one CTA per panel of column groups (32 columns, or one whole group when 2^G >= 32). The CTA histograms its
-// panel's codes by grid rank in shared memory, then one warp per group fits the table (kmeans.py:46-122): the group's
-// distinct codes when there are at most 16; otherwise quantile seeds and weighted Lloyd passes in float64 until two
-// passes agree to numpy.allclose or max_iters have run; every centre snapped to the nearest finder-safe value; the
-// table padded with unused values of smallest magnitude and sorted. Every sum is exact (codes times counts), so the
-// order of the shared-memory atomics does not change a bit.
+// tables: one CTA per panel of column groups (at most 32 columns, sized so the grid covers every SM about twice). The
+// CTA histograms its panel's codes by grid rank in shared memory, then one warp per group fits the table
+// (kmeans.py:46-122) with the work spread over its lanes (k_lut_tables). Every sum is exact (codes times counts), so
+// no summation order changes a bit.
 #include <algorithm>
 #include <mutex>
 #include <vector>
@@ -65,7 +63,7 @@ int64_t fx_mask(int e, int m) {                 // formats.py:72-73; 0: E2M3's f
 }
 
 struct FormatTables {
-  int e = 0, m = 0, ncodes = 0, nv = 0, nsafe = 0;
+  int e = 0, m = 0, ncodes = 0, nv = 0, nsafe = 0, nmag = 0;
   float vals[MAXV];            // value of every code (E5M2's top exponent: Inf / NaN)
   int64_t fx[MAXV];            // finder fixed point of every code
   float grid[MAXV];            // sorted distinct finite values
@@ -130,6 +128,11 @@ const FormatTables* format_tables(int e, int m) {
   std::sort(grid.begin(), grid.end());
   t.nv = (int)grid.size();
   for (int i = 0; i < t.nv; i++) t.grid[i] = grid[i];
+  // the kernel ranks a value by its magnitude code: the grid must be -mag[nmag-1] .. 0 .. mag[nmag-1] with mag[k] the
+  // value of code k (true of all four formats; checked here once)
+  t.nmag = (t.nv + 1) / 2;
+  for (int k = 0; k < t.nmag; k++)
+    if (t.grid[t.nmag - 1 + k] != t.vals[k] || t.grid[t.nmag - 1 - k] != -t.vals[k]) t.nmag = -1;
   // encode: value bits -> lowest code (formats.py:125-137, `lookup.setdefault(bits, c)`)
   std::vector<std::pair<uint32_t, int>> enc;
   for (int c = 0; c < t.ncodes; c++) {
@@ -151,60 +154,78 @@ const FormatTables* format_tables(int e, int m) {
 // ------------------------------------------------------------------------------------------- device side
 struct TableParams {                           // by value: what the tables kernel needs of a format
   int nv, nsafe;
+  int nmag, bias, m;                           // grid = -mag[nmag-1] .. -mag[1], 0, mag[1] .. mag[nmag-1]
   float grid[MAXV];
   float safe[MAXV];
   uint8_t order[MAXV];
 };
 
-__device__ __forceinline__ int lower_bound_f(const float* a, int n, float v) {
-  int lo = 0, hi = n;
-  while (lo < hi) {
-    int mid = (lo + hi) >> 1;
-    if (a[mid] < v) lo = mid + 1;
-    else hi = mid;
+constexpr int NW = NT / 32;                    // warps per CTA
+constexpr double MIN_GAP = 1.16415321826934814453125e-10;   // 2^-33: centres this far apart never tie by rounding
+
+// The grid rank of a value: its magnitude code from the float's bits (sign-magnitude formats whose finite
+// magnitudes increase with the code), clamped into [0, nv); the caller checks grid[rank] == v.
+__device__ __forceinline__ int grid_rank(float v, const TableParams& tp) {
+  const uint32_t u = f2u(v), a = u & 0x7fffffffu;
+  const int E = (int)(a >> 23) - 127;
+  int k;
+  if (E >= 1 - tp.bias) {
+    k = ((E + tp.bias) << tp.m) | (int)((a >> (23 - tp.m)) & ((1u << tp.m) - 1u));
+  } else {                                     // below the format's normal range: a multiple of its subnormal step
+    const int sh = 24 - tp.bias - tp.m - E;
+    k = (int)(((a & 0x007fffffu) | 0x00800000u) >> (sh < 31 ? sh : 31));
   }
-  return lo;
+  int r = (tp.nmag - 1) + ((u >> 31) ? -k : k);
+  return r < 0 ? 0 : (r >= tp.nv ? tp.nv - 1 : r);
 }
 
-// sort 16 doubles ascending (inf last), equal values merged into +inf, sorted again (_dedupe, kmeans.py:38-43)
-__device__ void dedupe16(double* c) {
-  for (int i = 1; i < LUT; i++) {
-    double v = c[i];
-    int j = i - 1;
-    while (j >= 0 && c[j] > v) {
-      c[j + 1] = c[j];
-      j--;
+// _dedupe (kmeans.py:38-43) across lanes 0-15 of a warp, lane t holding v_t: sort ascending (by rank, ties in lane
+// order), equal neighbours turned into +inf, sort again. `scratch` holds 16 doubles of this warp.
+__device__ __forceinline__ double dedupe_lanes(double v, double* scratch) {
+  const int lane = threadIdx.x & 31;
+  for (int pass = 0; pass < 2; pass++) {
+    int rank = 0;
+#pragma unroll
+    for (int s = 0; s < LUT; s++) {
+      const double o = __shfl_sync(0xffffffffu, v, s);
+      rank += (o < v) || (o == v && s < lane);
     }
-    c[j + 1] = v;
-  }
-  bool dup[LUT];
-  dup[0] = false;
-  for (int i = 1; i < LUT; i++) dup[i] = c[i] == c[i - 1];
-  for (int i = 1; i < LUT; i++)
-    if (dup[i]) c[i] = INFINITY;
-  for (int i = 1; i < LUT; i++) {
-    double v = c[i];
-    int j = i - 1;
-    while (j >= 0 && c[j] > v) {
-      c[j + 1] = c[j];
-      j--;
+    if (lane < LUT) scratch[rank] = v;
+    __syncwarp();
+    if (lane < LUT) v = scratch[lane];
+    __syncwarp();
+    if (pass == 0) {
+      const double prev = __shfl_up_sync(0xffffffffu, v, 1);
+      if (lane > 0 && lane < LUT && v == prev) v = INFINITY;
     }
-    c[j + 1] = v;
   }
+  return v;
 }
 
-// groups per CTA for a given G: a 32-column panel, or one group when it is wider
-__host__ __device__ __forceinline__ int groups_per_cta(int G) { return G >= 5 ? 1 : (32 >> G); }
-
+// The tables (kmeans.py:46-122). A CTA per panel of gpc column groups: (1) the panel's codes histogrammed by grid
+// rank in shared memory; then one warp per group: (2) prefix sums of counts and of counts x values over the sorted
+// codes (exact in float64: integers times grid values); the centres -- the present codes when there are at most 16,
+// else the quantile seeds, deduplicated, and weighted Lloyd passes until two passes agree to numpy.allclose or
+// max_iters have run; (3) each centre snapped to the nearest finder-safe value; (4) padded and sorted.
+//
+// A Lloyd pass in lanes: lane t holds centre t. Codes and centres are sorted and rounding is monotone, so every
+// centre takes a run of consecutive codes; lane t finds where its run ends -- the first code closer (rounded
+// float64 distance, ties to the lower centre, as argmin) to centre t + 1 -- by binary search, and its sum and weight
+// are differences of the prefix sums. That equals the reference's argmin over all 16 centres whenever consecutive
+// centres are at least 2^-33 apart (distances below 2^17 then never round to a tie across a centre); a pass that
+// finds two closer centres assigns code by code instead.
 __global__ void __launch_bounds__(NT) k_lut_tables(const float* __restrict__ P, int64_t K, int64_t n, int64_t sk,
-                                                   int64_t sj, int G, int max_iters, const __grid_constant__ TableParams tp,
-                                                   float* __restrict__ T, int* __restrict__ status) {
-  extern __shared__ int counts[];                           // [groups_per_cta][nv]
-  __shared__ double cent[NT / 32][LUT], sums[NT / 32][LUT], wsum[NT / 32][LUT], cdf[NT / 32][MAXV];
+                                                   int64_t sj, int G, int gpc, int max_iters,
+                                                   const __grid_constant__ TableParams tp, float* __restrict__ T,
+                                                   int* __restrict__ status) {
+  extern __shared__ int counts[];                           // [gpc][nv]
+  __shared__ double pw[NW][MAXV + 1], pwx[NW][MAXV + 1];     // prefix: counts, counts x values
+  __shared__ double scratch[NW][LUT], fsum[NW][LUT], fw[NW][LUT];
   __shared__ float sgrid[MAXV];
+  __shared__ unsigned char member[NW][MAXV];
   __shared__ int bad;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nv = tp.nv;
-  const int gpc = groups_per_cta(G);
+  const unsigned lt = (1u << lane) - 1u;
   const int64_t ng = (n + ((int64_t)1 << G) - 1) >> G;
   const int64_t g0 = (int64_t)blockIdx.x * gpc;
   const int64_t j0 = g0 << G, jend = (g0 + gpc) << G, j1 = jend < n ? jend : n;
@@ -214,15 +235,15 @@ __global__ void __launch_bounds__(NT) k_lut_tables(const float* __restrict__ P, 
   if (tid == 0) bad = 0;
   __syncthreads();
 
-  // 1. counts of each distinct code per group (kmeans.py:58-64); iterate so consecutive threads read consecutive memory
+  // 1. counts of each distinct code per group (kmeans.py:58-64); consecutive threads read consecutive memory
   const int64_t total = K * W;
   const bool kfast = sk == 1;
   bool mybad = false;
   for (int64_t e = tid; e < total; e += NT) {
-    int64_t k = kfast ? e % K : e / W, jj = kfast ? e / K : e % W;
-    float v = P[k * sk + (j0 + jj) * sj];
-    int b = lower_bound_f(sgrid, nv, v);
-    if (b >= nv || sgrid[b] != v) {
+    const int64_t k = kfast ? e % K : e / W, jj = kfast ? e / K : e % W;
+    const float v = P[k * sk + (j0 + jj) * sj];
+    const int b = grid_rank(v, tp);
+    if (sgrid[b] != v) {                                    // also every NaN
       mybad = true;
       continue;
     }
@@ -235,140 +256,178 @@ __global__ void __launch_bounds__(NT) k_lut_tables(const float* __restrict__ P, 
     return;
   }
 
-  // 2-4. one warp per group
-  for (int gl = warp; gl < gpc; gl += NT / 32) {
+  for (int gl = warp; gl < gpc; gl += NW) {
     const int64_t g = g0 + gl;
     if (g >= ng) break;
     const int* cnt = counts + gl * nv;
-    double* C = cent[warp];
-    // distinct codes present
+    double* PW = pw[warp];
+    double* PWX = pwx[warp];
+    // 2. prefix sums over the sorted codes, and the number of distinct codes present
+    double runw = 0.0, runx = 0.0;
     int npres = 0;
-    for (int b = lane; b < nv; b += 32) npres += cnt[b] > 0;
+    for (int b0 = 0; b0 < nv; b0 += 32) {
+      const int b = b0 + lane;
+      const int cb = b < nv ? cnt[b] : 0;
+      double w = (double)cb, wx = b < nv ? __dmul_rn((double)cb, (double)sgrid[b]) : 0.0;
+      npres += cb > 0;
+#pragma unroll
+      for (int s = 1; s < 32; s <<= 1) {                     // inclusive scans (exact sums)
+        const double ow = __shfl_up_sync(0xffffffffu, w, s), ox = __shfl_up_sync(0xffffffffu, wx, s);
+        if (lane >= s) {
+          w = __dadd_rn(w, ow);
+          wx = __dadd_rn(wx, ox);
+        }
+      }
+      if (b < nv) {
+        PW[b + 1] = __dadd_rn(runw, w);
+        PWX[b + 1] = __dadd_rn(runx, wx);
+      }
+      runw = __dadd_rn(runw, __shfl_sync(0xffffffffu, w, 31));
+      runx = __dadd_rn(runx, __shfl_sync(0xffffffffu, wx, 31));
+    }
+    if (lane == 0) {
+      PW[0] = 0.0;
+      PWX[0] = 0.0;
+    }
+#pragma unroll
     for (int s = 16; s > 0; s >>= 1) npres += __shfl_xor_sync(0xffffffffu, npres, s);
-    if (lane < LUT) C[lane] = INFINITY;
     __syncwarp();
-    if (npres <= LUT) {                                    // 2a: they are the centres, ascending
+
+    double c = INFINITY;                                     // lane t < 16: centre t
+    if (npres <= LUT) {                                      // 2a: the present codes are the centres, ascending
       int base = 0;
       for (int b0 = 0; b0 < nv; b0 += 32) {
-        int b = b0 + lane;
-        bool p = b < nv && cnt[b] > 0;
-        unsigned mask = __ballot_sync(0xffffffffu, p);
-        if (p) C[base + __popc(mask & ((1u << lane) - 1u))] = (double)sgrid[b];
+        const int b = b0 + lane;
+        const bool pr = b < nv && cnt[b] > 0;
+        const unsigned mask = __ballot_sync(0xffffffffu, pr);
+        if (pr) scratch[warp][base + __popc(mask & lt)] = (double)sgrid[b];
         base += __popc(mask);
       }
       __syncwarp();
-    } else {
-      // 2b: quantile seeds: the first code whose cumulative weight reaches (i + 0.5) / 16
-      long long run = 0;
-      long long tot = 0;
-      for (int b = lane; b < nv; b += 32) tot += cnt[b];
-      for (int s = 16; s > 0; s >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, s);
-      for (int b0 = 0; b0 < nv; b0 += 32) {
-        int b = b0 + lane;
-        long long c = b < nv ? cnt[b] : 0;
-        for (int s = 1; s < 32; s <<= 1) {                 // inclusive scan
-          long long o = __shfl_up_sync(0xffffffffu, c, s);
-          if (lane >= s) c += o;
-        }
-        if (b < nv) cdf[warp][b] = __ddiv_rn((double)(run + c), (double)tot);
-        run += __shfl_sync(0xffffffffu, c, 31);
-      }
+      if (lane < npres) c = scratch[warp][lane];
       __syncwarp();
+    } else {
+      // 2b: quantile seeds: the first code whose cumulative weight share reaches (t + 0.5) / 16
+      const double tot = PW[nv];
       if (lane < LUT) {
-        double probe = __ddiv_rn((double)lane + 0.5, (double)LUT);
+        const double probe = __ddiv_rn((double)lane + 0.5, (double)LUT);
         int lo = 0, hi = nv;
         while (lo < hi) {
-          int mid = (lo + hi) >> 1;
-          if (cdf[warp][mid] < probe) lo = mid + 1;
+          const int mid = (lo + hi) >> 1;
+          if (__ddiv_rn(PW[mid + 1], tot) < probe) lo = mid + 1;
           else hi = mid;
         }
-        if (lo > nv - 1) lo = nv - 1;
-        C[lane] = (double)sgrid[lo];
+        c = (double)sgrid[lo < nv - 1 ? lo : nv - 1];
       }
-      __syncwarp();
-      if (lane == 0) dedupe16(C);
-      __syncwarp();
-      // 2c: weighted Lloyd passes over the distinct codes
+      c = dedupe_lanes(c, scratch[warp]);
+      // 2c: weighted Lloyd passes
       for (int it = 0; it < max_iters; it++) {
-        if (lane < LUT) {
-          sums[warp][lane] = 0.0;
-          wsum[warp][lane] = 0.0;
-        }
-        __syncwarp();
-        double c[LUT];
-#pragma unroll
-        for (int t = 0; t < LUT; t++) c[t] = C[t];
-        for (int b = lane; b < nv; b += 32) {
-          if (cnt[b] == 0) continue;                       // a zero weight adds nothing to any sum
-          double x = (double)sgrid[b];
-          int best = 0;
-          double bd = fabs(__dsub_rn(x, c[0]));
-#pragma unroll
-          for (int t = 1; t < LUT; t++) {
-            double d = fabs(__dsub_rn(x, c[t]));
-            if (d < bd) {
-              bd = d;
-              best = t;
+        const double cn = __shfl_down_sync(0xffffffffu, c, 1);          // centre t + 1
+        const bool close = lane < LUT - 1 && finite_d(cn) && __dsub_rn(cn, c) < MIN_GAP;
+        double nw;
+        if (!__any_sync(0xffffffffu, close)) {
+          int end = nv;                                                  // first code past centre t's run
+          if (lane < LUT - 1 && finite_d(cn)) {
+            int lo = 0, hi = nv;
+            while (lo < hi) {
+              const int mid = (lo + hi) >> 1;
+              const double x = (double)sgrid[mid];
+              if (fabs(__dsub_rn(x, cn)) < fabs(__dsub_rn(x, c))) hi = mid;
+              else lo = mid + 1;
             }
+            end = lo;
           }
-          double w = (double)cnt[b];
-          atomicAdd(&sums[warp][best], __dmul_rn(w, x));
-          atomicAdd(&wsum[warp][best], w);
-        }
-        __syncwarp();
-        int same = 1;
-        if (lane == 0) {
-          double nw[LUT];
-          for (int t = 0; t < LUT; t++) nw[t] = wsum[warp][t] > 0.0 ? __ddiv_rn(sums[warp][t], wsum[warp][t]) : c[t];
-          dedupe16(nw);
-          for (int t = 0; t < LUT; t++) {
-            bool valid = finite_d(c[t]);
-            if (finite_d(nw[t]) != valid) same = 0;
-            if (valid && !(fabs(__dsub_rn(nw[t], c[t])) <= __dadd_rn(1e-8, __dmul_rn(1e-5, fabs(c[t]))))) same = 0;
+          int begin = __shfl_up_sync(0xffffffffu, end, 1);
+          if (lane == 0) begin = 0;
+          double ws = 0.0, sm = 0.0;
+          if (lane < LUT && begin < end) {
+            ws = __dsub_rn(PW[end], PW[begin]);
+            sm = __dsub_rn(PWX[end], PWX[begin]);
           }
-          if (!same)
-            for (int t = 0; t < LUT; t++) C[t] = nw[t];
+          nw = ws > 0.0 ? __ddiv_rn(sm, ws) : c;
+        } else {                                                         // code by code, as the reference's argmin
+          if (lane < LUT) {
+            fsum[warp][lane] = 0.0;
+            fw[warp][lane] = 0.0;
+          }
+          double cc[LUT];
+#pragma unroll
+          for (int t = 0; t < LUT; t++) cc[t] = __shfl_sync(0xffffffffu, c, t);
+          __syncwarp();
+          for (int b = lane; b < nv; b += 32) {
+            if (cnt[b] == 0) continue;
+            const double x = (double)sgrid[b];
+            int best = 0;
+            double bd = fabs(__dsub_rn(x, cc[0]));
+#pragma unroll
+            for (int t = 1; t < LUT; t++) {
+              const double d = fabs(__dsub_rn(x, cc[t]));
+              if (d < bd) {
+                bd = d;
+                best = t;
+              }
+            }
+            atomicAdd(&fsum[warp][best], __dmul_rn((double)cnt[b], x));
+            atomicAdd(&fw[warp][best], (double)cnt[b]);
+          }
+          __syncwarp();
+          const double ws = lane < LUT ? fw[warp][lane] : 0.0, sm = lane < LUT ? fsum[warp][lane] : 0.0;
+          nw = ws > 0.0 ? __ddiv_rn(sm, ws) : c;
+          __syncwarp();
         }
-        same = __shfl_sync(0xffffffffu, same, 0);
-        __syncwarp();
-        if (same) break;
+        nw = dedupe_lanes(lane < LUT ? nw : INFINITY, scratch[warp]);
+        const bool valid = finite_d(c);
+        const bool ok = lane >= LUT || (finite_d(nw) == valid &&
+                                        (!valid || fabs(__dsub_rn(nw, c)) <= __dadd_rn(1e-8, __dmul_rn(1e-5, fabs(c)))));
+        if (__all_sync(0xffffffffu, ok)) break;                          // converged: keep the current centres
+        c = nw;
       }
     }
-    // 3. each centre snapped to the nearest finder-safe value, ties to the smaller; 4. pad and sort
-    __shared__ unsigned char member[NT / 32][MAXV];
+    // 3. each centre snapped to the nearest finder-safe value (safe is sorted: the nearest is a neighbour of the
+    // insertion point), ties to the smaller
     for (int i = lane; i < tp.nsafe; i += 32) member[warp][i] = 0;
     __syncwarp();
-    if (lane < LUT) {
-      double cc = C[lane];
-      if (finite_d(cc)) {
-        int best = 0;
-        double bd = fabs(__dsub_rn(cc, (double)tp.safe[0]));
-        for (int i = 1; i < tp.nsafe; i++) {
-          double d = fabs(__dsub_rn(cc, (double)tp.safe[i]));
-          if (d < bd) {
-            bd = d;
-            best = i;
-          }
-        }
-        member[warp][best] = 1;
+    if (lane < LUT && finite_d(c)) {
+      int lo = 0, hi = tp.nsafe;
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if ((double)tp.safe[mid] < c) lo = mid + 1;
+        else hi = mid;
       }
+      int best = lo < tp.nsafe ? lo : tp.nsafe - 1;
+      if (lo > 0 && (lo == tp.nsafe || fabs(__dsub_rn(c, (double)tp.safe[lo - 1])) <=
+                                            fabs(__dsub_rn(c, (double)tp.safe[lo]))))
+        best = lo - 1;
+      member[warp][best] = 1;
     }
     __syncwarp();
-    if (lane == 0) {
-      int nmem = 0;
-      for (int i = 0; i < tp.nsafe; i++) nmem += member[warp][i];
-      for (int i = 0; i < tp.nsafe && nmem < LUT; i++) {
-        int s = tp.order[i];
-        if (!member[warp][s]) {
-          member[warp][s] = 1;
-          nmem++;
-        }
-      }
-      int r = 0;
-      for (int i = 0; i < tp.nsafe && r < LUT; i++)
-        if (member[warp][i]) T[g * LUT + r++] = tp.safe[i];
-      for (; r < LUT; r++) T[g * LUT + r] = INFINITY;
+    // 4. pad with unused values, smallest magnitude first, then write the members in ascending order
+    int nmem = 0;
+    for (int i0 = 0; i0 < tp.nsafe; i0 += 32) {
+      const int i = i0 + lane;
+      nmem += __popc(__ballot_sync(0xffffffffu, i < tp.nsafe && member[warp][i]));
     }
+    int need = LUT - nmem;
+    for (int i0 = 0; i0 < tp.nsafe && need > 0; i0 += 32) {
+      const int i = i0 + lane;
+      const int sidx = i < tp.nsafe ? tp.order[i] : 0;
+      const bool fr = i < tp.nsafe && !member[warp][sidx];
+      const unsigned mask = __ballot_sync(0xffffffffu, fr);
+      __syncwarp();
+      if (fr && __popc(mask & lt) < need) member[warp][sidx] = 1;
+      need -= __popc(mask);
+      __syncwarp();
+    }
+    int base = 0;
+    for (int i0 = 0; i0 < tp.nsafe && base < LUT; i0 += 32) {
+      const int i = i0 + lane;
+      const bool mb = i < tp.nsafe && member[warp][i];
+      const unsigned mask = __ballot_sync(0xffffffffu, mb);
+      const int pos = base + __popc(mask & lt);
+      if (mb && pos < LUT) T[g * LUT + pos] = tp.safe[i];
+      base += __popc(mask);
+    }
+    if (lane >= base && lane < LUT) T[g * LUT + lane] = INFINITY;
     __syncwarp();
   }
 }
@@ -531,6 +590,7 @@ int mxq_lut_tables(const float* P, float* T, int64_t K, int64_t n, int64_t sk, i
   MXQ_REQUIRE(max_iters >= 0, MXQ_ERR_VALUE, "mxq.lut: max_iters %d must be a non-negative integer", max_iters);
   MXQ_REQUIRE(status != nullptr, MXQ_ERR_VALUE, "mxq.lut.tables: no status word");
   const FormatTables* f = format_tables(e, m);
+  MXQ_REQUIRE(f->nmag > 0, MXQ_ERR_UNSUPPORTED, "lut.tables: (e=%d, m=%d) has no sign-magnitude grid", e, m);
   cudaStream_t st = as_stream(stream);
   if (int r = check_cuda(cudaMemsetAsync(status, 0, sizeof(int32_t), st), "lut.tables")) return r;
   const int64_t ng = (n + ((int64_t)1 << group) - 1) >> group;
@@ -538,19 +598,26 @@ int mxq_lut_tables(const float* P, float* T, int64_t K, int64_t n, int64_t sk, i
   TableParams tp;
   tp.nv = f->nv;
   tp.nsafe = f->nsafe;
+  tp.nmag = f->nmag;
+  tp.bias = (1 << (e - 1)) - 1;
+  tp.m = m;
   for (int i = 0; i < f->nv; i++) tp.grid[i] = f->grid[i];
   for (int i = 0; i < f->nsafe; i++) {
     tp.safe[i] = f->safe[i];
     tp.order[i] = f->order[i];
   }
-  const int gpc = groups_per_cta(group);
+  // groups per CTA: a panel of at most 32 columns (one group when it is wider), few enough groups that the grid
+  // covers every SM about twice (each group's fit is one warp)
+  const int64_t cap = group >= 5 ? 1 : (32 >> group);
+  int64_t want = (ng + 2 * (int64_t)sm_count() - 1) / (2 * (int64_t)sm_count());
+  const int gpc = (int)(want < 1 ? 1 : (want > cap ? cap : want));
   const size_t smem = (size_t)gpc * f->nv * sizeof(int);
   const unsigned grid = (unsigned)((ng + gpc - 1) / gpc);
-  // static (~22 KB) plus the histograms can pass the 48 KB default
+  // static (~40 KB) plus the histograms can pass the 48 KB default
   if (int r = check_cuda(cudaFuncSetAttribute(k_lut_tables, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                          "lut.tables: shared memory attribute"))
     return r;
-  k_lut_tables<<<grid, NT, smem, st>>>(P, K, n, sk, sj, group, max_iters, tp, T, status);
+  k_lut_tables<<<grid, NT, smem, st>>>(P, K, n, sk, sj, group, gpc, max_iters, tp, T, status);
   return MXQ_LAUNCH_CHECK("lut.tables");
 }
 
