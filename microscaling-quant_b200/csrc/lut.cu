@@ -500,35 +500,37 @@ __global__ void k_lut_decode(const int64_t* __restrict__ codes, float* __restric
                              const __grid_constant__ CodeTables ct, int* __restrict__ status) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     int64_t c = codes[i];
-    if (c < 0 || c >= ct.ncodes) {
-      atomicExch(status, 1);
+    if (c < -ct.ncodes || c >= ct.ncodes) {              // torch indexing: a negative code counts from the end
+      atomicOr(status, 1);
       out[i] = 0.0f;
     } else {
-      out[i] = ct.vals[c];
+      out[i] = ct.vals[c < 0 ? c + ct.ncodes : c];
     }
   }
 }
 
-// finder (formats.py:140-159): fixed points of the code and of the 16 entries, masked |difference|, first minimum
+// finder (formats.py:140-159): fixed points of the code and of the 16 entries, masked |difference|, first minimum.
+// status bits: 1 a code outside [-ncodes, ncodes) (negative codes count from the end, as torch indexes), 2 a table
+// value that is no code; the caller raises for bit 1 first, as the reference indexes the codes first.
 __global__ void k_lut_finder(const int64_t* __restrict__ codes, const float* __restrict__ T, int64_t K, int64_t n,
                              int G, long long mask, const __grid_constant__ CodeTables ct, int64_t* __restrict__ I,
                              int* __restrict__ status) {
   const int64_t total = K * n;
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
     const int64_t j = e % n, c = codes[e];
-    if (c < 0 || c >= ct.ncodes) {
-      atomicExch(status, 1);
+    if (c < -ct.ncodes || c >= ct.ncodes) {
+      atomicOr(status, 1);
       I[e] = 0;
       continue;
     }
-    const long long f = ct.fx[c];
+    const long long f = ct.fx[c < 0 ? c + ct.ncodes : c];
     const float* row = T + (j >> G) * LUT;
     int best = 0;
     long long bd = 0;
     for (int t = 0; t < LUT; t++) {
       int tc = encode1(ct, __ldg(row + t));
       if (tc < 0) {
-        atomicExch(status, 2);
+        atomicOr(status, 2);
         tc = 0;
       }
       long long d = f - ct.fx[tc];
@@ -541,6 +543,105 @@ __global__ void k_lut_finder(const int64_t* __restrict__ codes, const float* __r
     }
     I[e] = best;
   }
+}
+
+// Column forms of pick and finder for a row-major K x n operand with 16-entry tables: thread j walks rows
+// [k0, k1) of column j with its group's table in registers, so the table is read (and, for the finder, encoded)
+// once per column instead of once per element; consecutive threads read consecutive columns.
+constexpr int CT = 256;
+
+__global__ void __launch_bounds__(CT) k_lut_pick_cols(const float* __restrict__ P, const float* __restrict__ T,
+                                                      int64_t K, int64_t n, int G, int64_t rows,
+                                                      int64_t* __restrict__ I, float* __restrict__ out_vals) {
+  const int64_t j = (int64_t)blockIdx.x * CT + threadIdx.x;
+  if (j >= n) return;
+  const int64_t k0 = (int64_t)blockIdx.y * rows, k1 = k0 + rows < K ? k0 + rows : K;
+  float t[LUT];
+  const float4* row = reinterpret_cast<const float4*>(T + (j >> G) * LUT);
+#pragma unroll
+  for (int q = 0; q < LUT / 4; q++) {
+    const float4 v = __ldg(row + q);
+    t[4 * q] = v.x;
+    t[4 * q + 1] = v.y;
+    t[4 * q + 2] = v.z;
+    t[4 * q + 3] = v.w;
+  }
+  for (int64_t k = k0; k < k1; k++) {
+    const float v = P[k * n + j];
+    int cnt = 0;                                            // lower_bound: entries below v
+#pragma unroll
+    for (int i = 0; i < LUT; i++) cnt += t[i] < v;
+    const int lo = cnt < 1 ? 0 : (cnt > LUT - 1 ? LUT - 2 : cnt - 1);
+    float rl = t[0], rh = t[1];
+#pragma unroll
+    for (int i = 1; i < LUT - 1; i++)
+      if (lo == i) {
+        rl = t[i];
+        rh = t[i + 1];
+      }
+    const bool left = abs_f(__fsub_rn(v, rl)) <= abs_f(__fsub_rn(rh, v));
+    if (out_vals) out_vals[k * n + j] = left ? rl : rh;
+    else I[k * n + j] = lo + (left ? 0 : 1);
+  }
+}
+
+template <typename F>                                        // F: int where every fixed point fits, else long long
+__global__ void __launch_bounds__(CT) k_lut_finder_cols(const int64_t* __restrict__ codes, const float* __restrict__ T,
+                                                        int64_t K, int64_t n, int G, int64_t rows, long long mask,
+                                                        const __grid_constant__ CodeTables ct,
+                                                        int64_t* __restrict__ I, int* __restrict__ status) {
+  __shared__ F sfx[MAXV];
+  for (int i = threadIdx.x; i < ct.ncodes; i += CT) sfx[i] = (F)ct.fx[i];
+  __syncthreads();
+  const int64_t j = (int64_t)blockIdx.x * CT + threadIdx.x;
+  if (j >= n) return;
+  const int64_t k0 = (int64_t)blockIdx.y * rows, k1 = k0 + rows < K ? k0 + rows : K;
+  F ft[LUT];
+  bool tbad = false;
+#pragma unroll
+  for (int t = 0; t < LUT; t++) {
+    int tc = encode1(ct, __ldg(T + (j >> G) * LUT + t));
+    if (tc < 0) {
+      tbad = true;
+      tc = 0;
+    }
+    ft[t] = sfx[tc];
+  }
+  if (tbad && k1 > k0) atomicOr(status, 2);
+  const F fm = (F)mask;
+  for (int64_t k = k0; k < k1; k++) {
+    const int64_t c = codes[k * n + j];
+    if (c < -ct.ncodes || c >= ct.ncodes) {
+      atomicOr(status, 1);
+      I[k * n + j] = 0;
+      continue;
+    }
+    const F f = sfx[c < 0 ? c + ct.ncodes : c];
+    int best = 0;
+    F bd = 0;
+#pragma unroll
+    for (int t = 0; t < LUT; t++) {
+      F d = f - ft[t];
+      d = d < 0 ? -d : d;
+      if (mask) d &= fm;
+      if (t == 0 || d < bd) {
+        bd = d;
+        best = t;
+      }
+    }
+    I[k * n + j] = best;
+  }
+}
+
+// the column kernels' grid: column panels of CT threads, and row slices so that about 16 CTAs per SM are launched
+dim3 cols_grid(int64_t K, int64_t n, int64_t* rows) {
+  const int64_t panels = (n + CT - 1) / CT;
+  const int64_t want = 16 * (int64_t)sm_count();
+  int64_t slices = (want + panels - 1) / panels;
+  if (slices > K) slices = K;
+  if (slices < 1) slices = 1;
+  *rows = (K + slices - 1) / slices;
+  return dim3((unsigned)panels, (unsigned)((K + *rows - 1) / *rows));
 }
 
 int fmt_slot_check(int e, int m, const char* what) {
@@ -625,6 +726,12 @@ int mxq_lut_pick(const float* P, const float* T, int64_t* I, int64_t K, int64_t 
                  int32_t group, int32_t width, void* stream) {
   MXQ_REQUIRE(width >= 2, MXQ_ERR_VALUE, "mxq.lut.pick: tables need width >= 2");
   if (K * n == 0) return MXQ_OK;
+  if (sj == 1 && sk == n && width == LUT && (uintptr_t)T % 16 == 0 && K < (1ll << 31)) {
+    int64_t rows;
+    const dim3 grid = cols_grid(K, n, &rows);
+    k_lut_pick_cols<<<grid, CT, 0, as_stream(stream)>>>(P, T, K, n, group, rows, I, nullptr);
+    return MXQ_LAUNCH_CHECK("lut.pick");
+  }
   k_lut_pick<<<grid_for(K * n, 256), 256, 0, as_stream(stream)>>>(P, T, K, n, sk, sj, group, width, I, nullptr);
   return MXQ_LAUNCH_CHECK("lut.pick");
 }
@@ -633,6 +740,12 @@ int mxq_lut_pick_lookup(const float* P, const float* T, float* out, int64_t K, i
                         int32_t group, int32_t width, void* stream) {
   MXQ_REQUIRE(width >= 2, MXQ_ERR_VALUE, "mxq.lut.pick: tables need width >= 2");
   if (K * n == 0) return MXQ_OK;
+  if (sj == 1 && sk == n && width == LUT && (uintptr_t)T % 16 == 0 && K < (1ll << 31)) {
+    int64_t rows;
+    const dim3 grid = cols_grid(K, n, &rows);
+    k_lut_pick_cols<<<grid, CT, 0, as_stream(stream)>>>(P, T, K, n, group, rows, nullptr, out);
+    return MXQ_LAUNCH_CHECK("lut.pick_lookup");
+  }
   k_lut_pick<<<grid_for(K * n, 256), 256, 0, as_stream(stream)>>>(P, T, K, n, sk, sj, group, width, nullptr, out);
   return MXQ_LAUNCH_CHECK("lut.pick_lookup");
 }
@@ -668,6 +781,20 @@ int mxq_lut_finder(const int64_t* codes, const float* T, int64_t* I, int64_t K, 
   cudaStream_t st = as_stream(stream);
   if (int r = check_cuda(cudaMemsetAsync(status, 0, sizeof(int32_t), st), "lut.finder")) return r;
   if (K * n == 0) return MXQ_OK;
+  if ((uintptr_t)T % 16 == 0 && K < (1ll << 31)) {
+    int64_t rows;
+    const dim3 grid = cols_grid(K, n, &rows);
+    const FormatTables* f = format_tables(e, m);
+    bool narrow = true;                                       // every fixed point and difference fits in an int
+    for (int i = 0; i < f->ncodes; i++) narrow = narrow && f->fx[i] > -(1ll << 30) && f->fx[i] < (1ll << 30);
+    if (narrow)
+      k_lut_finder_cols<int><<<grid, CT, 0, st>>>(codes, T, K, n, group, rows, (long long)fx_mask(e, m),
+                                                  code_tables(f), I, status);
+    else
+      k_lut_finder_cols<long long><<<grid, CT, 0, st>>>(codes, T, K, n, group, rows, (long long)fx_mask(e, m),
+                                                        code_tables(f), I, status);
+    return MXQ_LAUNCH_CHECK("lut.finder");
+  }
   k_lut_finder<<<grid_for(K * n, 256), 256, 0, st>>>(codes, T, K, n, group, (long long)fx_mask(e, m),
                                                      code_tables(format_tables(e, m)), I, status);
   return MXQ_LAUNCH_CHECK("lut.finder");

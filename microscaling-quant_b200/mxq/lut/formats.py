@@ -103,8 +103,8 @@ def finder(codes: torch.Tensor, T: torch.Tensor, fmt: Union[str, Format], *, gro
     _lib.run("mxq_lut_finder", dev, _lib.ptr(c), _lib.ptr(t), _lib.ptr(out), c.shape[0], n, group, f.e, f.m,
              _lib.ptr(st))
     s = int(st.item())
-    if s == 2:
-        encode(t, f)                                     # raises with the offending value
-    if s:
+    if s & 1:                                            # the codes are indexed first (formats.py:152)
         raise IndexError("mxq.lut.finder: a code is outside the format")
+    if s & 2:
+        encode(t, f)                                     # raises with the offending value
     return _lib.back(out, home)

@@ -110,6 +110,24 @@ EXPORT int o_lut_encode(const float* T, int64_t n, int e, int m, int64_t* out) {
   return bad ? -1 : 0;
 }
 
+/* decode (formats.py:114-117): table[codes] with torch indexing (negative codes count from the end); -1 when a
+   code is outside [-nc, nc) */
+EXPORT int o_lut_decode(const int64_t* codes, int64_t n, int e, int m, float* out) {
+  int nc = 1 << (1 + e + m);
+  float* vals = (float*)malloc(sizeof(float) * nc);
+  int64_t* fx = (int64_t*)malloc(sizeof(int64_t) * nc);
+  float safe[512];
+  o_lut_format_tables(e, m, vals, fx, safe);
+  int bad = 0;
+  for (int64_t i = 0; i < n; i++) {
+    int64_t c = codes[i];
+    if (c < -nc || c >= nc) { bad = 1; out[i] = 0.0f; continue; }
+    out[i] = vals[c < 0 ? c + nc : c];
+  }
+  free(vals); free(fx);
+  return bad ? -1 : 0;
+}
+
 /* finder (formats.py:140-159): nearest in fixed point, |diff| masked, first minimum */
 EXPORT int o_lut_finder(const int64_t* codes, const float* T, int64_t K, int64_t n, int group, int e, int m,
                         int64_t* out) {
@@ -120,11 +138,17 @@ EXPORT int o_lut_finder(const int64_t* codes, const float* T, int64_t K, int64_t
   float safe[512];
   o_lut_format_tables(e, m, vals, fx, safe);
   int64_t* tcode = (int64_t*)malloc(sizeof(int64_t) * ng * LUT_SIZE);
-  int rc = o_lut_encode(T, ng * LUT_SIZE, e, m, tcode);
+  /* fx_all[codes] first (formats.py:152): a code outside [-nc, nc) is an IndexError, a negative one counts from
+     the end; then encode(T) (:153) */
+  int rc = 0;
+  for (int64_t i = 0; i < K * n; i++)
+    if (codes[i] < -nc || codes[i] >= nc) rc = -2;
+  if (rc == 0) rc = o_lut_encode(T, ng * LUT_SIZE, e, m, tcode);
   if (rc == 0) {
     for (int64_t k = 0; k < K; k++)
       for (int64_t j = 0; j < n; j++) {
-        int64_t f = fx[codes[k * n + j]];
+        int64_t c = codes[k * n + j];
+        int64_t f = fx[c < 0 ? c + nc : c];
         const int64_t* tc = tcode + (j >> group) * LUT_SIZE;
         int64_t best = 0, bd = 0;
         for (int t = 0; t < LUT_SIZE; t++) {

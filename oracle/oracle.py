@@ -400,8 +400,21 @@ def lut_finder(codes, T, fmt, group):
     K, n = codes.shape
     e, m = FORMATS[fmt][:2]
     out = np.empty((K, n), np.int64)
-    if lib().o_lut_finder(_p(codes, P_I64), _p(T, P_F32), I64(K), I64(n), I32(group), I32(e), I32(m), _p(out, P_I64)):
+    rc = lib().o_lut_finder(_p(codes, P_I64), _p(T, P_F32), I64(K), I64(n), I32(group), I32(e), I32(m), _p(out, P_I64))
+    if rc == -2:
+        raise IndexError("mxq.lut.finder: a code is outside the format")
+    if rc:
         raise ValueError(f"mxq.lut: a table value is not an exact {fmt} value")
+    return out
+
+
+def lut_decode(codes, fmt):
+    """decode (mxq/lut/formats.py:114-117): torch indexing, negative codes from the end."""
+    codes = np.ascontiguousarray(codes, dtype=np.int64)
+    e, m = FORMATS[fmt][:2]
+    out = np.empty(codes.shape, np.float32)
+    if lib().o_lut_decode(_p(codes, P_I64), I64(codes.size), I32(e), I32(m), _p(out, P_F32)):
+        raise IndexError("mxq.lut.decode: a code is outside the format")
     return out
 
 

@@ -400,6 +400,13 @@ def child(only):
                     out[f"lut/{fmt}/{G}/codes"] = N(codes)
                     out[f"lut/{fmt}/{G}/finder"] = N(lut.finder(codes, Tt, fmt, group=G))
                     out[f"lut/{fmt}/{G}/Tcodes"] = N(lut.encode(Tt, fmt))
+                    if G == 1:                                  # negative codes index from the end, as torch does
+                        nc = lf._tables(lf._format(fmt).name)[0].numel()
+                        neg = codes.clone()
+                        neg[::3] -= nc
+                        out[f"lut/{fmt}/codes_neg"] = N(neg)
+                        out[f"lut/{fmt}/decode_neg"] = N(lut.decode(neg, fmt))
+                        out[f"lut/{fmt}/finder_neg"] = N(lut.finder(neg, Tt, fmt, group=G))
         np.savez_compressed(os.path.join(HERE, "lut.npz"), **out)
         print("lut.npz:", len(out), "arrays", flush=True)
 

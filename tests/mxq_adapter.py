@@ -145,6 +145,10 @@ def lut_encode(Tt, fmt):
     return N(_lut.encode(T(np.asarray(Tt, np.float32)), fmt))
 
 
+def lut_decode(codes, fmt):
+    return N(_lut.decode(T(np.asarray(codes, np.int64)), fmt))
+
+
 def lut_finder(codes, Tt, fmt, group):
     return N(_lut.finder(T(np.asarray(codes, np.int64)), T(np.asarray(Tt, np.float32)), fmt, group=group))
 

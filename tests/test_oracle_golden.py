@@ -221,6 +221,22 @@ def test_lut_ops(oracle):
                 assert_bits(oracle.lut_encode(P, fmt), codes, f"encode {fmt}")
                 assert_bits(oracle.lut_encode(T, fmt), g[f"lut/{fmt}/{G}/Tcodes"], f"encode T {fmt}")
                 assert_bits(oracle.lut_finder(codes, T, fmt, G), g[f"lut/{fmt}/{G}/finder"], f"finder {fmt} G{G}")
+        # negative codes count from the end (torch indexing in decode and finder)
+        neg = g[f"lut/{fmt}/codes_neg"]
+        assert_bits(oracle.lut_decode(neg, fmt), g[f"lut/{fmt}/decode_neg"], f"decode negative {fmt}")
+        assert_bits(oracle.lut_finder(neg, g[f"lut/{fmt}/1/T"], fmt, 1), g[f"lut/{fmt}/finder_neg"],
+                    f"finder negative {fmt}")
+        # a code outside [-n, n) is an IndexError, raised before a table value that is no code is looked at
+        bad = neg.copy()
+        bad[0, 0] = 1 << 20
+        Tbad = g[f"lut/{fmt}/1/T"].copy()
+        Tbad[0, 0] = np.float32(0.1)
+        with pytest.raises(IndexError):
+            oracle.lut_finder(bad, Tbad, fmt, 1)
+        with pytest.raises(ValueError):
+            oracle.lut_finder(neg, Tbad, fmt, 1)
+        with pytest.raises(IndexError):
+            oracle.lut_decode(bad, fmt)
 
 
 def test_lut_block(oracle):
