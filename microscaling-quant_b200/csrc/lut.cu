@@ -239,15 +239,27 @@ __global__ void __launch_bounds__(NT) k_lut_tables(const float* __restrict__ P, 
   const int64_t total = K * W;
   const bool kfast = sk == 1;
   bool mybad = false;
-  for (int64_t e = tid; e < total; e += NT) {
-    const int64_t k = kfast ? e % K : e / W, jj = kfast ? e / K : e % W;
-    const float v = P[k * sk + (j0 + jj) * sj];
-    const int b = grid_rank(v, tp);
-    if (sgrid[b] != v) {                                    // also every NaN
-      mybad = true;
-      continue;
+  constexpr int BATCH = 8;                                  // loads in flight per thread
+  for (int64_t e0 = tid; e0 < total; e0 += (int64_t)NT * BATCH) {
+    float v[BATCH];
+    int gcol[BATCH];
+#pragma unroll
+    for (int u = 0; u < BATCH; u++) {
+      const int64_t e = e0 + (int64_t)u * NT;
+      const int64_t k = kfast ? e % K : e / W, jj = kfast ? e / K : e % W;
+      gcol[u] = e < total ? (int)(jj >> G) : -1;
+      v[u] = e < total ? P[k * sk + (j0 + jj) * sj] : 0.0f;
     }
-    atomicAdd(&counts[(int)(jj >> G) * nv + b], 1);
+#pragma unroll
+    for (int u = 0; u < BATCH; u++) {
+      if (gcol[u] < 0) continue;
+      const int b = grid_rank(v[u], tp);
+      if (sgrid[b] != v[u]) {                               // also every NaN
+        mybad = true;
+        continue;
+      }
+      atomicAdd(&counts[gcol[u] * nv + b], 1);
+    }
   }
   if (mybad) bad = 1;
   __syncthreads();
@@ -550,93 +562,125 @@ __global__ void k_lut_finder(const int64_t* __restrict__ codes, const float* __r
 // once per column instead of once per element; consecutive threads read consecutive columns.
 constexpr int CT = 256;
 
+constexpr int ROWP = LUT + 1;                                // a table row in shared memory, padded (banks)
+
 __global__ void __launch_bounds__(CT) k_lut_pick_cols(const float* __restrict__ P, const float* __restrict__ T,
                                                       int64_t K, int64_t n, int G, int64_t rows,
                                                       int64_t* __restrict__ I, float* __restrict__ out_vals) {
-  const int64_t j = (int64_t)blockIdx.x * CT + threadIdx.x;
+  __shared__ float st[CT * ROWP];                            // the panel's tables (at most one per column)
+  const int64_t jp = (int64_t)blockIdx.x * CT, j = jp + threadIdx.x;
+  const int64_t gfirst = jp >> G, glast = ((jp + CT < n ? jp + CT : n) - 1) >> G;
+  const int ngp = (int)(glast - gfirst + 1);
+  for (int i = threadIdx.x; i < ngp * LUT; i += CT) st[(i / LUT) * ROWP + i % LUT] = __ldg(T + gfirst * LUT + i);
+  __syncthreads();
   if (j >= n) return;
   const int64_t k0 = (int64_t)blockIdx.y * rows, k1 = k0 + rows < K ? k0 + rows : K;
-  float t[LUT];
-  const float4* row = reinterpret_cast<const float4*>(T + (j >> G) * LUT);
+  const float* t = st + (int)((j >> G) - gfirst) * ROWP;
+  constexpr int BATCH = 4;                                   // loads in flight per thread
+  for (int64_t kb = k0; kb < k1; kb += BATCH) {
+    float vb[BATCH];
 #pragma unroll
-  for (int q = 0; q < LUT / 4; q++) {
-    const float4 v = __ldg(row + q);
-    t[4 * q] = v.x;
-    t[4 * q + 1] = v.y;
-    t[4 * q + 2] = v.z;
-    t[4 * q + 3] = v.w;
-  }
-  for (int64_t k = k0; k < k1; k++) {
-    const float v = P[k * n + j];
-    int cnt = 0;                                            // lower_bound: entries below v
+    for (int u = 0; u < BATCH; u++) vb[u] = kb + u < k1 ? P[(kb + u) * n + j] : 0.0f;
 #pragma unroll
-    for (int i = 0; i < LUT; i++) cnt += t[i] < v;
-    const int lo = cnt < 1 ? 0 : (cnt > LUT - 1 ? LUT - 2 : cnt - 1);
-    float rl = t[0], rh = t[1];
-#pragma unroll
-    for (int i = 1; i < LUT - 1; i++)
-      if (lo == i) {
-        rl = t[i];
-        rh = t[i + 1];
-      }
+    for (int u = 0; u < BATCH; u++) {
+    const int64_t k = kb + u;
+    if (k >= k1) break;
+    const float v = vb[u];
+    int base = 0;                                            // lower_bound over 16 sorted entries, branch-free
+    base += t[base + 7] < v ? 8 : 0;
+    base += t[base + 3] < v ? 4 : 0;
+    base += t[base + 1] < v ? 2 : 0;
+    base += t[base] < v ? 1 : 0;
+    const int lb = base + (base == LUT - 1 && t[LUT - 1] < v ? 1 : 0);
+    const int lo = lb < 1 ? 0 : (lb > LUT - 1 ? LUT - 2 : lb - 1);
+    const float rl = t[lo], rh = t[lo + 1];
     const bool left = abs_f(__fsub_rn(v, rl)) <= abs_f(__fsub_rn(rh, v));
     if (out_vals) out_vals[k * n + j] = left ? rl : rh;
     else I[k * n + j] = lo + (left ? 0 : 1);
+    }
   }
 }
 
+// finder: each CTA first tabulates the answer for every (group of its panel, code) pair -- 16 masked fixed-point
+// distances, first minimum, as a packed (distance << 4 | index) minimum -- then an element is a shared-memory read.
 template <typename F>                                        // F: int where every fixed point fits, else long long
 __global__ void __launch_bounds__(CT) k_lut_finder_cols(const int64_t* __restrict__ codes, const float* __restrict__ T,
                                                         int64_t K, int64_t n, int G, int64_t rows, long long mask,
                                                         const __grid_constant__ CodeTables ct,
                                                         int64_t* __restrict__ I, int* __restrict__ status) {
+  extern __shared__ unsigned char ans[];                     // [groups of the panel][ncodes]
   __shared__ F sfx[MAXV];
-  for (int i = threadIdx.x; i < ct.ncodes; i += CT) sfx[i] = (F)ct.fx[i];
-  __syncthreads();
-  const int64_t j = (int64_t)blockIdx.x * CT + threadIdx.x;
-  if (j >= n) return;
+  __shared__ F sft[CT][LUT];                                 // the panel's tables as fixed points
+  __shared__ uint32_t sbits[MAXV];                           // encode's map (value bits -> lowest code), staged
+  __shared__ int16_t scode[MAXV];
+  const int nc = ct.ncodes, ne = ct.nenc;
+  const int64_t jp = (int64_t)blockIdx.x * CT;
+  const int64_t gfirst = jp >> G, glast = ((jp + CT < n ? jp + CT : n) - 1) >> G;
+  const int ngp = (int)(glast - gfirst + 1);
   const int64_t k0 = (int64_t)blockIdx.y * rows, k1 = k0 + rows < K ? k0 + rows : K;
-  F ft[LUT];
+  for (int i = threadIdx.x; i < nc; i += CT) sfx[i] = (F)ct.fx[i];
+  for (int i = threadIdx.x; i < ne; i += CT) {
+    sbits[i] = ct.enc_bits[i];
+    scode[i] = ct.enc_code[i];
+  }
+  __syncthreads();
   bool tbad = false;
-#pragma unroll
-  for (int t = 0; t < LUT; t++) {
-    int tc = encode1(ct, __ldg(T + (j >> G) * LUT + t));
+  for (int i = threadIdx.x; i < ngp * LUT; i += CT) {
+    const uint32_t b = f2u(__ldg(T + gfirst * LUT + i));
+    int lo = 0, hi = ne;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (sbits[mid] < b) lo = mid + 1;
+      else hi = mid;
+    }
+    int tc = (lo < ne && sbits[lo] == b) ? scode[lo] : -1;
     if (tc < 0) {
       tbad = true;
       tc = 0;
     }
-    ft[t] = sfx[tc];
+    sft[i / LUT][i % LUT] = sfx[tc];
   }
   if (tbad && k1 > k0) atomicOr(status, 2);
+  __syncthreads();
   const F fm = (F)mask;
-  for (int64_t k = k0; k < k1; k++) {
-    const int64_t c = codes[k * n + j];
-    if (c < -ct.ncodes || c >= ct.ncodes) {
-      atomicOr(status, 1);
-      I[k * n + j] = 0;
-      continue;
-    }
-    const F f = sfx[c < 0 ? c + ct.ncodes : c];
-    int best = 0;
-    F bd = 0;
+  for (int i = threadIdx.x; i < ngp * nc; i += CT) {
+    const int gl = i / nc;
+    const F f = sfx[i % nc];
+    long long key = 0;
 #pragma unroll
     for (int t = 0; t < LUT; t++) {
-      F d = f - ft[t];
+      F d = f - sft[gl][t];
       d = d < 0 ? -d : d;
       if (mask) d &= fm;
-      if (t == 0 || d < bd) {
-        bd = d;
-        best = t;
-      }
+      const long long kt = ((long long)d << 4) | t;          // the smaller distance, then the lower index
+      key = (t == 0 || kt < key) ? kt : key;
     }
-    I[k * n + j] = best;
+    ans[i] = (unsigned char)(key & 15);
+  }
+  __syncthreads();
+  const int64_t j = jp + threadIdx.x;
+  if (j >= n) return;
+  const unsigned char* a = ans + (int)((j >> G) - gfirst) * nc;
+  constexpr int BATCH = 4;                                   // loads in flight per thread
+  for (int64_t kb = k0; kb < k1; kb += BATCH) {
+    int64_t c[BATCH];
+#pragma unroll
+    for (int u = 0; u < BATCH; u++) c[u] = kb + u < k1 ? codes[(kb + u) * n + j] : 0;
+#pragma unroll
+    for (int u = 0; u < BATCH; u++) {
+      if (kb + u >= k1) break;
+      int64_t r = 0;
+      if (c[u] < -nc || c[u] >= nc) atomicOr(status, 1);
+      else r = a[c[u] < 0 ? c[u] + nc : c[u]];
+      I[(kb + u) * n + j] = r;
+    }
   }
 }
 
-// the column kernels' grid: column panels of CT threads, and row slices so that about 16 CTAs per SM are launched
-dim3 cols_grid(int64_t K, int64_t n, int64_t* rows) {
+// the column kernels' grid: column panels of CT threads, and row slices so that about per_sm CTAs per SM are launched
+dim3 cols_grid(int64_t K, int64_t n, int64_t* rows, int per_sm = 16) {
   const int64_t panels = (n + CT - 1) / CT;
-  const int64_t want = 16 * (int64_t)sm_count();
+  const int64_t want = per_sm * (int64_t)sm_count();
   int64_t slices = (want + panels - 1) / panels;
   if (slices > K) slices = K;
   if (slices < 1) slices = 1;
@@ -783,16 +827,27 @@ int mxq_lut_finder(const int64_t* codes, const float* T, int64_t* I, int64_t K, 
   if (K * n == 0) return MXQ_OK;
   if ((uintptr_t)T % 16 == 0 && K < (1ll << 31)) {
     int64_t rows;
-    const dim3 grid = cols_grid(K, n, &rows);
     const FormatTables* f = format_tables(e, m);
+    const dim3 grid = cols_grid(K, n, &rows, f->ncodes <= 64 ? 8 : 4);   // the answer table costs ncodes per column
     bool narrow = true;                                       // every fixed point and difference fits in an int
     for (int i = 0; i < f->ncodes; i++) narrow = narrow && f->fx[i] > -(1ll << 30) && f->fx[i] < (1ll << 30);
-    if (narrow)
-      k_lut_finder_cols<int><<<grid, CT, 0, st>>>(codes, T, K, n, group, rows, (long long)fx_mask(e, m),
-                                                  code_tables(f), I, status);
-    else
-      k_lut_finder_cols<long long><<<grid, CT, 0, st>>>(codes, T, K, n, group, rows, (long long)fx_mask(e, m),
-                                                        code_tables(f), I, status);
+    const size_t smem = (size_t)CT * f->ncodes;               // answers: at most one group per column
+    int r;
+    if (narrow) {
+      r = check_cuda(cudaFuncSetAttribute(k_lut_finder_cols<int>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem), "lut.finder: shared memory attribute");
+      if (r == MXQ_OK)
+        k_lut_finder_cols<int><<<grid, CT, smem, st>>>(codes, T, K, n, group, rows, (long long)fx_mask(e, m),
+                                                       code_tables(f), I, status);
+    } else {
+      r = check_cuda(cudaFuncSetAttribute(k_lut_finder_cols<long long>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                     "lut.finder: shared memory attribute");
+      if (r == MXQ_OK)
+        k_lut_finder_cols<long long><<<grid, CT, smem, st>>>(codes, T, K, n, group, rows,
+                                                             (long long)fx_mask(e, m), code_tables(f), I, status);
+    }
+    if (r) return r;
     return MXQ_LAUNCH_CHECK("lut.finder");
   }
   k_lut_finder<<<grid_for(K * n, 256), 256, 0, st>>>(codes, T, K, n, group, (long long)fx_mask(e, m),
