@@ -46,6 +46,16 @@ def _layout(V: torch.Tensor, axis: int, block_size: int):
     return axis, outer, L, inner, (L + block_size - 1) // block_size
 
 
+def _check_reshape(V: torch.Tensor, axis: int, block_size: int) -> None:
+    """The reference blocks V with reshape(*rest, -1, block_size) (mxq/block/_driver.py:23-32), which torch refuses
+    for an empty V whose other dimensions include a zero; the same RuntimeError here."""
+    if V.numel() == 0:
+        rest = [s for i, s in enumerate(V.shape) if i != axis]
+        if 0 in rest:
+            raise RuntimeError(f"cannot reshape tensor of 0 elements into shape {rest + [-1, block_size]} because the "
+                               "unspecified dimension size -1 can be any value and is ambiguous")
+
+
 def _blocked_shape(V, axis, nb, last):
     return tuple(V.shape[:axis]) + tuple(V.shape[axis + 1:]) + (nb, last)
 
@@ -53,6 +63,7 @@ def _blocked_shape(V, axis, nb, last):
 def to_blocks(V: torch.Tensor, axis: int, block_size: int, X: Optional[torch.Tensor] = None) -> Blocks:
     """V moved to (..., nblocks, block_size), zero-padded; divided by the blocked scales X when given."""
     axis_, outer, L, inner, nb = _layout(V, axis, block_size)
+    _check_reshape(V, axis_, block_size)
     home = _lib.home(V)
     dev = _lib.device_for(V, X)
     v = _lib.on(V, dev)
@@ -96,6 +107,7 @@ def compose(V: torch.Tensor, *, scale: Optional[Callable[[torch.Tensor], torch.T
     elem(z) -> P       z = block / X, shape (..., nblocks, block_size); P the same shape
     Either may be None: no scale step means X = 1, no element step means P = V / X."""
     axis_, outer, L, inner, nb = _layout(V, axis, block_size)
+    _check_reshape(V, axis_, block_size)
     home = _lib.home(V)
     dev = _lib.device_for(V)
     v = _lib.on(V, dev)
@@ -196,6 +208,7 @@ def quantize_fused(V: torch.Tensor, spec: "_lib.MxqQuantSpec", axis: int, block_
     """A named quantizer's compose as one kernel: P and X from V in one pass (mxq_block_quantize). A large host V
     streams through the device in chunks (_quantize_streamed) and P, X come back as pinned host tensors."""
     axis_, outer, L, inner, nb = _layout(V, axis, block_size)
+    _check_reshape(V, axis_, block_size)
     home = _lib.home(V)
     dev = _lib.device_for(V)
     if not V.is_cuda and V.numel() * 4 >= STREAM_MIN_BYTES:

@@ -26,6 +26,7 @@ def quantize(V: torch.Tensor, fmt, axis: int, block_size: int, *, rounding_mode:
     f = lut.formats._format(fmt)                               # refuse a non-LUT format first
     spec = mxgemmini.spec(fmt, rounding_mode, scale_floor)     # then what block.mxgemmini refuses
     _driver._layout(V, axis, block_size)
+    _driver._check_reshape(V, axis % 2, block_size)
     lut.kmeans._check(V if axis % 2 == 0 else V.t(), group)    # then what lut.tables refuses
     if not isinstance(max_iters, int) or isinstance(max_iters, bool) or max_iters < 0:
         raise ValueError(f"mxq.lut: max_iters {max_iters!r} must be a non-negative integer")

@@ -41,3 +41,15 @@ def test_version_and_errors():
     m = (ctypes.c_int32 * 16)(*([4] * 16))
     rc = L.mxq_systolic(None, None, None, None, None, 32, 1, 1, 32, 12, ctypes.byref(arith), e, m, None)
     assert rc == _lib.ERR_VALUE and b"must divide block size" in L.mxq_last_error()
+
+
+def test_empty_block_shapes_refused_like_torch_reshape():
+    """The reference blocks V with reshape(*rest, -1, block); torch refuses an empty V whose other dimensions hold a
+    zero, before any device work -- and so does this package."""
+    import pytest
+    import torch
+    from mxq import block
+    for shape, axis in (((0, 64), 1), ((64, 0), 0), ((0, 0), 0)):
+        for q in (block.mxquant.quantize, block.mxgemmini.quantize, block.ocp.quantize):
+            with pytest.raises(RuntimeError, match="cannot reshape tensor of 0 elements"):
+                q(torch.zeros(shape), "MXFP8_E4M3", axis=axis)
