@@ -137,6 +137,13 @@ int mxq_dequantize(const float* P, const float* X, float* out, int64_t outer, in
 int mxq_systolic(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
                  int64_t N, int64_t block, int64_t size, const mxq_arith* arith, const int32_t* sched_e,
                  const int32_t* sched_m, void* stream);
+/* No reference counterpart: mxq_systolic over `batch` independent problems stacked contiguously (PA batch x K x M,
+ * XA batch x ceil(K/block) x M, PB batch x K x N, XB batch x ceil(K/block) x N, Y batch x M x N), each result
+ * bit-identical to mxq_systolic on that problem alone; one launch for many small problems (attend's heads,
+ * mxq/nn/_attention.py:102-141). */
+int mxq_systolic_batched(const float* PA, const float* XA, const float* PB, const float* XB, float* Y,
+                         int64_t batch, int64_t K, int64_t M, int64_t N, int64_t block, int64_t size,
+                         const mxq_arith* arith, const int32_t* sched_e, const int32_t* sched_m, void* stream);
 /* mxq/matmul/_adder.py:42-71 adder_tree: log2(size) levels, level formats (level_e[l], level_m[l]) */
 int mxq_adder_tree(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
                    int64_t N, int64_t block, int64_t size, const mxq_arith* arith, const int32_t* level_e,

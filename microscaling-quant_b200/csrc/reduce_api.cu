@@ -59,6 +59,36 @@ int mxq_systolic(const float* PA, const float* XA, const float* PB, const float*
   return systolic_generic(PA, XA, PB, XB, Y, K, M, N, block, (int)size, A, lanes, st);
 }
 
+int mxq_systolic_batched(const float* PA, const float* XA, const float* PB, const float* XB, float* Y,
+                         int64_t batch, int64_t K, int64_t M, int64_t N, int64_t block, int64_t size,
+                         const mxq_arith* arith, const int32_t* sched_e, const int32_t* sched_m, void* stream) {
+  MXQ_REQUIRE(batch >= 0, MXQ_ERR_VALUE, "systolic: negative batch");
+  if (int r = check_dims(K, M, N, block, size, "systolic")) return r;
+  if (int r = check_arith(arith, "systolic")) return r;
+  LaneTable lanes;
+  if (int r = fill_lanes(lanes, sched_e, sched_m, size, "systolic")) return r;
+  if (M == 0 || N == 0 || batch == 0) return MXQ_OK;
+  ArithP A = to_arith(arith);
+  cudaStream_t st = as_stream(stream);
+  const int64_t nb = (K + block - 1) / block;
+  const Batch bt{K * M, nb * M, K * N, nb * N, M * N};
+  for (int64_t z0 = 0; z0 < batch; z0 += 65535) {           // gridDim.z holds at most 65535 problems
+    const int zb = (int)(batch - z0 < 65535 ? batch - z0 : 65535);
+    int r = systolic_fast(PA + z0 * bt.pa, XA + z0 * bt.xa, PB + z0 * bt.pb, XB + z0 * bt.xb, Y + z0 * bt.y, K, M, N,
+                          block, (int)size, A, lanes, st, zb, bt);
+    if (r == MXQ_ERR_UNSUPPORTED) {                           // no specialised kernel: one generic launch each
+      for (int64_t z = z0; z < z0 + zb; z++) {
+        r = systolic_generic(PA + z * bt.pa, XA + z * bt.xa, PB + z * bt.pb, XB + z * bt.xb, Y + z * bt.y, K, M, N,
+                             block, (int)size, A, lanes, st);
+        if (r) return r;
+      }
+    } else if (r) {
+      return r;
+    }
+  }
+  return MXQ_OK;
+}
+
 int mxq_adder_tree(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
                    int64_t N, int64_t block, int64_t size, const mxq_arith* arith, const int32_t* level_e,
                    const int32_t* level_m, void* stream) {

@@ -44,7 +44,15 @@ template <int RM, int RN>
 __global__ void __launch_bounds__(256, (RM * RN <= 32) ? 2 : 1)
     k_systolic_hw(const float* __restrict__ PA, const float* __restrict__ XA, const float* __restrict__ PB,
                   const float* __restrict__ XB, float* __restrict__ Y, int64_t K, int64_t M, int64_t N, ArithP A,
-                  LaneTable lanes) {
+                  LaneTable lanes, Batch bt) {
+  {                                                        // this CTA's problem of a batched launch
+    const int64_t z = blockIdx.z;
+    PA += z * bt.pa;
+    XA += z * bt.xa;
+    PB += z * bt.pb;
+    XB += z * bt.xb;
+    Y += z * bt.y;
+  }
   using TT = Tile<RM, RN>;
   constexpr int NT = TT::NT, BM = TT::BM, BN = TT::BN, HM = TT::HM, HN = TT::HN;
   extern __shared__ __align__(16) float smem[];
@@ -197,14 +205,14 @@ __global__ void __launch_bounds__(256, (RM * RN <= 32) ? 2 : 1)
 
 template <int RM, int RN>
 int launch_hw(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
-              int64_t N, const ArithP& A, const LaneTable& lanes, cudaStream_t st) {
+              int64_t N, const ArithP& A, const LaneTable& lanes, cudaStream_t st, int batch, const Batch& bt) {
   using TT = Tile<RM, RN>;
   if (int r = check_cuda(cudaFuncSetAttribute(k_systolic_hw<RM, RN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               (int)TT::SMEM),
                          "systolic: shared memory attribute"))
     return r;
-  dim3 grid((unsigned)((N + TT::BN - 1) / TT::BN), (unsigned)((M + TT::BM - 1) / TT::BM));
-  k_systolic_hw<RM, RN><<<grid, TT::NT, TT::SMEM, st>>>(PA, XA, PB, XB, Y, K, M, N, A, lanes);
+  dim3 grid((unsigned)((N + TT::BN - 1) / TT::BN), (unsigned)((M + TT::BM - 1) / TT::BM), (unsigned)batch);
+  k_systolic_hw<RM, RN><<<grid, TT::NT, TT::SMEM, st>>>(PA, XA, PB, XB, Y, K, M, N, A, lanes, bt);
   return MXQ_LAUNCH_CHECK("systolic");
 }
 
@@ -222,15 +230,17 @@ bool is_hw_final(const LaneTable& t, int size) {
 namespace mxq {
 
 int systolic_fast(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K, int64_t M,
-                  int64_t N, int64_t bs, int size, const ArithP& A, const LaneTable& lanes, cudaStream_t st) {
-  if (A.kind == MXQ_ARITH_MXQUANT) return systolic_mxquant_fast(PA, XA, PB, XB, Y, K, M, N, bs, size, A, lanes, st);
+                  int64_t N, int64_t bs, int size, const ArithP& A, const LaneTable& lanes, cudaStream_t st,
+                  int batch, Batch bt) {
+  if (A.kind == MXQ_ARITH_MXQUANT)
+    return systolic_mxquant_fast(PA, XA, PB, XB, Y, K, M, N, bs, size, A, lanes, st, batch, bt);
   const bool tapeout = A.kind == MXQ_ARITH_MXGEMMINI && A.prod_e == 4 && A.prod_m == 3 && A.has_floor &&
                        A.floor_thr == 1.52587890625e-05f && A.sat_limit == 448.0f && A.sat_value == 448.0f;
   const bool aligned = M % 4 == 0 && N % 4 == 0 && (uintptr_t)PA % 16 == 0 && (uintptr_t)PB % 16 == 0;
   if (!tapeout || bs != 32 || !is_hw_final(lanes, size) || !aligned || K == 0) return MXQ_ERR_UNSUPPORTED;
   // 4 x 8 micro-tiles: 123 registers, two CTAs (16 warps) per SM; measured 2.89 TMAC/s at 4096^3 against 2.56 for
   // 8 x 8 (255 registers, 8 warps)
-  return launch_hw<4, 8>(PA, XA, PB, XB, Y, K, M, N, A, lanes, st);
+  return launch_hw<4, 8>(PA, XA, PB, XB, Y, K, M, N, A, lanes, st, batch, bt);
 }
 
 }  // namespace mxq

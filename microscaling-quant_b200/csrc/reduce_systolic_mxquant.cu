@@ -60,7 +60,15 @@ template <int RM, int RN>
 __global__ void __launch_bounds__(256, 2)
     k_systolic_mxq(const float* __restrict__ PA, const float* __restrict__ XA, const float* __restrict__ PB,
                    const float* __restrict__ XB, float* __restrict__ Y, int64_t K, int64_t M, int64_t N, ArithP A,
-                   LaneTable lanes, QFmt qp, QLanes ql) {
+                   LaneTable lanes, QFmt qp, QLanes ql, Batch bt) {
+  {                                                        // this CTA's problem of a batched launch
+    const int64_t z = blockIdx.z;
+    PA += z * bt.pa;
+    XA += z * bt.xa;
+    PB += z * bt.pb;
+    XB += z * bt.xb;
+    Y += z * bt.y;
+  }
   using TT = Tile<RM, RN>;
   constexpr int NT = TT::NT, BM = TT::BM, BN = TT::BN, HM = TT::HM, HN = TT::HN;
   extern __shared__ __align__(16) float smem[];
@@ -178,7 +186,7 @@ namespace mxq {
 
 int systolic_mxquant_fast(const float* PA, const float* XA, const float* PB, const float* XB, float* Y, int64_t K,
                           int64_t M, int64_t N, int64_t bs, int size, const ArithP& A, const LaneTable& lanes,
-                          cudaStream_t st) {
+                          cudaStream_t st, int batch, Batch bt) {
   bool ok = A.kind == MXQ_ARITH_MXQUANT && A.prod_e >= 4 && A.prod_e <= 7 && A.prod_m >= 1 && A.prod_m <= 22 &&
             bs == 32 && size == 16 && M % 4 == 0 && N % 4 == 0 && (uintptr_t)PA % 16 == 0 &&
             (uintptr_t)PB % 16 == 0 && K > 0;
@@ -193,8 +201,8 @@ int systolic_mxquant_fast(const float* PA, const float* XA, const float* PB, con
                                               (int)TT::SMEM),
                          "systolic: shared memory attribute"))
     return r;
-  dim3 grid((unsigned)((N + TT::BN - 1) / TT::BN), (unsigned)((M + TT::BM - 1) / TT::BM));
-  k_systolic_mxq<RM, RN><<<grid, TT::NT, TT::SMEM, st>>>(PA, XA, PB, XB, Y, K, M, N, A, lanes, qp, ql);
+  dim3 grid((unsigned)((N + TT::BN - 1) / TT::BN), (unsigned)((M + TT::BM - 1) / TT::BM), (unsigned)batch);
+  k_systolic_mxq<RM, RN><<<grid, TT::NT, TT::SMEM, st>>>(PA, XA, PB, XB, Y, K, M, N, A, lanes, qp, ql, bt);
   return MXQ_LAUNCH_CHECK("systolic");
 }
 

@@ -68,6 +68,7 @@ _SIGS = {
     "mxq_from_blocks": [P, P, I64, I64, I64, I64, P],
     "mxq_dequantize": [P, P, P, I64, I64, I64, I64, P],
     "mxq_systolic": [P, P, P, P, P, I64, I64, I64, I64, I64, ctypes.POINTER(MxqArith), P, P, P],
+    "mxq_systolic_batched": [P, P, P, P, P, I64, I64, I64, I64, I64, I64, ctypes.POINTER(MxqArith), P, P, P],
     "mxq_adder_tree": [P, P, P, P, P, I64, I64, I64, I64, I64, ctypes.POINTER(MxqArith), P, P, P],
     "mxq_anchor_tree": [P, P, P, P, P, I64, I64, I64, I64, I64, ctypes.POINTER(MxqArith), P, P,
                         ctypes.POINTER(MxqAnchorSpec), P, P],

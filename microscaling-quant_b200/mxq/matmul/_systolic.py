@@ -12,7 +12,7 @@ from ..block import BLOCK
 from ._common import check_operands, check_schedule, int_pairs, kernel_spec, operands
 from ._arithmetic import Arithmetic
 
-__all__ = ["systolic"]
+__all__ = ["systolic", "systolic_batched"]
 
 
 def systolic(P_A: torch.Tensor, X_A: torch.Tensor, P_B: torch.Tensor, X_B: torch.Tensor,
@@ -31,4 +31,28 @@ def systolic(P_A: torch.Tensor, X_A: torch.Tensor, P_B: torch.Tensor, X_B: torch
     c = spec.c_struct()
     _lib.run("mxq_systolic", dev, _lib.ptr(pa), _lib.ptr(xa), _lib.ptr(pb), _lib.ptr(xb), _lib.ptr(Y), K, M, N,
              block_size, size, ctypes.byref(c), es, ms)
+    return _lib.back(Y, home)
+
+
+def systolic_batched(P_A: torch.Tensor, X_A: torch.Tensor, P_B: torch.Tensor, X_B: torch.Tensor,
+                     arith: Arithmetic, schedule: Sequence[Tuple[int, int]], size: int = 16,
+                     block_size: int = BLOCK) -> torch.Tensor:
+    """systolic over a stack: P_A S×K×M, X_A S×ceil(K/block_size)×M, P_B S×K×N, X_B S×ceil(K/block_size)×N ->
+    Y S×M×N, Y[s] bit-identical to systolic(P_A[s], X_A[s], P_B[s], X_B[s], ...). One launch for the stack (no
+    reference counterpart; attend uses it for all heads at once)."""
+    if any(t.ndim != 3 for t in (P_A, X_A, P_B, X_B)) or len({t.shape[0] for t in (P_A, X_A, P_B, X_B)}) != 1:
+        raise ValueError("systolic_batched: codes and scales must be 3-D stacks of one length")
+    S = P_A.shape[0]
+    K, M, N = check_operands(P_A[0], X_A[0], P_B[0], X_B[0], block_size) if S else (P_A.shape[1], P_A.shape[2],
+                                                                                     P_B.shape[2])
+    check_schedule(schedule, size)
+    if block_size % size != 0:
+        raise ValueError(f"size {size} must divide block size {block_size}")
+    spec = kernel_spec(arith, "systolic")
+    (pa, xa, pb, xb), dev, home = operands(P_A, X_A, P_B, X_B)
+    Y = torch.empty((S, M, N), dtype=torch.float32, device=dev)
+    es, ms = int_pairs(schedule)
+    c = spec.c_struct()
+    _lib.run("mxq_systolic_batched", dev, _lib.ptr(pa), _lib.ptr(xa), _lib.ptr(pb), _lib.ptr(xb), _lib.ptr(Y), S, K,
+             M, N, block_size, size, ctypes.byref(c), es, ms)
     return _lib.back(Y, home)

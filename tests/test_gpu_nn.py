@@ -65,6 +65,36 @@ def test_attend_golden():
         assert err <= 1e-6, f"{key}: {err} (bit-identical fraction {frac})"
 
 
+@pytest.mark.parametrize("B,H,Hkv,Tq,Tk,D,masked", [(2, 4, 4, 40, 40, 32, True), (3, 8, 2, 33, 50, 64, False),
+                                                     (2, 6, 3, 17, 17, 32, "per-row")])
+def test_attend_stacked_equals_loop(B, H, Hkv, Tq, Tk, D, masked):
+    """The stacked path (Schemes of this package's quantizers and systolic: every head in one launch) against the
+    per-head loop (the same Schemes with the quantizers wrapped, so they are not recognised) bit for bit: with and
+    without a mask, a per-batch-row mask, grouped KV heads, Tq != Tk."""
+    import mxq
+    from mxq import Scheme, block, matmul, schedule
+    from mxq.nn import attend
+    g = torch.Generator().manual_seed(B * 100 + H)
+    q = torch.randn(B, H, Tq, D, generator=g).cuda()
+    k = torch.randn(B, Hkv, Tk, D, generator=g).cuda()
+    v = torch.randn(B, Hkv, Tk, D, generator=g).cuda()
+    mask = None
+    if masked:
+        rows = B if masked == "per-row" else 1
+        m = torch.zeros(rows, 1, Tq, Tk)
+        m[..., Tk // 2:] = float("-inf")
+        m[..., 3] = -1.5
+        mask = m.cuda()
+    fast = hw_scheme()
+    q8 = partial(block.mxgemmini.quantize, fmt="MXFP8_E4M3", axis=0)
+    slow = Scheme("wrapped", a=lambda V: q8(V), b=lambda V: q8(V), reduce=fast.reduce)
+    from mxq.nn import _attention
+    assert _attention._stacked(fast) is not None and _attention._stacked(slow) is None
+    o1 = attend(q, k, v, mask, D ** -0.5, fast, fast)
+    o2 = attend(q, k, v, mask, D ** -0.5, slow, slow)
+    assert_bits(o1.cpu().numpy(), o2.cpu().numpy(), "stacked vs loop")
+
+
 def test_patched_llama():
     from transformers import LlamaConfig, LlamaForCausalLM
     from mxq.nn import patch
