@@ -46,6 +46,13 @@ __device__ __forceinline__ float rne_lane(float s, const Lane& l) {
   return __fsub_rn(__fadd_rn(s, c), c);
 }
 
+// two float32 values rounded to bf16 nearest-even by the hardware conversion, packed as pack_bf16 does (hi in the
+// upper half); finite inputs and infinities round exactly as bf16_rne does (a NaN becomes the canonical NaN)
+__device__ __forceinline__ uint32_t bf16x2_rne(float hi, float lo) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
 __device__ __forceinline__ uint32_t pack_bf16(float hi, float lo) {
   return (f2u(hi) & 0xffff0000u) | (f2u(lo) >> 16);
 }
