@@ -15,7 +15,8 @@
 //     rounding of the operands is the identity, the float32 sum is exact (multiples of 2^(-6-m) below 2^8) and one
 //     RNE remains; the magnitudes stay below 16, 32, 64 and 128, far inside float(4, m)'s range;
 //   * level 4 (bf16) and the tile add: level-3 nodes have at most 8 significant bits (m2 <= 7), so they are bf16
-//     values already, and a float32 sum of bf16 values rounded to bf16 is the exact sum rounded to bf16.
+//     values already, and a float32 sum of bf16 values rounded to bf16 is the exact sum rounded to bf16 (the
+//     hardware's pair conversion, cvt.rn.bf16x2.f32, does the rounding).
 // Zero signs never matter: lanes map -0 to +0, and the output C starts at +0 and is a sum of values under RNE.
 // A k-block outside the domain (or a short last block) runs the generic per-element tree for that block only.
 #include "common.cuh"
@@ -145,13 +146,12 @@ __global__ void __launch_bounds__(256, 2)
           for (int i = 0; i < RM; i++)
 #pragma unroll
             for (int j = 0; j < RN / 2; j++) {
-              const float r0 = bf16_rne(__fadd_rn(hold[i][2 * j], n3[i][2 * j]));
-              const float r1 = bf16_rne(__fadd_rn(hold[i][2 * j + 1], n3[i][2 * j + 1]));
-              const float t0 = bf16_rne(__fmul_rn(r0, __fmul_rn(xa[i], xb[2 * j])));
-              const float t1 = bf16_rne(__fmul_rn(r1, __fmul_rn(xa[i], xb[2 * j + 1])));
-              const float c0 = bf16_rne(__fadd_rn(unpack_hi(Cp[i][j]), t0));
-              const float c1 = bf16_rne(__fadd_rn(unpack_lo(Cp[i][j]), t1));
-              Cp[i][j] = pack_bf16(c0, c1);
+              const uint32_t r = bf16x2_rne(__fadd_rn(hold[i][2 * j], n3[i][2 * j]),
+                                            __fadd_rn(hold[i][2 * j + 1], n3[i][2 * j + 1]));
+              const uint32_t t = bf16x2_rne(__fmul_rn(unpack_hi(r), __fmul_rn(xa[i], xb[2 * j])),
+                                            __fmul_rn(unpack_lo(r), __fmul_rn(xa[i], xb[2 * j + 1])));
+              Cp[i][j] = bf16x2_rne(__fadd_rn(unpack_hi(Cp[i][j]), unpack_hi(t)),
+                                    __fadd_rn(unpack_lo(Cp[i][j]), unpack_lo(t)));
             }
         }
       }

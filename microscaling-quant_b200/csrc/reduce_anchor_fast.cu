@@ -227,11 +227,11 @@ __global__ void __launch_bounds__(256, 2)
             // 2^G from 2^-G: the biased exponents add up to 254
             const float s0 = __fmul_rn(acc[i][2 * j], u2f(0x7f000000u - f2u(inv[i][2 * j])));
             const float s1 = __fmul_rn(acc[i][2 * j + 1], u2f(0x7f000000u - f2u(inv[i][2 * j + 1])));
-            const float t0 = bf16_rne(__fmul_rn(bf16_rne(s0), __fmul_rn(xa(i), xb(2 * j))));
-            const float t1 = bf16_rne(__fmul_rn(bf16_rne(s1), __fmul_rn(xa(i), xb(2 * j + 1))));
-            const float c0 = bf16_rne(__fadd_rn(unpack_hi(Cp[i][j]), t0));
-            const float c1 = bf16_rne(__fadd_rn(unpack_lo(Cp[i][j]), t1));
-            Cp[i][j] = pack_bf16(c0, c1);
+            const uint32_t c = bf16x2_rne(s0, s1);                 // S4: the tree's bf16 lane
+            const uint32_t t = bf16x2_rne(__fmul_rn(unpack_hi(c), __fmul_rn(xa(i), xb(2 * j))),
+                                          __fmul_rn(unpack_lo(c), __fmul_rn(xa(i), xb(2 * j + 1))));
+            Cp[i][j] = bf16x2_rne(__fadd_rn(unpack_hi(Cp[i][j]), unpack_hi(t)),
+                                  __fadd_rn(unpack_lo(Cp[i][j]), unpack_lo(t)));
           }
       }
     } else {
