@@ -173,6 +173,10 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     for (int s = 0; s < STAGES; s++) mbar_init(&bars[s], 1);
     fence_mbar_init();
   }
+  // launched as a programmatic dependent of the kernel before it on the stream: everything above overlaps that
+  // kernel's last CTAs; no global memory is read or written before it has completed and flushed
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();
   if (tid == 0)
     for (int s = 0; s < STAGES; s++)
@@ -301,7 +305,18 @@ int launch(const CUtensorMap& map, bool cols, float* P, float* X, int64_t outer,
   if (per_sm < 0) return -per_sm;
   int64_t grid = (int64_t)sm_count() * per_sm;
   if (grid > ntiles) grid = ntiles;
-  kern<<<(unsigned)grid, NT, smem, st>>>(map, P, X, outer, len, inner, prm);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;     // may start while the previous kernel drains
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (int r = check_cuda(cudaLaunchKernelEx(&cfg, kern, map, P, X, outer, len, inner, prm), "block_quantize"))
+    return r;
   return MXQ_LAUNCH_CHECK("block_quantize");
 }
 
