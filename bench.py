@@ -204,6 +204,51 @@ def run_gpu(args):
     kname = f"{dom[0]}/axis{dom[1]}"
     tr = traffic_table().get(kname)
 
+    # -- the compact form: the OCP-grid families' sweep writing byte codes and E8M0 scales, through the C ABI (the
+    # Python call reads its status word after every launch; the bench reads one at the end)
+    import ctypes
+    from mxq import _lib
+    from mxq.block import mxgemmini as _mg, ocp as _oc
+    pk_runs = [(f, fmt, ax) for f in ("mxgemmini", "ocp") for fmt in FORMATS for ax in (0, 1)]
+    pk_st = torch.zeros(1, dtype=torch.int32, device=dev)
+    pk_out = {}
+    for f, fmt, ax in pk_runs:
+        spec = (_mg.spec(fmt) if f == "mxgemmini" else _oc.spec(fmt))
+        fe = spec.e + spec.m
+        codes = torch.empty((ROWS, COLS // 2 if fe == 3 else COLS), dtype=torch.uint8, device=dev)
+        scales = torch.empty((ROWS // 32, COLS) if ax == 0 else (ROWS, COLS // 32), dtype=torch.uint8, device=dev)
+        lay = (1, ROWS, COLS) if ax == 0 else (ROWS, COLS, 1)
+        pk_out[(f, fmt, ax)] = (spec, codes, scales, lay, fe)
+
+    def pk_step():
+        for run in pk_runs:
+            spec, codes, scales, lay, _ = pk_out[run]
+            _lib.call("mxq_block_quantize_packed", _lib.ptr(V), _lib.ptr(codes), _lib.ptr(scales), *lay, 32,
+                      ctypes.byref(spec), _lib.ptr(pk_st), ctypes.c_void_p(stream.cuda_stream))
+
+    for _ in range(args.warmup):
+        pk_step()
+    barrier()
+    pk_steps = max(1, min(args.steps, 100))
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    for _ in range(pk_steps):
+        pk_step()
+    p1.record(stream)
+    barrier()
+    if int(pk_st.item()):
+        raise RuntimeError("bench: the compact sweep reported a value the form cannot hold")
+    pk_ms = max_over_ranks(p0.elapsed_time(p1)) / pk_steps
+    pk_bytes = sum(elems * (4 + (0.5 if pk_out[r][4] == 3 else 1.0) + 1 / 32) for r in pk_runs) * world
+    packed = {"workload": "compact form: block.{mxgemmini,ocp}.quantize_packed x 5 MX formats x axis {0,1} on the "
+                          "same matrix (uint8 OCP codes, FP4 two a byte, E8M0 scale bytes), C ABI",
+              "GB/s": round(pk_bytes / (pk_ms * 1e-3) / 1e9, 1),
+              "Gelem/s": round(elems * len(pk_runs) * world / (pk_ms * 1e-3) / 1e9, 1),
+              "float32 path Gelem/s": round(elems * len(runs) * world / (ms_step * 1e-3) / 1e9, 1),
+              "ms_per_step": round(pk_ms, 4), "launches_per_step": len(pk_runs), "steps": pk_steps,
+              "bytes_per_element": "4 read + 1 code (FP4 0.5) + 1/32 scale"}
+    del pk_out
+
     # -- end to end through the public API with host tensors: each call streams its pinned host V through the
     # device and returns pinned host P, X (copies in and out on their own streams, overlapping the kernels); the
     # call returns once the results are on the host, so the host clock brackets the whole transfer
@@ -384,6 +429,7 @@ def run_gpu(args):
                                     "GB/s counts 8.125 B/element for block.lut, 4 tables, 12 pick, 16 finder",
                         "steps": args.extra_steps, **extra},
         "model": model_out,
+        "packed": packed,
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu

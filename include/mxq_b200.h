@@ -115,6 +115,22 @@ typedef struct mxq_quant_spec {
  * element rounding in one pass. */
 int mxq_block_quantize(const float* V, float* P, float* X, int64_t outer, int64_t len, int64_t inner, int64_t block,
                        const mxq_quant_spec* spec, void* stream);
+/* No reference counterpart: the compact operand form (the wire format of MX-Gemmini's LUT indices,
+ * mxq/lut/__init__.py:3-6). mxq_block_quantize for the OCP-grid families (mxgemmini without `via`, and ocp) writing
+ * each code as its element format's OCP bit pattern -- a byte per FP8 / FP6 element (FP6 in the low six bits), two
+ * FP4 elements per byte (the even element in the low nibble) -- in P's layout, and each scale as an E8M0 byte
+ * (2^(b - 127), 0xFF NaN) in X's layout. status bits: 1 a code the format cannot hold (Inf in E4M3 / FP6 / FP4,
+ * NaN in FP6 / FP4), 2 a scale that is not a power of two in [2^-127, 2^127] (mxgemmini's floor for an all-zero
+ * block, below it). Blocks of 32, rows (the innermost extent) a multiple of 4, 16-byte aligned V and codes. */
+int mxq_block_quantize_packed(const float* V, uint8_t* codes, uint8_t* scales, int64_t outer, int64_t len,
+                              int64_t inner, int64_t block, const mxq_quant_spec* spec, int32_t* status,
+                              void* stream);
+/* No reference counterpart: float32 codes and scales from the compact form (n_codes elements, n_scales scales) */
+int mxq_unpack(const uint8_t* codes, const uint8_t* scales, float* P, float* X, int64_t n_codes, int64_t n_scales,
+               int32_t e, int32_t m, void* stream);
+/* No reference counterpart: mxq_dequantize from the compact form */
+int mxq_dequantize_packed(const uint8_t* codes, const uint8_t* scales, float* out, int64_t outer, int64_t len,
+                          int64_t inner, int64_t block, int32_t e, int32_t m, void* stream);
 /* The pieces of compose with caller-supplied steps (mxq/block/_driver.py:23-42, :63-64): the blocked layout is
  * [outer, inner, nblocks, block] (the block axis moved last, zero-padded). */
 int mxq_block_amax(const float* V, float* amax, int64_t outer, int64_t len, int64_t inner, int64_t block,

@@ -117,9 +117,98 @@ __device__ __forceinline__ float divide(float v, float x, float r) {
   return FAM == MXQ_FAMILY_MXQUANT ? x86_div(v, x) : div_rn(v, x);
 }
 
+// Where a kernel puts its results. OutF: float32 codes and scales (the reference's outputs). OutPack: the compact
+// form -- each code as its OCP bit pattern (a byte; FP4: a nibble, two per byte, the even element low) and each
+// scale as an E8M0 byte -- with a flag for any value the form cannot hold. Element index idx is a multiple of 4.
+struct OutF {
+  float* P;
+  float* X;
+  template <bool FINITE = false>
+  __device__ __forceinline__ void codes(int64_t idx, float4 v) { __stcs(reinterpret_cast<float4*>(P + idx), v); }
+  __device__ __forceinline__ void scale(int64_t idx, float x) { X[idx] = x; }
+  __device__ __forceinline__ void finish() {}
+};
+
+// an OCP element code's bit pattern (sign at bit E + M); `bad` set for what the format lacks (Inf, and NaN in FP6 /
+// FP4; E4M3 keeps NaN as S.1111.111, E5M2 Inf as S.11111.00 and NaN as S.11111.11)
+template <int E, int M>
+__device__ __forceinline__ uint32_t ocp_code(float v, bool& bad) {
+  constexpr int BIAS = (1 << (E - 1)) - 1;
+  const uint32_t u = f2u(v), a = u & 0x7fffffffu, s = (u >> 31) << (E + M);
+  if (a >= 0x7f800000u) {
+    if (E == 5 && M == 2) return s | (a == 0x7f800000u ? 0x7cu : 0x7fu);
+    if (E == 4 && M == 3 && a > 0x7f800000u) return s | 0x7fu;
+    bad = true;
+    return s;
+  }
+  const int ev = (int)(a >> 23) - 127;
+  uint32_t c;
+  if (ev >= 1 - BIAS) {
+    c = ((uint32_t)(ev + BIAS) << M) | ((a >> (23 - M)) & ((1u << M) - 1u));
+  } else {                                     // below the format's normal range: a multiple of its subnormal step
+    const int sh = 24 - BIAS - M - ev;
+    c = a == 0u ? 0u : (((a & 0x007fffffu) | 0x00800000u) >> (sh < 31 ? sh : 31));
+  }
+  return s | c;
+}
+
+__device__ __forceinline__ uint32_t e8m0(float x, bool& bad) {     // 2^(b - 127); 0xFF NaN
+  const uint32_t u = f2u(x);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0xffu;
+  if (u == 0x00400000u) return 0u;                                  // 2^-127
+  if ((u & 0x807fffffu) == 0u && u >= 0x00800000u && u < 0x7f800000u) return u >> 23;
+  bad = true;                                                       // not a power of two the byte can hold
+  return 0u;
+}
+
+// the same for a finite code on the format's grid (a clean tile's), branch-free: a normal code's bits are the
+// float's exponent and top mantissa bits re-biased; a code below the normal range is the integer |v| / 2^(1-BIAS-M),
+// read from a float add at 2^23
+template <int E, int M>
+__device__ __forceinline__ uint32_t ocp_code_finite(float v) {
+  constexpr int BIAS = (1 << (E - 1)) - 1;
+  constexpr uint32_t MIN_NORMAL = (uint32_t)(128 - BIAS) << 23;
+  const uint32_t u = f2u(v), a = u & 0x7fffffffu;
+  const uint32_t normal = (a >> (23 - M)) - ((uint32_t)(127 - BIAS) << M);
+  const float scaled = __fmul_rn(u2f(a), u2f((uint32_t)(126 + BIAS + M) << 23));      // |v| * 2^(BIAS - 1 + M)
+  const uint32_t sub = f2u(__fadd_rn(scaled, 8388608.0f)) - 0x4b000000u;
+  return ((u >> 31) << (E + M)) | (a >= MIN_NORMAL ? normal : sub);
+}
+
+template <int E, int M>
+struct OutPack {
+  uint8_t* P;
+  uint8_t* X;
+  int* status;
+  bool bad_code = false, bad_scale = false;
+  template <bool FINITE = false>
+  __device__ __forceinline__ void codes(int64_t idx, float4 v) {
+    uint32_t c0, c1, c2, c3;
+    if (FINITE) {
+      c0 = ocp_code_finite<E, M>(v.x);
+      c1 = ocp_code_finite<E, M>(v.y);
+      c2 = ocp_code_finite<E, M>(v.z);
+      c3 = ocp_code_finite<E, M>(v.w);
+    } else {
+      c0 = ocp_code<E, M>(v.x, bad_code);
+      c1 = ocp_code<E, M>(v.y, bad_code);
+      c2 = ocp_code<E, M>(v.z, bad_code);
+      c3 = ocp_code<E, M>(v.w, bad_code);
+    }
+    if (E + M == 3) __stcs(reinterpret_cast<unsigned short*>(P + idx / 2),
+                           (unsigned short)(c0 | (c1 << 4) | (c2 << 8) | (c3 << 12)));
+    else __stcs(reinterpret_cast<unsigned int*>(P + idx), c0 | (c1 << 8) | (c2 << 16) | (c3 << 24));
+  }
+  __device__ __forceinline__ void scale(int64_t idx, float x) { X[idx] = (uint8_t)e8m0(x, bad_scale); }
+  __device__ __forceinline__ void finish() {
+    const int bits = (bad_code ? 1 : 0) | (bad_scale ? 2 : 0);
+    if (bits) atomicOr(status, bits);
+  }
+};
+
 // (2) for a clean tile: every thread quantizes TR / RPI float4 (float4 q = tid + NT i: row q / C4, column q % C4)
-template <int FAM, int E, int M, bool COLS, int MODE>
-__device__ __forceinline__ void pass_clean(const float* T, const float* s_r, float* __restrict__ P, int64_t rest,
+template <int FAM, int E, int M, bool COLS, int MODE, class Out>
+__device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out& out, int64_t rest,
                                            int64_t ct, int64_t nb, int64_t outer, int64_t len, int64_t inner) {
   const int tid = threadIdx.x, c4 = tid % C4;
   float4 rs;
@@ -138,18 +227,17 @@ __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, flo
     v.w = element_clean<FAM, E, M, MODE>(__fmul_rn(v.w, rs.w));
     if (COLS) {
       const int64_t b = rest % nb, o = rest / nb, l = b * TR + row, col = ct * TC + c4 * 4;
-      if (l < len && col < inner) __stcs(reinterpret_cast<float4*>(P + (o * len + l) * inner + col), v);
+      if (l < len && col < inner) out.template codes<true>((o * len + l) * inner + col, v);
     } else {
       const int64_t grow = rest * TR + row, col = ct * TC + c4 * 4;
-      if (grow < outer && col < len) __stcs(reinterpret_cast<float4*>(P + grow * len + col), v);
+      if (grow < outer && col < len) out.template codes<true>(grow * len + col, v);
     }
   }
 }
 
-template <int FAM, int E, int M, bool COLS>
-__global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtensorMap tmap, float* __restrict__ P,
-                                                  float* __restrict__ X, int64_t outer, int64_t len, int64_t inner,
-                                                  TParams prm) {
+template <int FAM, int E, int M, bool COLS, class Out>
+__global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtensorMap tmap, Out out, int64_t outer,
+                                                  int64_t len, int64_t inner, TParams prm) {
   extern __shared__ __align__(128) float tiles[];            // [STAGES][TR][TC]
   __shared__ __align__(8) uint64_t bars[STAGES];
   __shared__ float s_x[TC], s_r[TC];
@@ -186,7 +274,10 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
   for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, k++) {
     const int stage = k % STAGES;
     // every thread waits; the CTA leaves together if the (bounded) wait gave up anywhere
-    if (!__syncthreads_and(mbar_wait(&bars[stage], (unsigned)(k / STAGES) & 1u))) return;
+    if (!__syncthreads_and(mbar_wait(&bars[stage], (unsigned)(k / STAGES) & 1u))) {
+      out.finish();
+      return;
+    }
     const float* T = tiles + stage * TR * TC;
     const int64_t ct = tile % ctiles, rest = tile / ctiles;
 
@@ -204,7 +295,7 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
       s_x[tid] = x;
       s_r[tid] = r;
       bad = col < inner && (mbits >= 0x7f800000u || r == 0.0f);     // padding columns do not vote
-      if (col < inner) X[(o * nb + b) * inner + col] = x;
+      if (col < inner) out.scale((o * nb + b) * inner + col, x);
     } else {
       const int row = tid / BPR, blk = tid % BPR;            // TR rows x BPR blocks
       const float4* src = reinterpret_cast<const float4*>(T + row * TC + blk * 32);
@@ -222,17 +313,17 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
       s_r[tid] = r;
       const int64_t grow = rest * TR + row, gblk = ct * (TC / 32) + blk;
       bad = grow < outer && gblk < nb && (mbits >= 0x7f800000u || r == 0.0f);   // padding blocks do not vote
-      if (grow < outer && gblk < nb) X[grow * nb + gblk] = x;
+      if (grow < outer && gblk < nb) out.scale(grow * nb + gblk, x);
     }
     const bool clean = !__syncthreads_or(bad);              // the whole tile takes the short element step
 
     if (clean) {
       if (FAM == MXQ_FAMILY_MXQUANT || prm.rounding == 0)
-        pass_clean<FAM, E, M, COLS, 0>(T, s_r, P, rest, ct, nb, outer, len, inner);
+        pass_clean<FAM, E, M, COLS, 0>(T, s_r, out, rest, ct, nb, outer, len, inner);
       else if (prm.rounding == 1)
-        pass_clean<FAM, E, M, COLS, 1>(T, s_r, P, rest, ct, nb, outer, len, inner);
+        pass_clean<FAM, E, M, COLS, 1>(T, s_r, out, rest, ct, nb, outer, len, inner);
       else
-        pass_clean<FAM, E, M, COLS, 2>(T, s_r, P, rest, ct, nb, outer, len, inner);
+        pass_clean<FAM, E, M, COLS, 2>(T, s_r, out, rest, ct, nb, outer, len, inner);
       __syncthreads();                                      // every thread is done with this stage and s_x / s_r
       if (tid == 0 && tile + (int64_t)STAGES * gridDim.x < ntiles) issue(tile + (int64_t)STAGES * gridDim.x, stage);
       continue;
@@ -261,20 +352,21 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
       v.w = element<FAM, E, M>(divide<FAM>(v.w, xs.w, rs.w), prm);
       if (COLS) {
         const int64_t b = rest % nb, o = rest / nb, l = b * TR + row, col = ct * TC + c4 * 4;
-        if (l < len && col < inner) __stcs(reinterpret_cast<float4*>(P + (o * len + l) * inner + col), v);
+        if (l < len && col < inner) out.codes((o * len + l) * inner + col, v);
       } else {
         const int64_t grow = rest * TR + row, col = ct * TC + c4 * 4;
-        if (grow < outer && col < len) __stcs(reinterpret_cast<float4*>(P + grow * len + col), v);
+        if (grow < outer && col < len) out.codes(grow * len + col, v);
       }
     }
     __syncthreads();                                        // every thread is done with this stage and s_x / s_r
     if (tid == 0 && tile + (int64_t)STAGES * gridDim.x < ntiles) issue(tile + (int64_t)STAGES * gridDim.x, stage);
   }
+  out.finish();
 }
 
 // CTAs per SM of one kernel on the current device, with its shared-memory attribute set: done once per kernel and
 // device (the attribute is per device), then read from the cache.
-template <int FAM, int E, int M, bool COLS>
+template <int FAM, int E, int M, bool COLS, class Out>
 int ctas_per_sm(size_t smem) {
   static std::atomic<int> cache[kMaxDevices];
   int dev = 0;
@@ -282,7 +374,7 @@ int ctas_per_sm(size_t smem) {
   if (dev < 0 || dev >= kMaxDevices) return -set_error(MXQ_ERR_UNSUPPORTED, "block_quantize: device %d", dev);
   int per_sm = cache[dev].load(std::memory_order_relaxed);
   if (per_sm > 0) return per_sm;
-  auto kern = k_quant_tma<FAM, E, M, COLS>;
+  auto kern = k_quant_tma<FAM, E, M, COLS, Out>;
   if (int r = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                          "block_quantize: shared memory attribute"))
     return -r;
@@ -294,14 +386,14 @@ int ctas_per_sm(size_t smem) {
   return per_sm;
 }
 
-template <int FAM, int E, int M>
-int launch(const CUtensorMap& map, bool cols, float* P, float* X, int64_t outer, int64_t len, int64_t inner,
+template <int FAM, int E, int M, class Out>
+int launch(const CUtensorMap& map, bool cols, Out out, int64_t outer, int64_t len, int64_t inner,
            const TParams& prm, cudaStream_t st) {
   const int64_t nb = (len + TR - 1) / TR;
   const int64_t ntiles = cols ? outer * nb * ((inner + TC - 1) / TC) : ((outer + TR - 1) / TR) * ((len + TC - 1) / TC);
   const size_t smem = STAGES * TILE_BYTES;
-  auto kern = cols ? k_quant_tma<FAM, E, M, true> : k_quant_tma<FAM, E, M, false>;
-  const int per_sm = cols ? ctas_per_sm<FAM, E, M, true>(smem) : ctas_per_sm<FAM, E, M, false>(smem);
+  auto kern = cols ? k_quant_tma<FAM, E, M, true, Out> : k_quant_tma<FAM, E, M, false, Out>;
+  const int per_sm = cols ? ctas_per_sm<FAM, E, M, true, Out>(smem) : ctas_per_sm<FAM, E, M, false, Out>(smem);
   if (per_sm < 0) return -per_sm;
   int64_t grid = (int64_t)sm_count() * per_sm;
   if (grid > ntiles) grid = ntiles;
@@ -315,19 +407,36 @@ int launch(const CUtensorMap& map, bool cols, float* P, float* X, int64_t outer,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (int r = check_cuda(cudaLaunchKernelEx(&cfg, kern, map, P, X, outer, len, inner, prm), "block_quantize"))
+  if (int r = check_cuda(cudaLaunchKernelEx(&cfg, kern, map, out, outer, len, inner, prm), "block_quantize"))
     return r;
   return MXQ_LAUNCH_CHECK("block_quantize");
 }
 
+// the float32 outputs (packed == nullptr) or the compact ones
+struct Dest {
+  float* P;
+  float* X;
+  uint8_t* Pc;
+  uint8_t* Xc;
+  int* status;
+};
+
+template <int FAM, int E, int M>
+int launch_dest(const CUtensorMap& map, bool cols, const Dest& d, int64_t outer, int64_t len, int64_t inner,
+                const TParams& prm, cudaStream_t st) {
+  if (d.Pc == nullptr) return launch<FAM, E, M>(map, cols, OutF{d.P, d.X}, outer, len, inner, prm, st);
+  if (FAM == MXQ_FAMILY_MXQUANT) return MXQ_ERR_UNSUPPORTED;          // the qtorch grid is not the OCP one
+  return launch<FAM, E, M>(map, cols, OutPack<E, M>{d.Pc, d.Xc, d.status}, outer, len, inner, prm, st);
+}
+
 template <int FAM>
-int launch_fmt(int e, int m, const CUtensorMap& map, bool cols, float* P, float* X, int64_t outer, int64_t len,
+int launch_fmt(int e, int m, const CUtensorMap& map, bool cols, const Dest& d, int64_t outer, int64_t len,
                int64_t inner, const TParams& prm, cudaStream_t st) {
-  if (e == 4 && m == 3) return launch<FAM, 4, 3>(map, cols, P, X, outer, len, inner, prm, st);
-  if (e == 5 && m == 2) return launch<FAM, 5, 2>(map, cols, P, X, outer, len, inner, prm, st);
-  if (e == 3 && m == 2) return launch<FAM, 3, 2>(map, cols, P, X, outer, len, inner, prm, st);
-  if (e == 2 && m == 3) return launch<FAM, 2, 3>(map, cols, P, X, outer, len, inner, prm, st);
-  if (e == 2 && m == 1) return launch<FAM, 2, 1>(map, cols, P, X, outer, len, inner, prm, st);
+  if (e == 4 && m == 3) return launch_dest<FAM, 4, 3>(map, cols, d, outer, len, inner, prm, st);
+  if (e == 5 && m == 2) return launch_dest<FAM, 5, 2>(map, cols, d, outer, len, inner, prm, st);
+  if (e == 3 && m == 2) return launch_dest<FAM, 3, 2>(map, cols, d, outer, len, inner, prm, st);
+  if (e == 2 && m == 3) return launch_dest<FAM, 2, 3>(map, cols, d, outer, len, inner, prm, st);
+  if (e == 2 && m == 1) return launch_dest<FAM, 2, 1>(map, cols, d, outer, len, inner, prm, st);
   return MXQ_ERR_UNSUPPORTED;
 }
 
@@ -337,13 +446,14 @@ namespace mxq {
 
 // The TMA kernel for blocks of 32 when the layout allows a tensor map (16-byte aligned base, rows a multiple of 16
 // bytes, extents below 2^31); MXQ_ERR_UNSUPPORTED otherwise (the caller then takes the register kernels).
-int quantize_tma(const float* V, float* P, float* X, int64_t outer, int64_t len, int64_t inner, int64_t block,
-                 const mxq_quant_spec& s, cudaStream_t st) {
+int quantize_tma_dest(const float* V, const Dest& d, int64_t outer, int64_t len, int64_t inner, int64_t block,
+                      const mxq_quant_spec& s, cudaStream_t st) {
   if (block != 32 || s.family == MXQ_FAMILY_FP32 || (s.family == MXQ_FAMILY_MXGEMMINI && s.via_e != 0))
     return MXQ_ERR_UNSUPPORTED;
   const bool cols = inner > 1;
   const int64_t rowlen = cols ? inner : len;
-  if ((uintptr_t)V % 16 || (uintptr_t)P % 16 || rowlen % 4 || outer >= (1ll << 31) || len >= (1ll << 31) ||
+  const uintptr_t out_base = d.Pc ? (uintptr_t)d.Pc : (uintptr_t)d.P;
+  if ((uintptr_t)V % 16 || out_base % 16 || rowlen % 4 || outer >= (1ll << 31) || len >= (1ll << 31) ||
       inner >= (1ll << 31))
     return MXQ_ERR_UNSUPPORTED;
   CUtensorMap map;
@@ -360,11 +470,21 @@ int quantize_tma(const float* V, float* P, float* X, int64_t outer, int64_t len,
   }
   TParams prm{s.rounding, s.placement, s.via_e, s.via_m, s.scale_floor, s.scale_emax};
   switch (s.family) {
-    case MXQ_FAMILY_MXQUANT: return launch_fmt<MXQ_FAMILY_MXQUANT>(s.e, s.m, map, cols, P, X, outer, len, inner, prm, st);
+    case MXQ_FAMILY_MXQUANT: return launch_fmt<MXQ_FAMILY_MXQUANT>(s.e, s.m, map, cols, d, outer, len, inner, prm, st);
     case MXQ_FAMILY_MXGEMMINI:
-      return launch_fmt<MXQ_FAMILY_MXGEMMINI>(s.e, s.m, map, cols, P, X, outer, len, inner, prm, st);
-    default: return launch_fmt<MXQ_FAMILY_OCP>(s.e, s.m, map, cols, P, X, outer, len, inner, prm, st);
+      return launch_fmt<MXQ_FAMILY_MXGEMMINI>(s.e, s.m, map, cols, d, outer, len, inner, prm, st);
+    default: return launch_fmt<MXQ_FAMILY_OCP>(s.e, s.m, map, cols, d, outer, len, inner, prm, st);
   }
+}
+
+int quantize_tma(const float* V, float* P, float* X, int64_t outer, int64_t len, int64_t inner, int64_t block,
+                 const mxq_quant_spec& s, cudaStream_t st) {
+  return quantize_tma_dest(V, Dest{P, X, nullptr, nullptr, nullptr}, outer, len, inner, block, s, st);
+}
+
+int quantize_tma_packed(const float* V, uint8_t* Pc, uint8_t* Xc, int* status, int64_t outer, int64_t len,
+                        int64_t inner, int64_t block, const mxq_quant_spec& s, cudaStream_t st) {
+  return quantize_tma_dest(V, Dest{nullptr, nullptr, Pc, Xc, status}, outer, len, inner, block, s, st);
 }
 
 }  // namespace mxq

@@ -6,7 +6,7 @@
 
 The named quantizers run as one fused CUDA kernel each (read V once, write P and X once).
 """
-from ._driver import BLOCK, compose, dequantize
+from ._driver import BLOCK, compose, dequantize, dequantize_packed, unpack
 from . import mxquant, mxgemmini, ocp, lut
 
-__all__ = ["BLOCK", "compose", "dequantize", "mxquant", "mxgemmini", "ocp", "lut"]
+__all__ = ["BLOCK", "compose", "dequantize", "mxquant", "mxgemmini", "ocp", "lut", "unpack", "dequantize_packed"]

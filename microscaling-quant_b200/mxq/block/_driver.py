@@ -236,3 +236,81 @@ def dequantize(P: torch.Tensor, X: torch.Tensor, axis: int = 0, block_size: int 
     out = torch.empty_like(p)
     _lib.run("mxq_dequantize", dev, _lib.ptr(p), _lib.ptr(x), _lib.ptr(out), outer, L, inner, block_size)
     return _lib.back(out, home)
+
+
+# ---------------------------------------------------------------------------------------- compact form
+def _packed_shape(shape, e: int, m: int):
+    """The codes tensor of the compact form: P's shape, the innermost extent halved for FP4 (two codes a byte)."""
+    shape = list(shape)
+    if e + m == 3:
+        if not shape or shape[-1] % 2:
+            raise ValueError(f"compact FP4 codes pair up along the innermost dimension, which is {shape[-1:]}")
+        shape[-1] //= 2
+    return shape
+
+
+def quantize_packed(V: torch.Tensor, spec: "_lib.MxqQuantSpec", axis: int, block_size: int):
+    """A named quantizer's codes and scales in the compact form (no reference counterpart): codes as the element
+    format's OCP bit patterns (uint8; FP4 two per byte, the even element low) in P's layout, scales as E8M0 bytes
+    (2^(b - 127), 0xFF NaN) in X's layout. ValueError when a code or a scale has no such byte."""
+    import ctypes
+    axis_, outer, L, inner, nb = _layout(V, axis, block_size)
+    _check_reshape(V, axis_, block_size)
+    home = _lib.home(V)
+    dev = _lib.device_for(V)
+    v = _lib.on(V, dev)
+    codes = torch.empty(_packed_shape(V.shape, spec.e, spec.m), dtype=torch.uint8, device=dev)
+    xshape = list(V.shape)
+    xshape[axis_] = nb
+    scales = torch.empty(xshape, dtype=torch.uint8, device=dev)
+    st = torch.empty(1, dtype=torch.int32, device=dev)
+    _lib.run("mxq_block_quantize_packed", dev, _lib.ptr(v), _lib.ptr(codes), _lib.ptr(scales), outer, L, inner,
+             block_size, ctypes.byref(spec), _lib.ptr(st))
+    bits = int(st.item())
+    if bits & 1:
+        raise ValueError("compact form: a code is Inf or NaN, which this element format cannot hold")
+    if bits & 2:
+        raise ValueError("compact form: a scale is not a power of two an E8M0 byte can hold (an all-zero block "
+                         "under the scale floor?)")
+    return _lib.back(codes, home), _lib.back(scales, home)
+
+
+def unpack(codes: torch.Tensor, scales: torch.Tensor, fmt) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(P, X) float32 from the compact form, codes in P's layout (FP4: two per byte) and scales in X's."""
+    from ..element_quant.formats import get
+    f = get(fmt)
+    if f is None or codes.dtype != torch.uint8 or scales.dtype != torch.uint8:
+        raise ValueError("unpack: uint8 codes and scales of an MX element format")
+    home = _lib.home(codes)
+    dev = _lib.device_for(codes, scales)
+    c, x = codes.to(dev).contiguous(), scales.to(dev).contiguous()
+    shape = list(c.shape)
+    if f.e + f.m == 3:
+        shape[-1] *= 2
+    P = torch.empty(shape, dtype=torch.float32, device=dev)
+    X = torch.empty(x.shape, dtype=torch.float32, device=dev)
+    _lib.run("mxq_unpack", dev, _lib.ptr(c), _lib.ptr(x), _lib.ptr(P), _lib.ptr(X), P.numel(), X.numel(), f.e, f.m)
+    return _lib.back(P, home), _lib.back(X, home)
+
+
+def dequantize_packed(codes: torch.Tensor, scales: torch.Tensor, fmt, axis: int = 0,
+                      block_size: int = BLOCK) -> torch.Tensor:
+    """dequantize straight from the compact form: each code's value times its block's scale, float32."""
+    from ..element_quant.formats import get
+    f = get(fmt)
+    if f is None or codes.dtype != torch.uint8 or scales.dtype != torch.uint8:
+        raise ValueError("dequantize_packed: uint8 codes and scales of an MX element format")
+    shape = list(codes.shape)
+    if f.e + f.m == 3:
+        shape[-1] *= 2
+    ref = torch.empty(shape, dtype=torch.float32, device="meta")
+    axis_, outer, L, inner, nb = _layout(ref, axis, block_size)
+    home = _lib.home(codes)
+    dev = _lib.device_for(codes, scales)
+    c, x = codes.to(dev).contiguous(), scales.to(dev).contiguous()
+    if x.numel() != outer * nb * inner:
+        raise ValueError(f"dequantize_packed: scales of shape {tuple(scales.shape)} do not match codes {tuple(shape)}")
+    out = torch.empty(shape, dtype=torch.float32, device=dev)
+    _lib.run("mxq_dequantize_packed", dev, _lib.ptr(c), _lib.ptr(x), _lib.ptr(out), outer, L, inner, block_size, f.e,
+             f.m)
+    return _lib.back(out, home)

@@ -35,5 +35,13 @@ def quantize(V: torch.Tensor, fmt: Union[str, Format], axis: int = 0, block_size
     return _driver.quantize_fused(V, spec(fmt, rounding_mode, scale_bits, placement), axis, block_size)
 
 
+def quantize_packed(V: torch.Tensor, fmt: Union[str, Format], axis: int = 0, block_size: int = _driver.BLOCK,
+                    rounding_mode: str = "even", scale_bits: int = 8,
+                    placement: str = "top") -> Tuple[torch.Tensor, torch.Tensor]:
+    """quantize's codes and scales in the compact form (no reference counterpart): uint8 OCP bit patterns (FP4 two
+    per byte) and E8M0 scale bytes; block.unpack gives back exactly quantize's (P, X)."""
+    return _driver.quantize_packed(V, spec(fmt, rounding_mode, scale_bits, placement), axis, block_size)
+
+
 def dequantize(P: torch.Tensor, X: torch.Tensor, axis: int = 0, block_size: int = _driver.BLOCK) -> torch.Tensor:
     return _driver.dequantize(P, X, axis, block_size)
