@@ -206,10 +206,31 @@ struct OutPack {
   }
 };
 
+// A tile's coordinates, from its index by 32-bit division once per tile: column tile ct, and rest = the row tile
+// (ROWS) or (o, b) = the outer slice and block (COLS). Tile counts stay below 2^31 (the launch checks).
+struct TileAt {
+  int64_t ct, rest, b, o;
+};
+template <bool COLS>
+__device__ __forceinline__ TileAt tile_at(int64_t tile, uint32_t ctiles, uint32_t nb) {
+  TileAt t;
+  const uint32_t i = (uint32_t)tile, rest = i / ctiles;
+  t.ct = i - rest * ctiles;
+  t.rest = rest;
+  if (COLS) {
+    const uint32_t o = rest / nb;
+    t.o = o;
+    t.b = rest - o * nb;
+  } else {
+    t.o = t.b = 0;
+  }
+  return t;
+}
+
 // (2) for a clean tile: every thread quantizes TR / RPI float4 (float4 q = tid + NT i: row q / C4, column q % C4)
 template <int FAM, int E, int M, bool COLS, int MODE, class Out>
-__device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out& out, int64_t rest,
-                                           int64_t ct, int64_t nb, int64_t outer, int64_t len, int64_t inner) {
+__device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out& out, const TileAt& at,
+                                           int64_t outer, int64_t len, int64_t inner) {
   const int tid = threadIdx.x, c4 = tid % C4;
   float4 rs;
   if (COLS) rs = *reinterpret_cast<const float4*>(s_r + c4 * 4);
@@ -226,10 +247,10 @@ __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out
     v.z = element_clean<FAM, E, M, MODE>(__fmul_rn(v.z, rs.z));
     v.w = element_clean<FAM, E, M, MODE>(__fmul_rn(v.w, rs.w));
     if (COLS) {
-      const int64_t b = rest % nb, o = rest / nb, l = b * TR + row, col = ct * TC + c4 * 4;
-      if (l < len && col < inner) out.template codes<true>((o * len + l) * inner + col, v);
+      const int64_t l = at.b * TR + row, col = at.ct * TC + c4 * 4;
+      if (l < len && col < inner) out.template codes<true>((at.o * len + l) * inner + col, v);
     } else {
-      const int64_t grow = rest * TR + row, col = ct * TC + c4 * 4;
+      const int64_t grow = at.rest * TR + row, col = at.ct * TC + c4 * 4;
       if (grow < outer && col < len) out.template codes<true>(grow * len + col, v);
     }
   }
@@ -248,13 +269,14 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
   const int64_t ctiles = COLS ? (inner + TC - 1) / TC : (len + TC - 1) / TC;
   const int64_t ntiles = COLS ? outer * nb * ctiles : ((outer + TR - 1) / TR) * ctiles;
 
+  const uint32_t ctiles32 = (uint32_t)ctiles, nb32 = (uint32_t)nb;
   auto issue = [&](int64_t tile, int stage) {
-    const int64_t ct = tile % ctiles, rest = tile / ctiles;
+    const TileAt at = tile_at<COLS>(tile, ctiles32, nb32);
     float* dst = tiles + stage * TR * TC;
     fence_proxy_async();
     mbar_expect_tx(&bars[stage], TILE_BYTES);
-    if (COLS) tma_load_3d(dst, &tmap, (int)(ct * TC), (int)((rest % nb) * TR), (int)(rest / nb), &bars[stage]);
-    else tma_load_2d(dst, &tmap, (int)(ct * TC), (int)(rest * TR), &bars[stage]);
+    if (COLS) tma_load_3d(dst, &tmap, (int)(at.ct * TC), (int)(at.b * TR), (int)at.o, &bars[stage]);
+    else tma_load_2d(dst, &tmap, (int)(at.ct * TC), (int)(at.rest * TR), &bars[stage]);
   };
 
   if (tid == 0) {
@@ -279,13 +301,14 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
       return;
     }
     const float* T = tiles + stage * TR * TC;
-    const int64_t ct = tile % ctiles, rest = tile / ctiles;
+    const TileAt at = tile_at<COLS>(tile, ctiles32, nb32);
+    const int64_t ct = at.ct, rest = at.rest;
 
     // (1) block scales: one thread per block of the tile (TC of them)
     bool bad = false;
     if (tid >= TC) {
     } else if (COLS) {
-      const int64_t b = rest % nb, o = rest / nb, col = ct * TC + tid;
+      const int64_t b = at.b, o = at.o, col = ct * TC + tid;
       uint32_t mbits = 0u;                                  // max |v| as bits: a NaN pattern tops every number
 #pragma unroll 8
       for (int r = 0; r < TR; r++) mbits = max(mbits, f2u(T[r * TC + tid]) & 0x7fffffffu);
@@ -319,11 +342,11 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
 
     if (clean) {
       if (FAM == MXQ_FAMILY_MXQUANT || prm.rounding == 0)
-        pass_clean<FAM, E, M, COLS, 0>(T, s_r, out, rest, ct, nb, outer, len, inner);
+        pass_clean<FAM, E, M, COLS, 0>(T, s_r, out, at, outer, len, inner);
       else if (prm.rounding == 1)
-        pass_clean<FAM, E, M, COLS, 1>(T, s_r, out, rest, ct, nb, outer, len, inner);
+        pass_clean<FAM, E, M, COLS, 1>(T, s_r, out, at, outer, len, inner);
       else
-        pass_clean<FAM, E, M, COLS, 2>(T, s_r, out, rest, ct, nb, outer, len, inner);
+        pass_clean<FAM, E, M, COLS, 2>(T, s_r, out, at, outer, len, inner);
       __syncthreads();                                      // every thread is done with this stage and s_x / s_r
       if (tid == 0 && tile + (int64_t)STAGES * gridDim.x < ntiles) issue(tile + (int64_t)STAGES * gridDim.x, stage);
       continue;
@@ -351,8 +374,8 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
       v.z = element<FAM, E, M>(divide<FAM>(v.z, xs.z, rs.z), prm);
       v.w = element<FAM, E, M>(divide<FAM>(v.w, xs.w, rs.w), prm);
       if (COLS) {
-        const int64_t b = rest % nb, o = rest / nb, l = b * TR + row, col = ct * TC + c4 * 4;
-        if (l < len && col < inner) out.codes((o * len + l) * inner + col, v);
+        const int64_t l = at.b * TR + row, col = ct * TC + c4 * 4;
+        if (l < len && col < inner) out.codes((at.o * len + l) * inner + col, v);
       } else {
         const int64_t grow = rest * TR + row, col = ct * TC + c4 * 4;
         if (grow < outer && col < len) out.codes(grow * len + col, v);
@@ -391,6 +414,7 @@ int launch(const CUtensorMap& map, bool cols, Out out, int64_t outer, int64_t le
            const TParams& prm, cudaStream_t st) {
   const int64_t nb = (len + TR - 1) / TR;
   const int64_t ntiles = cols ? outer * nb * ((inner + TC - 1) / TC) : ((outer + TR - 1) / TR) * ((len + TC - 1) / TC);
+  if (ntiles >= (1ll << 31)) return MXQ_ERR_UNSUPPORTED;   // the kernel's tile coordinates are 32-bit
   const size_t smem = STAGES * TILE_BYTES;
   auto kern = cols ? k_quant_tma<FAM, E, M, true, Out> : k_quant_tma<FAM, E, M, false, Out>;
   const int per_sm = cols ? ctas_per_sm<FAM, E, M, true, Out>(smem) : ctas_per_sm<FAM, E, M, false, Out>(smem);
