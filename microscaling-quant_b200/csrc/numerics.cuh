@@ -161,6 +161,15 @@ MXQ_HD float floor_small(float s) {
 #endif
 }
 MXQ_HD float rint_small(float s) { return sub_rn(add_rn(s, 8388608.0f), 8388608.0f); }
+// a + b rounded toward zero (the host form: the TwoSum error of the nearest sum says whether it overshot)
+MXQ_HD float add_rz(float a, float b) {
+#if defined(__CUDA_ARCH__)
+  return __fadd_rz(a, b);
+#else
+  const float r = a + b, bb = r - a, err = (a - (r - bb)) + (b - bb);     // a + b = r + err exactly
+  return (err != 0.0f && ((err < 0.0f) != (r < 0.0f))) ? nextafterf(r, 0.0f) : r;
+#endif
+}
 MXQ_HD double floor_d(double x) { return floor(x); }
 MXQ_HD double trunc_d(double x) { return trunc(x); }
 MXQ_HD double rint_d(double x) { return rint(x); }
@@ -597,6 +606,28 @@ MXQ_HD float q_ocp_bits(float x, int e, int m, int mode, float max_norm) {
   float r = u2f(f2u(val) | (u & 0x80000000u));
   return a == 0u ? 0.0f : (a >= 0x7f800000u ? x : r);
 }
+// A finite a >= 0 rounded to a multiple of the step q = 2^(E - 127 - m) by one float add, E << 23 = e23 the
+// binade's biased exponent field in place (a < 2^(E - 126)): C = 1.5 * 2^23 * q has ulp q and a is far below C's
+// binade width, so a + C lands on C + (a rounded to a multiple of q) in the add's own rounding (to nearest even, or
+// toward zero = down), and subtracting C is exact (Sterbenz). Ties away (RM_TIES_AWAY) first adds q / 2 rounded to
+// nearest, which is the reference's fl(a / q + 0.5) scaled by q, then rounds down. E - 127 - m + 23 must stay a
+// normal float32 exponent: a < 2^17 and E >= 106 keep it.
+MXQ_HD float step_round(float a, uint32_t e23, int m, int mode) {
+  const float c = u2f(e23 + (((uint32_t)(23 - m) << 23) | 0x400000u));
+  if (mode == RM_RNE) return sub_rn(add_rn(a, c), c);
+  if (mode == RM_TRUNCATE) return sub_rn(add_rz(a, c), c);
+  return sub_rn(add_rz(add_rn(a, u2f(e23 - ((uint32_t)(m + 1) << 23))), c), c);
+}
+// q_ocp_bits for finite |x| < 2^17 (a block quantizer's scaled value in a tile whose scales are powers of two):
+// the same grid, its rounding by step_round
+MXQ_HD float q_ocp_small(float x, int e, int m, int mode, float max_norm) {
+  const uint32_t u = f2u(x), a = u & 0x7fffffffu;
+  const uint32_t lo = (uint32_t)(128 - bias_of(e)) << 23;
+  const uint32_t e23 = (a & 0x7f800000u) > lo ? (a & 0x7f800000u) : lo;
+  const float val = fminf(step_round(u2f(a), e23, m, mode), max_norm);
+  return a == 0u ? 0.0f : u2f(f2u(val) | (u & 0x80000000u));
+}
+
 // q_microsoft with saturate_normals=True and exp_bits > 0
 MXQ_HD float q_microsoft_sat(float A, int bits, int exp_bits, float max_norm, int round) {
   uint32_t u = f2u(A), a = u & 0x7fffffffu;
@@ -653,6 +684,33 @@ MXQ_HD float q_microsoft_ocp_core(float A, int bits, int exp_bits, float max_nor
     r = add_rn(rint_small(t), f2u(t) == 0x3effffffu ? 1.0f : 0.0f);
   }
   const float val = fminf(mul_rn(r, u2f(e23 - ((uint32_t)(bits - 2) << 23))), max_norm);   // r * 2^(pe-bits+2)
+  return a == 0u ? 0.0f : u2f(f2u(val) | (u & 0x80000000u));
+}
+// q_microsoft_ocp_core for |A| < 2^17 with the rounding by step_round (step 2^(pe - bits + 2)): nearest is
+// floor(fl(t + 0.5)) = ties away, floor rounds down, and even is RNE except at t = 0.5 - 2^-25 (only reached with
+// pe clipped at min_exp, i.e. at one value of |A|), which rounds up to one step.
+MXQ_HD float q_microsoft_ocp_small(float A, int bits, int exp_bits, float max_norm, int round) {
+  const uint32_t u = f2u(A), a = u & 0x7fffffffu;
+  const int min_exp = 2 - (1 << (exp_bits - 1)), m = bits - 2;
+  const uint32_t lo = (uint32_t)(min_exp + 127) << 23;
+  uint32_t e23;
+  if (round == MS_FLOOR) {
+    int pe = a ? floor_log2_rn(u2f(a)) : 0;
+    e23 = (uint32_t)((pe > min_exp ? pe : min_exp) + 127) << 23;
+  } else {
+    e23 = (a & 0x7f800000u) > lo ? (a & 0x7f800000u) : lo;
+  }
+  float r;
+  if (round == MS_FLOOR) {
+    r = step_round(u2f(a), e23, m, RM_TRUNCATE);
+  } else if (round == MS_NEAREST) {
+    r = step_round(u2f(a), e23, m, RM_TIES_AWAY);
+  } else {
+    const uint32_t a_star = lo - ((uint32_t)(m + 2) << 23) + 0x7fffffu;     // (0.5 - 2^-25) * 2^(min_exp - m)
+    r = step_round(u2f(a), e23, m, RM_RNE);
+    if (a == a_star) r = u2f(lo - ((uint32_t)m << 23));
+  }
+  const float val = fminf(r, max_norm);
   return a == 0u ? 0.0f : u2f(f2u(val) | (u & 0x80000000u));
 }
 MXQ_HD float q_microsoft_ocp(float A, int bits, int exp_bits, float max_norm, int round) {

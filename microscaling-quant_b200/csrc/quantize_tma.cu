@@ -84,13 +84,13 @@ __device__ __forceinline__ float element(float z, const TParams& p) {
 }
 
 // The element step of a clean tile (every block finite, every scale a power of two with an exact reciprocal): z is
-// then finite and |z| < 2^17, so the Inf / NaN / huge-value branches cannot be taken, and the rounding mode is a
-// template argument.
+// then finite and |z| < 2^17, so the Inf / NaN / huge-value branches cannot be taken, the rounding is one float add
+// at the step's magic constant (q_ocp_small, q_microsoft_ocp_small), and the rounding mode is a template argument.
 template <int FAM, int E, int M, int MODE>
 __device__ __forceinline__ float element_clean(float z) {
   if (FAM == MXQ_FAMILY_MXQUANT) return qtorch_ties_away<E, M>(z);
-  if (FAM == MXQ_FAMILY_MXGEMMINI) return ocp_grid_core<E, M>(z, MODE);
-  return q_microsoft_ocp_core(z, M + 2, E, Fmt<E, M>::MAX_NORM, MODE);
+  if (FAM == MXQ_FAMILY_MXGEMMINI) return q_ocp_small(z, E, M, MODE, Fmt<E, M>::MAX_NORM);
+  return q_microsoft_ocp_small(z, M + 2, E, Fmt<E, M>::MAX_NORM, MODE);
 }
 
 template <int FAM, int E, int M>
@@ -261,7 +261,8 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
                                                   int64_t len, int64_t inner, TParams prm) {
   extern __shared__ __align__(128) float tiles[];            // [STAGES][TR][TC]
   __shared__ __align__(8) uint64_t bars[STAGES];
-  __shared__ float s_x[TC], s_r[TC];
+  __shared__ __align__(16) float s_x[TC];                   // read as float4 (COLS): 16-byte aligned
+  __shared__ __align__(16) float s_r[TC];
 
   const int tid = threadIdx.x;
   // tile grid: ROWS -> (row tiles, column tiles) of the [outer, len] matrix; COLS -> (outer, blocks, column tiles)

@@ -84,6 +84,21 @@ X int64_t h_fast_forms_mismatches(uint64_t lo, uint64_t hi, uint64_t stride, int
   }
   return bad;
 }
+// the one-add forms of clean tiles (|x| < 2^17) against the general ones, over bit patterns lo, lo+stride, ... < hi
+// (patterns with |x| >= 2^17 skipped): which 0 q_ocp_small / q_ocp_bits, 1 q_microsoft_ocp_small / _core
+X int64_t h_small_forms_mismatches(uint64_t lo, uint64_t hi, uint64_t stride, int which, int e, int m, int mode) {
+  int64_t bad = 0;
+  float mn = ocp_max_norm(e, m);
+  for (uint64_t v = lo; v < hi; v += stride) {
+    if (((uint32_t)v & 0x7fffffffu) >= 0x48000000u) continue;
+    float x = u2f((uint32_t)v);
+    float a, b;
+    if (which == 0) { a = q_ocp_small(x, e, m, mode, mn); b = q_ocp_bits(x, e, m, mode, mn); }
+    else { a = q_microsoft_ocp_small(x, m + 2, e, mn, mode); b = q_microsoft_ocp_core(x, m + 2, e, mn, mode); }
+    if (f2u(a) != f2u(b)) bad++;
+  }
+  return bad;
+}
 // q_microsoft_ocp against q_microsoft (saturating) over bit patterns lo, lo+stride, ... < hi
 X int64_t h_ms_ocp_mismatches(uint64_t lo, uint64_t hi, uint64_t stride, int e, int m, int mode) {
   int64_t bad = 0;

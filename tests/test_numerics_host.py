@@ -132,6 +132,31 @@ def test_microsoft_ocp_form_matches_general(shim):
     assert bad == 0
 
 
+@pytest.mark.parametrize("which", [0, 1], ids=["ocp_grid", "microsoft"])
+def test_small_forms_match_general(shim, which):
+    """The clean-tile element forms (q_ocp_small, q_microsoft_ocp_small: rounding by one float add at the step's
+    magic constant) equal q_ocp_bits / q_microsoft_ocp_core on every pattern with |x| < 2^17 on a dense stride, for
+    every OCP format and rounding mode, including the one value where microxcaling's even is not RNE."""
+    f = shim.h_small_forms_mismatches
+    f.restype = ctypes.c_int64
+    f.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                  ctypes.c_int]
+    from concurrent.futures import ThreadPoolExecutor
+    stride, chunk = 1021, 1 << 29
+    jobs = [(lo, e, m, mode) for (e, m) in [(4, 3), (5, 2), (3, 2), (2, 3), (2, 1)] for mode in range(3)
+            for lo in range(0, 1 << 32, chunk)]
+    with ThreadPoolExecutor(8) as ex:
+        bad = sum(ex.map(lambda j: f(j[0], j[0] + chunk, stride, which, j[1], j[2], j[3]), jobs))
+    assert bad == 0
+    # the exception itself: (0.5 - 2^-25) * 2^(min_exp - m) in every format, both signs, with its neighbours
+    for (e, m) in [(4, 3), (5, 2), (3, 2), (2, 3), (2, 1)]:
+        min_exp = 2 - (1 << (e - 1))
+        star = ((min_exp + 127 - m - 2) << 23) | 0x7FFFFF
+        for v in (star - 1, star, star + 1, star | 0x80000000):
+            for mode in range(3):
+                assert f(v, v + 1, 1, which, e, m, mode) == 0
+
+
 def test_microsoft_even_is_not_rint(shim):
     """Regression: the reference's even rounding rounds |t| + 0.5 in float32 before the floor, so 2^-10 (1 - 2^-24)
     in MXFP8_E4M3 (t = 0.5 - 2^-25 after clipping) becomes 2^-9, where round-half-even would give 0."""
