@@ -1,7 +1,9 @@
-// The block quantizers' main kernel on sm_100a: persistent CTAs stream 32 x TC float32 tiles of V (TC = 256) through
-// shared memory with TMA (cp.async.bulk.tensor, two stages, mbarrier-tracked), so each tile's load overlaps the
-// previous tile's arithmetic, and one pass over HBM reads V once and writes P and X once. (32 x 128 tiles, five
-// CTAs per SM instead of three, measured slower: the per-tile work no longer covers the per-tile synchronisation.)
+// The block quantizers' main kernel on sm_100a: one CTA per 32 x TC float32 tile of V (TC = 256). A CTA loads its
+// tile into shared memory with one TMA copy (cp.async.bulk.tensor, mbarrier-tracked, bounded wait), quantizes it and
+// exits; the block scheduler keeps several such CTAs resident per SM, so one CTA's load overlaps the others'
+// arithmetic and stores, and one pass over HBM reads V once and writes P and X once. (Persistent CTAs cycling
+// through tiles with a two- or three-stage pipeline measured 11-12% slower on the same sweep: fewer loads in
+// flight per SM, and each launch ended on a partial round of 32 KB tiles.)
 //
 // Two layouts of the [outer, len, inner] view (blocks of 32 along len):
 //   ROWS (inner == 1): a tile is 32 rows x TC consecutive values of a row, i.e. TC / 32 blocks per row;
@@ -12,8 +14,6 @@
 // power-of-two scale); (2) every thread quantizes its float4 of the tile, reading values and scales from shared
 // memory and writing P with coalesced 128-bit streaming stores -- a clean tile with the short element step.
 // The element format is a template parameter, so the grid constants of each format fold into immediates.
-#include <atomic>
-
 #include "common.cuh"
 #include "numerics.cuh"
 #include "tma.cuh"
@@ -22,13 +22,12 @@ using namespace mxq;
 
 namespace {
 
-constexpr int TR = 32, TC = 256, NT = 256, STAGES = 2;
+constexpr int TR = 32, TC = 256, NT = 256;
 constexpr int C4 = TC / 4;              // float4 per tile row
 constexpr int BPR = TC / 32;            // blocks per tile row (ROWS layout)
 constexpr int RPI = NT / C4;            // tile rows per pass of the CTA in the element step
 static_assert(TC % 32 == 0 && TC <= NT && NT % C4 == 0 && TR % RPI == 0, "tile shape");
-constexpr int kMaxDevices = 64;
-constexpr unsigned TILE_BYTES = TR * TC * sizeof(float);
+constexpr unsigned TILE_BYTES = TR * TC * sizeof(float);   // 32 KB: below the 48 KB default, no attribute needed
 
 struct TParams {
   int rounding, placement, via_e, via_m;
@@ -259,8 +258,8 @@ __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out
 template <int FAM, int E, int M, bool COLS, class Out>
 __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtensorMap tmap, Out out, int64_t outer,
                                                   int64_t len, int64_t inner, TParams prm) {
-  extern __shared__ __align__(128) float tiles[];            // [STAGES][TR][TC]
-  __shared__ __align__(8) uint64_t bars[STAGES];
+  extern __shared__ __align__(128) float T[];               // [TR][TC]: this CTA's tile
+  __shared__ __align__(8) uint64_t bar;
   __shared__ __align__(16) float s_x[TC];                   // read as float4 (COLS): 16-byte aligned
   __shared__ __align__(16) float s_r[TC];
 
@@ -268,20 +267,11 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
   // tile grid: ROWS -> (row tiles, column tiles) of the [outer, len] matrix; COLS -> (outer, blocks, column tiles)
   const int64_t nb = (len + TR - 1) / TR;
   const int64_t ctiles = COLS ? (inner + TC - 1) / TC : (len + TC - 1) / TC;
-  const int64_t ntiles = COLS ? outer * nb * ctiles : ((outer + TR - 1) / TR) * ctiles;
-
-  const uint32_t ctiles32 = (uint32_t)ctiles, nb32 = (uint32_t)nb;
-  auto issue = [&](int64_t tile, int stage) {
-    const TileAt at = tile_at<COLS>(tile, ctiles32, nb32);
-    float* dst = tiles + stage * TR * TC;
-    fence_proxy_async();
-    mbar_expect_tx(&bars[stage], TILE_BYTES);
-    if (COLS) tma_load_3d(dst, &tmap, (int)(at.ct * TC), (int)(at.b * TR), (int)at.o, &bars[stage]);
-    else tma_load_2d(dst, &tmap, (int)(at.ct * TC), (int)(at.rest * TR), &bars[stage]);
-  };
+  const TileAt at = tile_at<COLS>(blockIdx.x, (uint32_t)ctiles, (uint32_t)nb);
+  const int64_t ct = at.ct, rest = at.rest;
 
   if (tid == 0) {
-    for (int s = 0; s < STAGES; s++) mbar_init(&bars[s], 1);
+    mbar_init(&bar, 1);
     fence_mbar_init();
   }
   // launched as a programmatic dependent of the kernel before it on the stream: everything above overlaps that
@@ -289,143 +279,111 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();
-  if (tid == 0)
-    for (int s = 0; s < STAGES; s++)
-      if (blockIdx.x + (int64_t)s * gridDim.x < ntiles) issue(blockIdx.x + (int64_t)s * gridDim.x, s);
+  if (tid == 0) {
+    fence_proxy_async();
+    mbar_expect_tx(&bar, TILE_BYTES);
+    if (COLS) tma_load_3d(T, &tmap, (int)(ct * TC), (int)(at.b * TR), (int)at.o, &bar);
+    else tma_load_2d(T, &tmap, (int)(ct * TC), (int)(rest * TR), &bar);
+  }
+  // every thread waits; the CTA leaves together if the (bounded) wait gave up anywhere
+  if (!__syncthreads_and(mbar_wait(&bar, 0u))) {
+    out.finish();
+    return;
+  }
 
-  int k = 0;
-  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x, k++) {
-    const int stage = k % STAGES;
-    // every thread waits; the CTA leaves together if the (bounded) wait gave up anywhere
-    if (!__syncthreads_and(mbar_wait(&bars[stage], (unsigned)(k / STAGES) & 1u))) {
-      out.finish();
-      return;
-    }
-    const float* T = tiles + stage * TR * TC;
-    const TileAt at = tile_at<COLS>(tile, ctiles32, nb32);
-    const int64_t ct = at.ct, rest = at.rest;
-
-    // (1) block scales: one thread per block of the tile (TC of them)
-    bool bad = false;
-    if (tid >= TC) {
-    } else if (COLS) {
-      const int64_t b = at.b, o = at.o, col = ct * TC + tid;
-      uint32_t mbits = 0u;                                  // max |v| as bits: a NaN pattern tops every number
+  // (1) block scales: one thread per block of the tile (TC of them)
+  bool bad = false;
+  if (tid >= TC) {
+  } else if (COLS) {
+    const int64_t col = ct * TC + tid;
+    uint32_t mbits = 0u;                                    // max |v| as bits: a NaN pattern tops every number
 #pragma unroll 8
-      for (int r = 0; r < TR; r++) mbits = max(mbits, f2u(T[r * TC + tid]) & 0x7fffffffu);
-      const bool nan = mbits > 0x7f800000u;
-      const float x = block_scale<FAM, E, M>(nan ? qnan_f() : u2f(mbits), prm);
-      const float r = reciprocal_of<FAM>(x, nan);
-      s_x[tid] = x;
-      s_r[tid] = r;
-      bad = col < inner && (mbits >= 0x7f800000u || r == 0.0f);     // padding columns do not vote
-      if (col < inner) out.scale((o * nb + b) * inner + col, x);
-    } else {
-      const int row = tid / BPR, blk = tid % BPR;            // TR rows x BPR blocks
-      const float4* src = reinterpret_cast<const float4*>(T + row * TC + blk * 32);
-      uint32_t mbits = 0u;                                  // max |v| as bits: a NaN pattern tops every number
+    for (int r = 0; r < TR; r++) mbits = max(mbits, f2u(T[r * TC + tid]) & 0x7fffffffu);
+    const bool nan = mbits > 0x7f800000u;
+    const float x = block_scale<FAM, E, M>(nan ? qnan_f() : u2f(mbits), prm);
+    const float r = reciprocal_of<FAM>(x, nan);
+    s_x[tid] = x;
+    s_r[tid] = r;
+    bad = col < inner && (mbits >= 0x7f800000u || r == 0.0f);       // padding columns do not vote
+    if (col < inner) out.scale((at.o * nb + at.b) * inner + col, x);
+  } else {
+    const int row = tid / BPR, blk = tid % BPR;              // TR rows x BPR blocks
+    const float4* src = reinterpret_cast<const float4*>(T + row * TC + blk * 32);
+    uint32_t mbits = 0u;                                    // max |v| as bits: a NaN pattern tops every number
 #pragma unroll
-      for (int i = 0; i < 8; i++) {
-        const float4 v = src[(i + tid) & 7];
-        mbits = max(max(mbits, f2u(v.x) & 0x7fffffffu), max(f2u(v.y) & 0x7fffffffu, f2u(v.z) & 0x7fffffffu));
-        mbits = max(mbits, f2u(v.w) & 0x7fffffffu);
-      }
-      const bool nan = mbits > 0x7f800000u;
-      const float x = block_scale<FAM, E, M>(nan ? qnan_f() : u2f(mbits), prm);
-      const float r = reciprocal_of<FAM>(x, nan);
-      s_x[tid] = x;
-      s_r[tid] = r;
-      const int64_t grow = rest * TR + row, gblk = ct * (TC / 32) + blk;
-      bad = grow < outer && gblk < nb && (mbits >= 0x7f800000u || r == 0.0f);   // padding blocks do not vote
-      if (grow < outer && gblk < nb) out.scale(grow * nb + gblk, x);
+    for (int i = 0; i < 8; i++) {
+      const float4 v = src[(i + tid) & 7];
+      mbits = max(max(mbits, f2u(v.x) & 0x7fffffffu), max(f2u(v.y) & 0x7fffffffu, f2u(v.z) & 0x7fffffffu));
+      mbits = max(mbits, f2u(v.w) & 0x7fffffffu);
     }
-    const bool clean = !__syncthreads_or(bad);              // the whole tile takes the short element step
+    const bool nan = mbits > 0x7f800000u;
+    const float x = block_scale<FAM, E, M>(nan ? qnan_f() : u2f(mbits), prm);
+    const float r = reciprocal_of<FAM>(x, nan);
+    s_x[tid] = x;
+    s_r[tid] = r;
+    const int64_t grow = rest * TR + row, gblk = ct * (TC / 32) + blk;
+    bad = grow < outer && gblk < nb && (mbits >= 0x7f800000u || r == 0.0f);     // padding blocks do not vote
+    if (grow < outer && gblk < nb) out.scale(grow * nb + gblk, x);
+  }
+  const bool clean = !__syncthreads_or(bad);                // the whole tile takes the short element step
 
-    if (clean) {
-      if (FAM == MXQ_FAMILY_MXQUANT || prm.rounding == 0)
-        pass_clean<FAM, E, M, COLS, 0>(T, s_r, out, at, outer, len, inner);
-      else if (prm.rounding == 1)
-        pass_clean<FAM, E, M, COLS, 1>(T, s_r, out, at, outer, len, inner);
-      else
-        pass_clean<FAM, E, M, COLS, 2>(T, s_r, out, at, outer, len, inner);
-      __syncthreads();                                      // every thread is done with this stage and s_x / s_r
-      if (tid == 0 && tile + (int64_t)STAGES * gridDim.x < ntiles) issue(tile + (int64_t)STAGES * gridDim.x, stage);
-      continue;
-    }
+  if (clean) {
+    if (FAM == MXQ_FAMILY_MXQUANT || prm.rounding == 0)
+      pass_clean<FAM, E, M, COLS, 0>(T, s_r, out, at, outer, len, inner);
+    else if (prm.rounding == 1)
+      pass_clean<FAM, E, M, COLS, 1>(T, s_r, out, at, outer, len, inner);
+    else
+      pass_clean<FAM, E, M, COLS, 2>(T, s_r, out, at, outer, len, inner);
+    out.finish();
+    return;
+  }
 
-    // (2) elements: float4 q = tid + NT i of the tile (row q / C4, float4 column q % C4)
-    const int c4 = tid % C4;
-    float4 xs, rs;
-    if (COLS) {
-      xs = *reinterpret_cast<const float4*>(s_x + c4 * 4);
-      rs = *reinterpret_cast<const float4*>(s_r + c4 * 4);
-    }
+  // (2) elements: float4 q = tid + NT i of the tile (row q / C4, float4 column q % C4)
+  const int c4 = tid % C4;
+  float4 xs, rs;
+  if (COLS) {
+    xs = *reinterpret_cast<const float4*>(s_x + c4 * 4);
+    rs = *reinterpret_cast<const float4*>(s_r + c4 * 4);
+  }
 #pragma unroll 2
-    for (int i = 0; i < TR / RPI; i++) {
-      const int row = tid / C4 + RPI * i;
-      float4 v = reinterpret_cast<const float4*>(T + row * TC)[c4];
-      if (!COLS) {
-        const int b = row * BPR + (c4 >> 3);
-        const float x = s_x[b], r = s_r[b];
-        xs = make_float4(x, x, x, x);
-        rs = make_float4(r, r, r, r);
-      }
-      v.x = element<FAM, E, M>(divide<FAM>(v.x, xs.x, rs.x), prm);
-      v.y = element<FAM, E, M>(divide<FAM>(v.y, xs.y, rs.y), prm);
-      v.z = element<FAM, E, M>(divide<FAM>(v.z, xs.z, rs.z), prm);
-      v.w = element<FAM, E, M>(divide<FAM>(v.w, xs.w, rs.w), prm);
-      if (COLS) {
-        const int64_t l = at.b * TR + row, col = ct * TC + c4 * 4;
-        if (l < len && col < inner) out.codes((at.o * len + l) * inner + col, v);
-      } else {
-        const int64_t grow = rest * TR + row, col = ct * TC + c4 * 4;
-        if (grow < outer && col < len) out.codes(grow * len + col, v);
-      }
+  for (int i = 0; i < TR / RPI; i++) {
+    const int row = tid / C4 + RPI * i;
+    float4 v = reinterpret_cast<const float4*>(T + row * TC)[c4];
+    if (!COLS) {
+      const int b = row * BPR + (c4 >> 3);
+      const float x = s_x[b], r = s_r[b];
+      xs = make_float4(x, x, x, x);
+      rs = make_float4(r, r, r, r);
     }
-    __syncthreads();                                        // every thread is done with this stage and s_x / s_r
-    if (tid == 0 && tile + (int64_t)STAGES * gridDim.x < ntiles) issue(tile + (int64_t)STAGES * gridDim.x, stage);
+    v.x = element<FAM, E, M>(divide<FAM>(v.x, xs.x, rs.x), prm);
+    v.y = element<FAM, E, M>(divide<FAM>(v.y, xs.y, rs.y), prm);
+    v.z = element<FAM, E, M>(divide<FAM>(v.z, xs.z, rs.z), prm);
+    v.w = element<FAM, E, M>(divide<FAM>(v.w, xs.w, rs.w), prm);
+    if (COLS) {
+      const int64_t l = at.b * TR + row, col = ct * TC + c4 * 4;
+      if (l < len && col < inner) out.codes((at.o * len + l) * inner + col, v);
+    } else {
+      const int64_t grow = rest * TR + row, col = ct * TC + c4 * 4;
+      if (grow < outer && col < len) out.codes(grow * len + col, v);
+    }
   }
   out.finish();
 }
 
-// CTAs per SM of one kernel on the current device, with its shared-memory attribute set: done once per kernel and
-// device (the attribute is per device), then read from the cache.
-template <int FAM, int E, int M, bool COLS, class Out>
-int ctas_per_sm(size_t smem) {
-  static std::atomic<int> cache[kMaxDevices];
-  int dev = 0;
-  if (int r = check_cuda(cudaGetDevice(&dev), "block_quantize: current device")) return -r;
-  if (dev < 0 || dev >= kMaxDevices) return -set_error(MXQ_ERR_UNSUPPORTED, "block_quantize: device %d", dev);
-  int per_sm = cache[dev].load(std::memory_order_relaxed);
-  if (per_sm > 0) return per_sm;
-  auto kern = k_quant_tma<FAM, E, M, COLS, Out>;
-  if (int r = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                         "block_quantize: shared memory attribute"))
-    return -r;
-  if (int r = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NT, smem),
-                         "block_quantize: occupancy"))
-    return -r;
-  if (per_sm < 1) per_sm = 1;
-  cache[dev].store(per_sm, std::memory_order_relaxed);
-  return per_sm;
-}
-
+// One CTA per tile: the hardware's block scheduler streams the tiles, so every SM keeps several tiles' loads in
+// flight (one 32 KB TMA load per resident CTA) while other CTAs quantize and store, and the last tiles of a launch
+// spread over the SMs a CTA at a time. Launched as a programmatic dependent (PDL) of the kernel before it.
 template <int FAM, int E, int M, class Out>
 int launch(const CUtensorMap& map, bool cols, Out out, int64_t outer, int64_t len, int64_t inner,
            const TParams& prm, cudaStream_t st) {
   const int64_t nb = (len + TR - 1) / TR;
   const int64_t ntiles = cols ? outer * nb * ((inner + TC - 1) / TC) : ((outer + TR - 1) / TR) * ((len + TC - 1) / TC);
-  if (ntiles >= (1ll << 31)) return MXQ_ERR_UNSUPPORTED;   // the kernel's tile coordinates are 32-bit
-  const size_t smem = STAGES * TILE_BYTES;
+  if (ntiles >= (1ll << 31)) return MXQ_ERR_UNSUPPORTED;   // one CTA per tile; 32-bit tile coordinates
   auto kern = cols ? k_quant_tma<FAM, E, M, true, Out> : k_quant_tma<FAM, E, M, false, Out>;
-  const int per_sm = cols ? ctas_per_sm<FAM, E, M, true, Out>(smem) : ctas_per_sm<FAM, E, M, false, Out>(smem);
-  if (per_sm < 0) return -per_sm;
-  int64_t grid = (int64_t)sm_count() * per_sm;
-  if (grid > ntiles) grid = ntiles;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)grid);
+  cfg.gridDim = dim3((unsigned)ntiles);
   cfg.blockDim = dim3(NT);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = TILE_BYTES;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;     // may start while the previous kernel drains
