@@ -3,6 +3,8 @@
 // E8M0 bytes, in the float32 outputs' own layouts. One byte per FP8 / FP6 element (FP6 in the low six bits), two
 // FP4 elements per byte (the even one in the low nibble); a scale byte b is 2^(b - 127), 0xFF NaN. The quantizer is
 // the fused TMA kernel with a packing output stage (quantize_tma.cu); unpacking decodes a byte arithmetically.
+#include <type_traits>
+
 #include "common.cuh"
 #include "numerics.cuh"
 
@@ -67,6 +69,79 @@ __global__ void k_dequantize_packed(const uint8_t* __restrict__ codes, const uin
   }
 }
 
+// unpack on vectors, the format as template arguments (the decode folds to a few integer ops): a thread turns 4 codes
+// (one 32-bit word of FP8 / FP6 bytes, or one 16-bit word of FP4 nibbles) into a float4 of P, and 4 scale bytes
+// into a float4 of X. Preconditions: n_codes and n_scales multiples of 4, 16-byte aligned P and X, codes aligned to
+// the word, fewer than 2^32 codes.
+template <int E, int M>
+__global__ void __launch_bounds__(256) k_unpack4(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales,
+                                                 float4* __restrict__ P, float4* __restrict__ X, uint32_t nc4,
+                                                 uint32_t ns4) {
+  const uint32_t q = blockIdx.x * 256u + threadIdx.x;
+  if (q < nc4) {
+    uint32_t w;
+    if (E + M == 3) {
+      w = reinterpret_cast<const uint16_t*>(codes)[q];
+      P[q] = make_float4(ocp_value(w & 15u, E, M), ocp_value((w >> 4) & 15u, E, M), ocp_value((w >> 8) & 15u, E, M),
+                         ocp_value((w >> 12) & 15u, E, M));
+    } else {
+      w = reinterpret_cast<const uint32_t*>(codes)[q];
+      P[q] = make_float4(ocp_value(w & 255u, E, M), ocp_value((w >> 8) & 255u, E, M),
+                         ocp_value((w >> 16) & 255u, E, M), ocp_value(w >> 24, E, M));
+    }
+  }
+  if (q < ns4) {
+    const uint32_t w = reinterpret_cast<const uint32_t*>(scales)[q];
+    X[q] = make_float4(e8m0_value(w & 255u), e8m0_value((w >> 8) & 255u), e8m0_value((w >> 16) & 255u),
+                       e8m0_value(w >> 24));
+  }
+}
+
+// dequantize_packed on vectors: a thread decodes 4 codes and multiplies by their scales (one E8M0 byte for a run
+// along a row, 4 bytes for a run along inner). Preconditions as k_dequantize4 (quantize.cu), codes aligned to the
+// word, and for COLS the 4 scale bytes at a multiple of 4.
+template <int E, int M, bool COLS>
+__global__ void __launch_bounds__(256) k_dequantize_packed4(const uint8_t* __restrict__ codes,
+                                                            const uint8_t* __restrict__ scales,
+                                                            float4* __restrict__ out, uint32_t n4, uint32_t len,
+                                                            uint32_t inner, uint32_t block, uint32_t nb) {
+  const uint32_t q = blockIdx.x * 256u + threadIdx.x;
+  if (q >= n4) return;
+  const uint32_t e = q * 4u;
+  float4 v;
+  if (E + M == 3) {
+    const uint32_t w = reinterpret_cast<const uint16_t*>(codes)[q];
+    v = make_float4(ocp_value(w & 15u, E, M), ocp_value((w >> 4) & 15u, E, M), ocp_value((w >> 8) & 15u, E, M),
+                    ocp_value((w >> 12) & 15u, E, M));
+  } else {
+    const uint32_t w = reinterpret_cast<const uint32_t*>(codes)[q];
+    v = make_float4(ocp_value(w & 255u, E, M), ocp_value((w >> 8) & 255u, E, M), ocp_value((w >> 16) & 255u, E, M),
+                    ocp_value(w >> 24, E, M));
+  }
+  float4 x;
+  if (COLS) {
+    const uint32_t ol = e / inner, j = e - ol * inner, o = ol / len, l = ol - o * len;
+    const uint32_t w = reinterpret_cast<const uint32_t*>(scales)[((o * nb + l / block) * inner + j) / 4u];
+    x = make_float4(e8m0_value(w & 255u), e8m0_value((w >> 8) & 255u), e8m0_value((w >> 16) & 255u),
+                    e8m0_value(w >> 24));
+  } else {
+    const uint32_t o = e / len, l = e - o * len;
+    const float s = e8m0_value(scales[o * nb + l / block]);
+    x = make_float4(s, s, s, s);
+  }
+  out[q] = make_float4(__fmul_rn(v.x, x.x), __fmul_rn(v.y, x.y), __fmul_rn(v.z, x.z), __fmul_rn(v.w, x.w));
+}
+
+// the (e, m) of an MX element format as template arguments: f(std::integral_constant<int, E>, ...<int, M>)
+template <class F>
+int by_format(int e, int m, F f) {
+  if (e == 4 && m == 3) return f(std::integral_constant<int, 4>(), std::integral_constant<int, 3>());
+  if (e == 5 && m == 2) return f(std::integral_constant<int, 5>(), std::integral_constant<int, 2>());
+  if (e == 3 && m == 2) return f(std::integral_constant<int, 3>(), std::integral_constant<int, 2>());
+  if (e == 2 && m == 3) return f(std::integral_constant<int, 2>(), std::integral_constant<int, 3>());
+  return f(std::integral_constant<int, 2>(), std::integral_constant<int, 1>());
+}
+
 }  // namespace
 
 extern "C" {
@@ -100,6 +175,19 @@ int mxq_unpack(const uint8_t* codes, const uint8_t* scales, float* P, float* X, 
   MXQ_REQUIRE(n_codes >= 0 && n_scales >= 0, MXQ_ERR_VALUE, "unpack: negative size");
   const int64_t n = n_codes > n_scales ? n_codes : n_scales;
   if (n == 0) return MXQ_OK;
+  const int word = e + m == 3 ? 2 : 4;                      // code bytes per 4 codes
+  if (n_codes % 4 == 0 && n_scales % 4 == 0 && n < (1ll << 32) && (uintptr_t)codes % word == 0 &&
+      (uintptr_t)scales % 4 == 0 && (uintptr_t)P % 16 == 0 && (uintptr_t)X % 16 == 0) {
+    const uint32_t nc4 = (uint32_t)(n_codes / 4), ns4 = (uint32_t)(n_scales / 4);
+    const uint32_t grid = ((nc4 > ns4 ? nc4 : ns4) + 255) / 256;
+    cudaStream_t st = as_stream(stream);
+    by_format(e, m, [&](auto E, auto M) {
+      k_unpack4<decltype(E)::value, decltype(M)::value><<<grid, 256, 0, st>>>(
+          codes, scales, reinterpret_cast<float4*>(P), reinterpret_cast<float4*>(X), nc4, ns4);
+      return 0;
+    });
+    return MXQ_LAUNCH_CHECK("unpack");
+  }
   k_unpack<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(codes, scales, P, X, n_codes, n_scales, e, m);
   return MXQ_LAUNCH_CHECK("unpack");
 }
@@ -108,8 +196,24 @@ int mxq_dequantize_packed(const uint8_t* codes, const uint8_t* scales, float* ou
                           int64_t inner, int64_t block, int32_t e, int32_t m, void* stream) {
   MXQ_REQUIRE(ocp_format(e, m), MXQ_ERR_VALUE, "dequantize_packed: (e=%d, m=%d) is not an MX element format", e, m);
   MXQ_REQUIRE(outer >= 0 && len >= 0 && inner >= 0 && block >= 1, MXQ_ERR_VALUE, "dequantize_packed: bad layout");
-  const int64_t n = outer * len * inner;
+  const int64_t n = outer * len * inner, nb = (len + block - 1) / block;
   if (n == 0) return MXQ_OK;
+  const int word = e + m == 3 ? 2 : 4;
+  const bool al = (uintptr_t)codes % word == 0 && (uintptr_t)out % 16 == 0 && n < (1ll << 32) &&
+                  outer * nb * inner < (1ll << 32);
+  const bool cols = inner % 4 == 0 && (uintptr_t)scales % 4 == 0, rows = inner == 1 && len % 4 == 0 && block % 4 == 0;
+  if (al && (cols || rows)) {
+    const uint32_t n4 = (uint32_t)(n / 4), grid = (n4 + 255) / 256;
+    cudaStream_t st = as_stream(stream);
+    by_format(e, m, [&](auto E, auto M) {
+      constexpr int e_ = decltype(E)::value, m_ = decltype(M)::value;
+      auto kern = cols ? k_dequantize_packed4<e_, m_, true> : k_dequantize_packed4<e_, m_, false>;
+      kern<<<grid, 256, 0, st>>>(codes, scales, reinterpret_cast<float4*>(out), n4, (uint32_t)len, (uint32_t)inner,
+                                 (uint32_t)block, (uint32_t)nb);
+      return 0;
+    });
+    return MXQ_LAUNCH_CHECK("dequantize_packed");
+  }
   k_dequantize_packed<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(codes, scales, out, outer, len, inner, block,
                                                                        e, m);
   return MXQ_LAUNCH_CHECK("dequantize_packed");

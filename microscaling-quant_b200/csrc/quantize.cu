@@ -353,6 +353,30 @@ __global__ void k_dequantize(const float* __restrict__ P, const float* __restric
   }
 }
 
+// dequantize on float4: one float4 per thread (one-shot grid), 32-bit index arithmetic. Preconditions (checked by
+// the launcher): 16-byte aligned P and out, fewer than 2^32 elements, and either inner % 4 == 0 (the float4 runs along
+// inner, its scales are a float4 of X, 16-byte aligned) or inner == 1 with len % 4 == 0 and block % 4 == 0 (the
+// float4 lies in one block of one row: one scale).
+template <bool COLS>
+__global__ void __launch_bounds__(256) k_dequantize4(const float4* __restrict__ P, const float* __restrict__ X,
+                                                     float4* __restrict__ out, uint32_t n4, uint32_t len,
+                                                     uint32_t inner, uint32_t block, uint32_t nb) {
+  const uint32_t q = blockIdx.x * 256u + threadIdx.x;
+  if (q >= n4) return;
+  const uint32_t e = q * 4u;
+  const float4 p = P[q];
+  float4 x;
+  if (COLS) {
+    const uint32_t ol = e / inner, j = e - ol * inner, o = ol / len, l = ol - o * len;
+    x = reinterpret_cast<const float4*>(X)[((o * nb + l / block) * inner + j) / 4u];
+  } else {
+    const uint32_t o = e / len, l = e - o * len;
+    const float s = X[o * nb + l / block];
+    x = make_float4(s, s, s, s);
+  }
+  out[q] = make_float4(x86_mul(p.x, x.x), x86_mul(p.y, x.y), x86_mul(p.z, x.z), x86_mul(p.w, x.w));
+}
+
 int check_layout(int64_t outer, int64_t len, int64_t inner, int64_t block, const char* what) {
   MXQ_REQUIRE(outer >= 0 && len >= 0 && inner >= 0, MXQ_ERR_VALUE, "%s: negative extent", what);
   MXQ_REQUIRE(block >= 1, MXQ_ERR_VALUE, "%s: block_size must be >= 1, got %lld", what, (long long)block);
@@ -430,6 +454,15 @@ int mxq_dequantize(const float* P, const float* X, float* out, int64_t outer, in
   if (int r = check_layout(outer, len, inner, block, "dequantize")) return r;
   int64_t nb = (len + block - 1) / block, n = outer * len * inner;
   if (n == 0) return MXQ_OK;
+  const bool al = (uintptr_t)P % 16 == 0 && (uintptr_t)out % 16 == 0 && n < (1ll << 32) && outer * nb * inner < (1ll << 32);
+  const bool cols = inner % 4 == 0 && (uintptr_t)X % 16 == 0, rows = inner == 1 && len % 4 == 0 && block % 4 == 0;
+  if (al && (cols || rows)) {
+    const uint32_t n4 = (uint32_t)(n / 4), grid = (n4 + 255) / 256;
+    auto kern = cols ? k_dequantize4<true> : k_dequantize4<false>;
+    kern<<<grid, 256, 0, as_stream(stream)>>>(reinterpret_cast<const float4*>(P), X, reinterpret_cast<float4*>(out),
+                                              n4, (uint32_t)len, (uint32_t)inner, (uint32_t)block, (uint32_t)nb);
+    return MXQ_LAUNCH_CHECK("dequantize");
+  }
   k_dequantize<<<grid_for(n, 256), 256, 0, as_stream(stream)>>>(P, X, out, outer, len, inner, block, nb);
   return MXQ_LAUNCH_CHECK("dequantize");
 }
