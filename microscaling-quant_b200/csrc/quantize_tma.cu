@@ -78,7 +78,10 @@ __device__ __forceinline__ float ocp_grid(float x, int mode) {
 template <int FAM, int E, int M>
 __device__ __forceinline__ float element(float z, const TParams& p) {
   if (FAM == MXQ_FAMILY_MXQUANT) return qtorch_ties_away<E, M>(z);
-  if (FAM == MXQ_FAMILY_MXGEMMINI) return ocp_grid<E, M>(z, p.rounding);
+  if (FAM == MXQ_FAMILY_MXGEMMINI) {
+    if (p.via_e) z = q_ieee(z, p.via_e, p.via_m, p.rounding);          // mxgemmini.py:50-55: the via pre-rounding
+    return ocp_grid<E, M>(z, p.rounding);
+  }
   return q_microsoft_ocp(z, M + 2, E, Fmt<E, M>::MAX_NORM, p.rounding);
 }
 
@@ -325,7 +328,8 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     bad = grow < outer && gblk < nb && (mbits >= 0x7f800000u || r == 0.0f);     // padding blocks do not vote
     if (grow < outer && gblk < nb) out.scale(grow * nb + gblk, x);
   }
-  const bool clean = !__syncthreads_or(bad);                // the whole tile takes the short element step
+  // the whole tile takes the short element step (which has no via pre-rounding)
+  const bool clean = !__syncthreads_or(bad) && !(FAM == MXQ_FAMILY_MXGEMMINI && prm.via_e != 0);
 
   if (clean) {
     if (FAM == MXQ_FAMILY_MXQUANT || prm.rounding == 0)
@@ -431,8 +435,7 @@ namespace mxq {
 // bytes, extents below 2^31); MXQ_ERR_UNSUPPORTED otherwise (the caller then takes the register kernels).
 int quantize_tma_dest(const float* V, const Dest& d, int64_t outer, int64_t len, int64_t inner, int64_t block,
                       const mxq_quant_spec& s, cudaStream_t st) {
-  if (block != 32 || s.family == MXQ_FAMILY_FP32 || (s.family == MXQ_FAMILY_MXGEMMINI && s.via_e != 0))
-    return MXQ_ERR_UNSUPPORTED;
+  if (block != 32 || s.family == MXQ_FAMILY_FP32) return MXQ_ERR_UNSUPPORTED;
   const bool cols = inner > 1;
   const int64_t rowlen = cols ? inner : len;
   const uintptr_t out_base = d.Pc ? (uintptr_t)d.Pc : (uintptr_t)d.P;

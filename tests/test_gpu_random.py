@@ -58,6 +58,20 @@ def test_block_random_bits(oracle, axis):
             assert_bits(X, Xo, f"{family}/{rm}/{fmt}/{axis} X")
 
 
+@pytest.mark.parametrize("axis", [0, 1])
+def test_block_via_vs_oracle(oracle, axis):
+    """block.mxgemmini with the via pre-rounding (mxgemmini.py:50-55) on the fused kernel, every format and rounding
+    mode, against the oracle; the float(3, 1) requantizer and a float(8, 7) one."""
+    V = config2_like(512, 256, 41 + axis)
+    for via in ((3, 1), (8, 7), (5, 10)):
+        for rm in ("ties_away", "rne", "truncate"):
+            for fmt in FMTS:
+                P, X = prod.block_quantize(V, "mxgemmini", fmt, axis, rounding_mode=rm, via=via)
+                Po, Xo = oracle.block_quantize(V, "mxgemmini", fmt, axis, 32, rm, via=via)
+                assert_bits(P, Po, f"via {via} {rm} {fmt} {axis} P")
+                assert_bits(X, Xo, f"via {via} {rm} {fmt} {axis} X")
+
+
 def test_block_layout_paths(oracle):
     """The three kernel paths (rows of 32, column runs of 4/2/1, generic) on shapes that force each."""
     rng = np.random.default_rng(5)
