@@ -247,6 +247,33 @@ def run_gpu(args):
               "float32 path Gelem/s": round(elems * len(runs) * world / (ms_step * 1e-3) / 1e9, 1),
               "ms_per_step": round(pk_ms, 4), "launches_per_step": len(pk_runs), "steps": pk_steps,
               "bytes_per_element": "4 read + 1 code (FP4 0.5) + 1/32 scale"}
+    # -- the way back: dequantize (P, X) and the compact form's unpack / dequantize_packed, two formats x two axes
+    def timed(fn, reps):
+        fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+    back = {"workload": "block.dequantize of the float32 codes, block.unpack and block.dequantize_packed of the "
+                        "compact form, on the sweep's matrix (mxgemmini codes)",
+            "bytes_per_element": "dequantize 8.125; unpack code + 4 + 1.125/32; dequantize_packed code + 4 + 1/32"}
+    reps = max(1, min(args.steps, 50))
+    for fmt in ("MXFP8_E4M3", "MXFP4"):
+        for ax in (0, 1):
+            spec, codes, scales, lay, fe = pk_out[("mxgemmini", fmt, ax)]
+            cb = 0.5 if fe == 3 else 1.0
+            P, X = quant["mxgemmini"](V, fmt, axis=ax)
+            t_dq = timed(lambda: block.dequantize(P, X, axis=ax), reps)
+            t_un = timed(lambda: block.unpack(codes, scales, fmt), reps)
+            t_dp = timed(lambda: block.dequantize_packed(codes, scales, fmt, axis=ax), reps)
+            back[f"{fmt}/axis{ax}"] = {
+                "dequantize GB/s": round(BYTES_PER_ELEM * elems / (t_dq * 1e-3) / 1e9, 1),
+                "unpack GB/s": round((cb + 4 + 1.125 / 32) * elems / (t_un * 1e-3) / 1e9, 1),
+                "dequantize_packed GB/s": round((cb + 4 + 1 / 32) * elems / (t_dp * 1e-3) / 1e9, 1)}
+            del P, X
     del pk_out
 
     # -- end to end through the public API with host tensors: each call streams its pinned host V through the
@@ -430,6 +457,7 @@ def run_gpu(args):
                         "steps": args.extra_steps, **extra},
         "model": model_out,
         "packed": packed,
+        "dequantize": back,
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu

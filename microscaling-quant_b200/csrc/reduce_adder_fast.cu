@@ -103,6 +103,7 @@ __global__ void __launch_bounds__(256, 2)
 
     if (domain && kcount == BK) {
       float hold[RM][RN];                                 // the first half-group's level-3 node
+      const F2 magic0 = pk2(L0.magic, L0.magic);
 #pragma unroll 1
       for (int oct = 0; oct < 4; oct++) {                 // 8 k per pass: one level-3 node per output
         const float* Ak = As + oct * 8 * BM;
@@ -119,21 +120,35 @@ __global__ void __launch_bounds__(256, 2)
           lds<HN>(b0 + HN, Bk + (2 * t) * BN + bc1);
           lds<HN>(b1, Bk + (2 * t + 1) * BN + bc0);
           lds<HN>(b1 + HN, Bk + (2 * t + 1) * BN + bc1);
+          // pairs of columns: the products, their snaps and the exact adds on the packed FP32 instructions (the
+          // same IEEE operations in half the issue slots), the lane roundings scalar
 #pragma unroll
-          for (int i = 0; i < RM; i++)
+          for (int i = 0; i < RM; i++) {
+            const F2 ai0 = pk2(a0[i], a0[i]), ai1 = pk2(a1[i], a1[i]);
 #pragma unroll
-            for (int j = 0; j < RN; j++) {
-              const float s = __fadd_rn(__fadd_rn(trunc3(a0[i], b0[j]), L0.magic),
-                                        __fsub_rn(trunc3(a1[i], b1[j]), L0.magic));
-              const float n1 = rne_lane(s, L0);
+            for (int j = 0; j < RN; j += 2) {
+              const F2 p0 = mul2(ai0, pk2(b0[j], b0[j + 1])), p1 = mul2(ai1, pk2(b1[j], b1[j + 1]));
+              const F2 t0 = pk2(u2f(f2u(lo2(p0)) & 0xfff00000u), u2f(f2u(hi2(p0)) & 0xfff00000u));
+              const F2 t1 = pk2(u2f(f2u(lo2(p1)) & 0xfff00000u), u2f(f2u(hi2(p1)) & 0xfff00000u));
+              const F2 s = add2(add2(t0, magic0), sub2(t1, magic0));
+              const float n1l = rne_lane(lo2(s), L0), n1h = rne_lane(hi2(s), L0);
               if (t == 0 || t == 2) {
-                n1a[i][j] = n1;
+                n1a[i][j] = n1l;
+                n1a[i][j + 1] = n1h;
               } else {
-                const float n2 = rne_lane(__fadd_rn(n1a[i][j], n1), L1);
-                if (t == 1) n2a[i][j] = n2;
-                else n3[i][j] = rne_lane(__fadd_rn(n2a[i][j], n2), L2);
+                const F2 u = add2(pk2(n1a[i][j], n1a[i][j + 1]), pk2(n1l, n1h));
+                const float n2l = rne_lane(lo2(u), L1), n2h = rne_lane(hi2(u), L1);
+                if (t == 1) {
+                  n2a[i][j] = n2l;
+                  n2a[i][j + 1] = n2h;
+                } else {
+                  const F2 w = add2(pk2(n2a[i][j], n2a[i][j + 1]), pk2(n2l, n2h));
+                  n3[i][j] = rne_lane(lo2(w), L2);
+                  n3[i][j + 1] = rne_lane(hi2(w), L2);
+                }
               }
             }
+          }
         }
         if ((oct & 1) == 0) {
 #pragma unroll

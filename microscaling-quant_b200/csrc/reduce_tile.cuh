@@ -59,6 +59,47 @@ __device__ __forceinline__ uint32_t pack_bf16(float hi, float lo) {
 __device__ __forceinline__ float unpack_hi(uint32_t p) { return u2f(p & 0xffff0000u); }
 __device__ __forceinline__ float unpack_lo(uint32_t p) { return u2f(p << 16); }
 
+// Two float32 lanes in one 64-bit register pair for sm_100's packed FP32 instructions (add / sub / mul .rn.f32x2):
+// each half is the IEEE single-precision operation with round-to-nearest-even, so a pair computes exactly what two
+// scalar __fadd_rn / __fsub_rn / __fmul_rn would, in one issue slot. lo is the first element, hi the second.
+typedef unsigned long long F2;
+__device__ __forceinline__ F2 pk2(float lo, float hi) {
+  F2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float lo2(F2 v) {
+  float lo;
+  asm("{\n .reg .f32 h;\n mov.b64 {%0, h}, %1;\n}" : "=f"(lo) : "l"(v));
+  return lo;
+}
+__device__ __forceinline__ float hi2(F2 v) {
+  float hi;
+  asm("{\n .reg .f32 l;\n mov.b64 {l, %0}, %1;\n}" : "=f"(hi) : "l"(v));
+  return hi;
+}
+__device__ __forceinline__ F2 add2(F2 a, F2 b) {
+  F2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ F2 sub2(F2 a, F2 b) {
+  F2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ F2 mul2(F2 a, F2 b) {
+  F2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// trunc3 of a pair of products, then the lane's snap of both (snap(trunc3(a * b)) per half)
+__device__ __forceinline__ F2 snap_trunc3_2(F2 a, F2 b, F2 magic) {
+  const F2 p = mul2(a, b);
+  const F2 t = pk2(u2f(f2u(lo2(p)) & 0xfff00000u), u2f(f2u(hi2(p)) & 0xfff00000u));
+  return sub2(add2(t, magic), magic);
+}
+
 // CTA tile (RM * 16) x (RN * 16) with 256 threads on a 16 x 16 grid; a thread owns rows ty*(RM/2) + {..} and
 // RM*8 + ty*(RM/2) + {..}, likewise columns, so its shared-memory reads are conflict-free float2 / float4 loads.
 template <int RM, int RN>
