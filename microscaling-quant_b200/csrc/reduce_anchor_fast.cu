@@ -208,15 +208,24 @@ __global__ void __launch_bounds__(256, 2)
                 acc[i][j] = __fadd_rn(acc[i][j], fabsf(p) >= 1.52587890625e-05f ? term : 0.0f);
               }
           } else {
+            // pairs of columns on the packed FP32 instructions (the same IEEE operations, fewer issue slots)
 #pragma unroll
-            for (int i = 0; i < RM; i++)
+            for (int i = 0; i < RM; i++) {
+              const F2 ai = pk2(a[i], a[i]);
 #pragma unroll
-              for (int j = 0; j < RN; j++) {
-                const float y = __fmul_rn(trunc3(a[i], b[j]), inv[i][j]);
-                const float c = P.drop_rne ? keep_magic : u2f((f2u(y) & 0x80000000u) | 0x4b000000u);
-                const float term = P.drop_rne ? __fsub_rn(__fadd_rn(y, c), c) : __fsub_rn(__fadd_rz(y, c), c);
-                acc[i][j] = __fadd_rn(acc[i][j], term);
+              for (int j = 0; j < RN; j += 2) {
+                const F2 p = mul2(ai, pk2(b[j], b[j + 1]));
+                const F2 y = mul2(pk2(u2f(f2u(lo2(p)) & 0xfff00000u), u2f(f2u(hi2(p)) & 0xfff00000u)),
+                                  pk2(inv[i][j], inv[i][j + 1]));
+                const float c0 = P.drop_rne ? keep_magic : u2f((f2u(lo2(y)) & 0x80000000u) | 0x4b000000u);
+                const float c1 = P.drop_rne ? keep_magic : u2f((f2u(hi2(y)) & 0x80000000u) | 0x4b000000u);
+                const F2 c = pk2(c0, c1);
+                const F2 t = P.drop_rne ? sub2(add2(y, c), c) : sub2(addrz2(y, c), c);
+                const F2 acc2 = add2(pk2(acc[i][j], acc[i][j + 1]), t);
+                acc[i][j] = lo2(acc2);
+                acc[i][j + 1] = hi2(acc2);
               }
+            }
           }
         }
         // S4 (bf16 lane) and the tile add, C packed as bf16 pairs

@@ -88,6 +88,11 @@ __device__ __forceinline__ F2 sub2(F2 a, F2 b) {
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+__device__ __forceinline__ F2 addrz2(F2 a, F2 b) {            // rounded toward zero
+  F2 r;
+  asm("add.rz.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
 __device__ __forceinline__ F2 mul2(F2 a, F2 b) {
   F2 r;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
