@@ -266,9 +266,35 @@ int systolic_fast(const float* PA, const float* XA, const float* PB, const float
                        A.floor_thr == 1.52587890625e-05f && A.sat_limit == 448.0f && A.sat_value == 448.0f;
   const bool aligned = M % 4 == 0 && N % 4 == 0 && (uintptr_t)PA % 16 == 0 && (uintptr_t)PB % 16 == 0;
   if (!tapeout || bs != 32 || !is_hw_final(lanes, size) || !aligned || K == 0) return MXQ_ERR_UNSUPPORTED;
-  // 4 x 8 micro-tiles: 123 registers, two CTAs (16 warps) per SM; measured 2.89 TMAC/s at 4096^3 against 2.56 for
-  // 8 x 8 (255 registers, 8 warps)
-  return launch_hw<4, 8>(PA, XA, PB, XB, Y, K, M, N, A, lanes, st, batch, bt);
+  // The CTA tile: 4 x 8 micro-tiles (64 x 128 outputs, 115 registers, two CTAs per SM) are the fastest per MAC
+  // (3.56 TMAC/s at 4096^3; 8 x 8 measured 2.56), smaller tiles trade some of that for more CTAs when the output is
+  // small. Measured per-MAC rates relative to 4 x 8, with every SM busy: 4 x 4 0.92, 2 x 4 0.85, 2 x 2 0.78. Score
+  // = that rate x the fraction of the launched waves' CTA slots (two per SM) that hold a CTA; the best score wins.
+  // (256 x 512 x 512, PR1's GEMM: 16 CTAs of 4 x 8 ran 206 us, 128 CTAs of 2 x 2 52 us; 1024^3 picks 4 x 4.)
+  const int64_t slots = 2 * (int64_t)sm_count();
+  struct Choice {
+    int rm, rn;
+    double rate;
+  };
+  const Choice choices[4] = {{4, 8, 1.0}, {4, 4, 0.92}, {2, 4, 0.85}, {2, 2, 0.78}};
+  int best = 0;
+  double best_score = -1.0;
+  for (int c = 0; c < 4; c++) {
+    const int64_t ctas = ((N + 16 * choices[c].rn - 1) / (16 * choices[c].rn)) *
+                         ((M + 16 * choices[c].rm - 1) / (16 * choices[c].rm)) * batch;
+    const int64_t waves = (ctas + slots - 1) / slots;
+    const double score = choices[c].rate * (double)ctas / (double)(waves * slots);
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = c;
+    }
+  }
+  switch (best) {
+    case 0: return launch_hw<4, 8>(PA, XA, PB, XB, Y, K, M, N, A, lanes, st, batch, bt);
+    case 1: return launch_hw<4, 4>(PA, XA, PB, XB, Y, K, M, N, A, lanes, st, batch, bt);
+    case 2: return launch_hw<2, 4>(PA, XA, PB, XB, Y, K, M, N, A, lanes, st, batch, bt);
+    default: return launch_hw<2, 2>(PA, XA, PB, XB, Y, K, M, N, A, lanes, st, batch, bt);
+  }
 }
 
 }  // namespace mxq
