@@ -610,8 +610,9 @@ MXQ_HD float q_ocp_bits(float x, int e, int m, int mode, float max_norm) {
 // binade's biased exponent field in place (a < 2^(E - 126)): C = 1.5 * 2^23 * q has ulp q and a is far below C's
 // binade width, so a + C lands on C + (a rounded to a multiple of q) in the add's own rounding (to nearest even, or
 // toward zero = down), and subtracting C is exact (Sterbenz). Ties away (RM_TIES_AWAY) first adds q / 2 rounded to
-// nearest, which is the reference's fl(a / q + 0.5) scaled by q, then rounds down. E - 127 - m + 23 must stay a
-// normal float32 exponent: a < 2^17 and E >= 106 keep it.
+// nearest, which is the reference's fl(a / q + 0.5) scaled by q, then rounds down. Needs m <= 21 (a + C must stay
+// in C's binade, a < C / 3, which a < 2^(E - 126) gives when m <= 21) and C and q / 2 normal (E >= m + 2); callers
+// keep a < 2^17.
 MXQ_HD float step_round(float a, uint32_t e23, int m, int mode) {
   const float c = u2f(e23 + (((uint32_t)(23 - m) << 23) | 0x400000u));
   if (mode == RM_RNE) return sub_rn(add_rn(a, c), c);
@@ -626,6 +627,20 @@ MXQ_HD float q_ocp_small(float x, int e, int m, int mode, float max_norm) {
   const uint32_t e23 = (a & 0x7f800000u) > lo ? (a & 0x7f800000u) : lo;
   const float val = fminf(step_round(u2f(a), e23, m, mode), max_norm);
   return a == 0u ? 0.0f : u2f(f2u(val) | (u & 0x80000000u));
+}
+
+// q_ieee_f for finite |x| < 2^17, m <= 21 and bias(e) + m <= 126 (every such float(e, m) with e <= 7): the same step
+// 2^(max(E, emin) - m), its rounding by step_round; overflow past 2^(emax + 1) to Inf, a nonzero value that rounds
+// to zero to +0, a zero unchanged
+MXQ_HD float q_ieee_small(float x, int e, int m, int mode) {
+  const uint32_t u = f2u(x), a = u & 0x7fffffffu;
+  if (a == 0u) return x;
+  const int b = bias_of(e);
+  const uint32_t lo = (uint32_t)(128 - b) << 23;
+  const uint32_t e23 = (a & 0x7f800000u) > lo ? (a & 0x7f800000u) : lo;
+  float val = step_round(u2f(a), e23, m, mode);
+  if (f2u(val) >= (uint32_t)(128 + b) << 23) val = inf_f();                 // >= 2^(emax + 1)
+  return val == 0.0f ? 0.0f : u2f(f2u(val) | (u & 0x80000000u));
 }
 
 // q_microsoft with saturate_normals=True and exp_bits > 0

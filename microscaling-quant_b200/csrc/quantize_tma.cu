@@ -88,10 +88,15 @@ __device__ __forceinline__ float element(float z, const TParams& p) {
 // The element step of a clean tile (every block finite, every scale a power of two with an exact reciprocal): z is
 // then finite and |z| < 2^17, so the Inf / NaN / huge-value branches cannot be taken, the rounding is one float add
 // at the step's magic constant (q_ocp_small, q_microsoft_ocp_small), and the rounding mode is a template argument.
-template <int FAM, int E, int M, int MODE>
-__device__ __forceinline__ float element_clean(float z) {
+// VIA: block.mxgemmini's pre-rounding onto float(via_e, via_m) (mxgemmini.py:50-55), for via_e <= 7 and via_m <= 21
+// (q_ieee_small's range).
+template <int FAM, int E, int M, int MODE, bool VIA>
+__device__ __forceinline__ float element_clean(float z, int via_e, int via_m) {
   if (FAM == MXQ_FAMILY_MXQUANT) return qtorch_ties_away<E, M>(z);
-  if (FAM == MXQ_FAMILY_MXGEMMINI) return q_ocp_small(z, E, M, MODE, Fmt<E, M>::MAX_NORM);
+  if (FAM == MXQ_FAMILY_MXGEMMINI) {
+    if (VIA) z = q_ieee_small(z, via_e, via_m, MODE);
+    return q_ocp_small(z, E, M, MODE, Fmt<E, M>::MAX_NORM);
+  }
   return q_microsoft_ocp_small(z, M + 2, E, Fmt<E, M>::MAX_NORM, MODE);
 }
 
@@ -230,9 +235,9 @@ __device__ __forceinline__ TileAt tile_at(int64_t tile, uint32_t ctiles, uint32_
 }
 
 // (2) for a clean tile: every thread quantizes TR / RPI float4 (float4 q = tid + NT i: row q / C4, column q % C4)
-template <int FAM, int E, int M, bool COLS, int MODE, class Out>
+template <int FAM, int E, int M, bool COLS, int MODE, bool VIA, class Out>
 __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out& out, const TileAt& at,
-                                           int64_t outer, int64_t len, int64_t inner) {
+                                           int64_t outer, int64_t len, int64_t inner, int via_e, int via_m) {
   const int tid = threadIdx.x, c4 = tid % C4;
   float4 rs;
   if (COLS) rs = *reinterpret_cast<const float4*>(s_r + c4 * 4);
@@ -244,10 +249,10 @@ __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out
       const float r = s_r[row * BPR + (c4 >> 3)];
       rs = make_float4(r, r, r, r);
     }
-    v.x = element_clean<FAM, E, M, MODE>(__fmul_rn(v.x, rs.x));
-    v.y = element_clean<FAM, E, M, MODE>(__fmul_rn(v.y, rs.y));
-    v.z = element_clean<FAM, E, M, MODE>(__fmul_rn(v.z, rs.z));
-    v.w = element_clean<FAM, E, M, MODE>(__fmul_rn(v.w, rs.w));
+    v.x = element_clean<FAM, E, M, MODE, VIA>(__fmul_rn(v.x, rs.x), via_e, via_m);
+    v.y = element_clean<FAM, E, M, MODE, VIA>(__fmul_rn(v.y, rs.y), via_e, via_m);
+    v.z = element_clean<FAM, E, M, MODE, VIA>(__fmul_rn(v.z, rs.z), via_e, via_m);
+    v.w = element_clean<FAM, E, M, MODE, VIA>(__fmul_rn(v.w, rs.w), via_e, via_m);
     if (COLS) {
       const int64_t l = at.b * TR + row, col = at.ct * TC + c4 * 4;
       if (l < len && col < inner) out.template codes<true>((at.o * len + l) * inner + col, v);
@@ -328,16 +333,29 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     bad = grow < outer && gblk < nb && (mbits >= 0x7f800000u || r == 0.0f);     // padding blocks do not vote
     if (grow < outer && gblk < nb) out.scale(grow * nb + gblk, x);
   }
-  // the whole tile takes the short element step (which has no via pre-rounding)
-  const bool clean = !__syncthreads_or(bad) && !(FAM == MXQ_FAMILY_MXGEMMINI && prm.via_e != 0);
+  // the whole tile takes the short element step (with a via pre-rounding in q_ieee_small's range)
+  const bool via = FAM == MXQ_FAMILY_MXGEMMINI && prm.via_e != 0;
+  const bool clean = !__syncthreads_or(bad) && (!via || (prm.via_e <= 7 && prm.via_m <= 21));
 
   if (clean) {
+    if constexpr (FAM == MXQ_FAMILY_MXGEMMINI) {
+      if (via) {
+        if (prm.rounding == 0)
+          pass_clean<FAM, E, M, COLS, 0, true>(T, s_r, out, at, outer, len, inner, prm.via_e, prm.via_m);
+        else if (prm.rounding == 1)
+          pass_clean<FAM, E, M, COLS, 1, true>(T, s_r, out, at, outer, len, inner, prm.via_e, prm.via_m);
+        else
+          pass_clean<FAM, E, M, COLS, 2, true>(T, s_r, out, at, outer, len, inner, prm.via_e, prm.via_m);
+        out.finish();
+        return;
+      }
+    }
     if (FAM == MXQ_FAMILY_MXQUANT || prm.rounding == 0)
-      pass_clean<FAM, E, M, COLS, 0>(T, s_r, out, at, outer, len, inner);
+      pass_clean<FAM, E, M, COLS, 0, false>(T, s_r, out, at, outer, len, inner, 0, 0);
     else if (prm.rounding == 1)
-      pass_clean<FAM, E, M, COLS, 1>(T, s_r, out, at, outer, len, inner);
+      pass_clean<FAM, E, M, COLS, 1, false>(T, s_r, out, at, outer, len, inner, 0, 0);
     else
-      pass_clean<FAM, E, M, COLS, 2>(T, s_r, out, at, outer, len, inner);
+      pass_clean<FAM, E, M, COLS, 2, false>(T, s_r, out, at, outer, len, inner, 0, 0);
     out.finish();
     return;
   }

@@ -99,6 +99,16 @@ X int64_t h_small_forms_mismatches(uint64_t lo, uint64_t hi, uint64_t stride, in
   }
   return bad;
 }
+// q_ieee_small against q_ieee_f on patterns with |x| < 2^17, over bit patterns lo, lo+stride, ... < hi
+X int64_t h_ieee_small_mismatches(uint64_t lo, uint64_t hi, uint64_t stride, int e, int m, int mode) {
+  int64_t bad = 0;
+  for (uint64_t v = lo; v < hi; v += stride) {
+    if (((uint32_t)v & 0x7fffffffu) >= 0x48000000u) continue;
+    float x = u2f((uint32_t)v);
+    if (f2u(q_ieee_small(x, e, m, mode)) != f2u(q_ieee_f(x, e, m, mode))) bad++;
+  }
+  return bad;
+}
 // q_microsoft_ocp against q_microsoft (saturating) over bit patterns lo, lo+stride, ... < hi
 X int64_t h_ms_ocp_mismatches(uint64_t lo, uint64_t hi, uint64_t stride, int e, int m, int mode) {
   int64_t bad = 0;

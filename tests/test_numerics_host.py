@@ -157,6 +157,20 @@ def test_small_forms_match_general(shim, which):
                 assert f(v, v + 1, 1, which, e, m, mode) == 0
 
 
+def test_ieee_small_matches_general(shim):
+    """q_ieee_small (the via pre-rounding of clean tiles: one float add at the step's magic constant) equals
+    q_ieee_f on patterns with |x| < 2^17, on a stride, for float(e, m) with e 1..7 and m from 1 to 21, every mode."""
+    f = shim.h_ieee_small_mismatches
+    f.restype = ctypes.c_int64
+    f.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    from concurrent.futures import ThreadPoolExecutor
+    fmts = [(e, m) for e in range(1, 8) for m in (1, 2, 3, 5, 10, 21)]
+    jobs = [(lo, e, m, mode) for (e, m) in fmts for mode in range(3) for lo in range(0, 1 << 32, 1 << 30)]
+    with ThreadPoolExecutor(8) as ex:
+        bad = sum(ex.map(lambda j: f(j[0], j[0] + (1 << 30), 65537, j[1], j[2], j[3]), jobs))
+    assert bad == 0
+
+
 def test_microsoft_even_is_not_rint(shim):
     """Regression: the reference's even rounding rounds |t| + 0.5 in float32 before the floor, so 2^-10 (1 - 2^-24)
     in MXFP8_E4M3 (t = 0.5 - 2^-25 after clipping) becomes 2^-9, where round-half-even would give 0."""
