@@ -240,26 +240,61 @@ __global__ void __launch_bounds__(NT) k_lut_tables(const float* __restrict__ P, 
   const bool kfast = sk == 1;
   bool mybad = false;
   constexpr int BATCH = 8;                                  // loads in flight per thread
+  auto count = [&](float v, int gc) {
+    const int b = grid_rank(v, tp);
+    if (sgrid[b] != v) mybad = true;                        // also every NaN
+    else atomicAdd(&counts[gc * nv + b], 1);
+  };
+  if (sj == 1 && W % 4 == 0 && W <= 4 * NT && sk % 4 == 0 && ((uintptr_t)P + j0 * 4) % 16 == 0) {
+    // rows of the panel as float4: thread (row r, quad q) of rows_per_pass rows at a time, pointers advanced by
+    // whole rows (no index arithmetic per element)
+    const int qpr = (int)(W / 4), rows_per_pass = NT / qpr, r = tid / qpr, q = tid - r * qpr;
+    if (r < rows_per_pass) {
+      const float4* src = reinterpret_cast<const float4*>(P + j0) + q;
+      int gc[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) gc[i] = (4 * q + i) >> G;
+      for (int64_t k0 = r; k0 < K; k0 += (int64_t)rows_per_pass * BATCH) {
+        float4 v[BATCH];
+#pragma unroll
+        for (int u = 0; u < BATCH; u++)
+          v[u] = k0 + (int64_t)u * rows_per_pass < K ? src[(k0 + (int64_t)u * rows_per_pass) * (sk / 4)]
+                                                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int u = 0; u < BATCH; u++) {
+          if (k0 + (int64_t)u * rows_per_pass >= K) break;
+          count(v[u].x, gc[0]);
+          count(v[u].y, gc[1]);
+          count(v[u].z, gc[2]);
+          count(v[u].w, gc[3]);
+        }
+      }
+    }
+  } else {
+  // element e = (kfast ? jj * K + k : k * W + jj) walked without a division per element: the position (major,
+  // minor) advances by NT elements as (NT / R, NT % R) with R the minor extent, plus a carry
+  const int64_t R = kfast ? K : W, dmaj = NT / R, dmin = NT % R;
+  int64_t maj = tid / R, mnr = tid % R;
   for (int64_t e0 = tid; e0 < total; e0 += (int64_t)NT * BATCH) {
     float v[BATCH];
     int gcol[BATCH];
 #pragma unroll
     for (int u = 0; u < BATCH; u++) {
       const int64_t e = e0 + (int64_t)u * NT;
-      const int64_t k = kfast ? e % K : e / W, jj = kfast ? e / K : e % W;
+      const int64_t k = kfast ? mnr : maj, jj = kfast ? maj : mnr;
       gcol[u] = e < total ? (int)(jj >> G) : -1;
       v[u] = e < total ? P[k * sk + (j0 + jj) * sj] : 0.0f;
+      maj += dmaj;
+      mnr += dmin;
+      if (mnr >= R) {
+        mnr -= R;
+        maj++;
+      }
     }
 #pragma unroll
-    for (int u = 0; u < BATCH; u++) {
-      if (gcol[u] < 0) continue;
-      const int b = grid_rank(v[u], tp);
-      if (sgrid[b] != v[u]) {                               // also every NaN
-        mybad = true;
-        continue;
-      }
-      atomicAdd(&counts[gcol[u] * nv + b], 1);
-    }
+    for (int u = 0; u < BATCH; u++)
+      if (gcol[u] >= 0) count(v[u], gcol[u]);
+  }
   }
   if (mybad) bad = 1;
   __syncthreads();
@@ -755,6 +790,7 @@ int mxq_lut_tables(const float* P, float* T, int64_t K, int64_t n, int64_t sk, i
   // covers every SM about twice (each group's fit is one warp)
   const int64_t cap = group >= 5 ? 1 : (32 >> group);
   int64_t want = (ng + 2 * (int64_t)sm_count() - 1) / (2 * (int64_t)sm_count());
+  if (group < 2) want = (want + (4 >> group) - 1) / (4 >> group) * (4 >> group);    // panels of whole float4
   const int gpc = (int)(want < 1 ? 1 : (want > cap ? cap : want));
   const size_t smem = (size_t)gpc * f->nv * sizeof(int);
   const unsigned grid = (unsigned)((ng + gpc - 1) / gpc);
