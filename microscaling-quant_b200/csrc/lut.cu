@@ -696,7 +696,7 @@ __global__ void __launch_bounds__(CT) k_lut_finder_cols(const int64_t* __restric
   const int64_t j = jp + threadIdx.x;
   if (j >= n) return;
   const unsigned char* a = ans + (int)((j >> G) - gfirst) * nc;
-  constexpr int BATCH = 4;                                   // loads in flight per thread
+  constexpr int BATCH = 8;                                   // loads in flight per thread
   for (int64_t kb = k0; kb < k1; kb += BATCH) {
     int64_t c[BATCH];
 #pragma unroll
@@ -864,7 +864,9 @@ int mxq_lut_finder(const int64_t* codes, const float* T, int64_t* I, int64_t K, 
   if ((uintptr_t)T % 16 == 0 && K < (1ll << 31)) {
     int64_t rows;
     const FormatTables* f = format_tables(e, m);
-    const dim3 grid = cols_grid(K, n, &rows, f->ncodes <= 64 ? 8 : 4);   // the answer table costs ncodes per column
+    // fewer, longer CTAs than pick: each CTA first builds its panel's answer table (ncodes per column group,
+    // 16 distances each), so row slices repeat that work (measured best: 4 per SM for 64 codes, 1 for 256)
+    const dim3 grid = cols_grid(K, n, &rows, f->ncodes <= 64 ? 4 : 1);
     bool narrow = true;                                       // every fixed point and difference fits in an int
     for (int i = 0; i < f->ncodes; i++) narrow = narrow && f->fx[i] > -(1ll << 30) && f->fx[i] < (1ll << 30);
     const size_t smem = (size_t)CT * f->ncodes;               // answers: at most one group per column
