@@ -164,6 +164,27 @@ def test_systolic_fast_equals_generic(oracle):
     assert_bits(fast, want, "fast vs oracle")
 
 
+@pytest.mark.parametrize("M,N", [(2048, 2048), (1024, 1024), (512, 1024), (96, 160)],
+                         ids=["tile64x128", "tile64x64", "tile32x64", "tile32x32"])
+def test_systolic_tiles_equal_generic(M, N):
+    """The tapeout kernel picks its CTA tile by output size (on 148 SMs: 64 x 128 for 2048^2, 64 x 64 for 1024^2,
+    32 x 64 for 512 x 1024, 32 x 32 for small outputs); every tile gives the generic kernel's bits (M - 1 columns
+    force the generic kernel)."""
+    import torch
+    import mxq
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    K = 96
+    A = torch.randn(K, M, device="cuda", generator=g) * torch.exp2(torch.randint(-20, 20, (1, M), device="cuda",
+                                                                                  generator=g).float())
+    B = torch.randn(K, N, device="cuda", generator=g)
+    P_A, X_A = mxq.block.mxgemmini.quantize(A, "MXFP8_E4M3", axis=0)
+    P_B, X_B = mxq.block.mxgemmini.quantize(B, "MXFP8_E4M3", axis=0)
+    ar, hw = mxq.matmul.MXGEMMINI(), mxq.schedule.HW_FINAL
+    fast = mxq.matmul.systolic(P_A, X_A, P_B, X_B, ar, hw)
+    generic = mxq.matmul.systolic(P_A[:, :M - 1].contiguous(), X_A[:, :M - 1].contiguous(), P_B, X_B, ar, hw)
+    assert_bits(fast[:M - 1].cpu().numpy(), generic.cpu().numpy(), f"tile for {M}x{N}")
+
+
 @pytest.mark.parametrize("prod,lanes", [((4, 3), HW), ((5, 4), [(5, 2)] * 8 + [(6, 9)] * 4 + [(7, 3)] * 3 + [(8, 7)])])
 def test_systolic_mxquant_fast_equals_generic(oracle, prod, lanes):
     """The MXQuant-arithmetic systolic kernel (M, N multiples of 4) against the generic kernel (M = 127) and the
