@@ -141,6 +141,8 @@ def on(t, device, dtype=torch.float32):
     """t as a contiguous tensor of `dtype` on `device` (a copy when it is elsewhere or strided)."""
     if not isinstance(t, torch.Tensor):
         t = torch.as_tensor(t)
+    if t.dtype == dtype and t.device == device and t.is_contiguous():
+        return t
     return t.detach().to(device=device, dtype=dtype).contiguous()
 
 
@@ -181,5 +183,28 @@ class using:
 
 def run(name, device, *args):
     """call() with `device` current; the last argument of every entry point is the stream, appended here."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx == torch.cuda.current_device():                 # the usual case: no device switch
+        call(name, *args, stream(device))
+        return
     with torch.cuda.device(device):
         call(name, *args, stream(device))
+
+
+def cached(make):
+    """`make` memoised on its (hashable) arguments, for building the small spec structs of a call: the structs are
+    only read by the library (const pointers), so one object can serve every call with the same arguments.
+    Unhashable arguments (a Format object, a list) build a fresh struct."""
+    memo = {}
+
+    def get(*args):
+        try:
+            return memo[args]
+        except KeyError:
+            if len(memo) >= 256:                            # e.g. NaN arguments, which never compare equal
+                memo.clear()
+            s = memo[args] = make(*args)
+            return s
+        except TypeError:
+            return make(*args)
+    return get

@@ -28,12 +28,14 @@ def spec(fmt, rounding_mode="ties_away", scale_floor=scale_factor.MXQUANT_FLOOR,
     return _lib.MxqQuantSpec(2, f.e, f.m, code, float(np.float32(scale_floor)), 0, 0.0, ve, vm)
 
 
+_spec = _lib.cached(spec)                  # quantize's own calls share one struct per argument set
+
 def quantize(V: torch.Tensor, fmt: Union[str, Format], axis: int = 0, block_size: int = _driver.BLOCK,
              rounding_mode: str = "ties_away",
              scale_floor: float = scale_factor.MXQUANT_FLOOR,
              via: Optional[Tuple[int, int]] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """MX-Gemmini block quantize V along `axis`. Returns (P codes, X power-of-two scales), float32."""
-    return _driver.quantize_fused(V, spec(fmt, rounding_mode, scale_floor, via), axis, block_size)
+    return _driver.quantize_fused(V, _spec(fmt, rounding_mode, scale_floor, via), axis, block_size)
 
 
 def quantize_packed(V: torch.Tensor, fmt: Union[str, Format], axis: int = 0, block_size: int = _driver.BLOCK,

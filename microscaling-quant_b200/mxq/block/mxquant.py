@@ -22,10 +22,12 @@ def spec(fmt) -> "_lib.MxqQuantSpec":
     return _lib.MxqQuantSpec(1, f.e, f.m, 0, float(np.float32(scale_factor.MXQUANT_FLOOR)), 0, 0.0, 0, 0)
 
 
+_spec = _lib.cached(spec)                  # quantize's own calls share one struct per argument set
+
 def quantize(V: torch.Tensor, fmt: Union[str, Format], axis: int = 0,
              block_size: int = _driver.BLOCK) -> Tuple[torch.Tensor, torch.Tensor]:
     """MXQuant-simulation block quantize V along `axis`. Returns (P codes, X power-of-two scales), float32."""
-    return _driver.quantize_fused(V, spec(fmt), axis, block_size)
+    return _driver.quantize_fused(V, _spec(fmt), axis, block_size)
 
 
 def dequantize(P: torch.Tensor, X: torch.Tensor, axis: int = 0, block_size: int = _driver.BLOCK) -> torch.Tensor:

@@ -29,10 +29,12 @@ def spec(fmt, rounding_mode="even", scale_bits=8, placement="top") -> "_lib.MxqQ
                              scale_factor.scale_emax(scale_bits), 0, 0)
 
 
+_spec = _lib.cached(spec)                  # quantize's own calls share one struct per argument set
+
 def quantize(V: torch.Tensor, fmt: Union[str, Format], axis: int = 0, block_size: int = _driver.BLOCK,
              rounding_mode: str = "even", scale_bits: int = 8, placement: str = "top") -> Tuple[torch.Tensor, torch.Tensor]:
     """OCP block quantize V along `axis`. Returns (P codes, X power-of-two scales), float32."""
-    return _driver.quantize_fused(V, spec(fmt, rounding_mode, scale_bits, placement), axis, block_size)
+    return _driver.quantize_fused(V, _spec(fmt, rounding_mode, scale_bits, placement), axis, block_size)
 
 
 def quantize_packed(V: torch.Tensor, fmt: Union[str, Format], axis: int = 0, block_size: int = _driver.BLOCK,

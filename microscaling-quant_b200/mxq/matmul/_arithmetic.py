@@ -42,11 +42,18 @@ class ArithSpec:
     sat_value: float = 0.0
 
     def c_struct(self) -> "_lib.MxqArith":
+        """The struct the reducer entry points read (const): one per spec, built on first use."""
+        return _c_struct(self)
+
+    def _make_c_struct(self) -> "_lib.MxqArith":
         if self.kind == "mxquant":
             return _lib.MxqArith(0, self.prod_e, self.prod_m, 0, 0.0, 0.0, 0.0)
         thr = float(np.float32(2.0 ** self.prod_floor)) if self.prod_floor is not None else 0.0
         return _lib.MxqArith(1, self.prod_e, self.prod_m, int(self.prod_floor is not None), thr,
                              float(np.float32(self.sat_limit)), float(np.float32(self.sat_value)))
+
+
+_c_struct = _lib.cached(ArithSpec._make_c_struct)
 
 
 @dataclass(frozen=True)

@@ -54,8 +54,20 @@ def operands(P_A, X_A, P_B, X_B):
     return [_lib.on(t, dev) for t in (P_A, X_A, P_B, X_B)], dev, home
 
 
-def int_pairs(pairs):
+def _make_int_pairs(pairs):
     import ctypes
     es = (ctypes.c_int32 * max(1, len(pairs)))(*[int(e) for e, _ in pairs])
     ms = (ctypes.c_int32 * max(1, len(pairs)))(*[int(m) for _, m in pairs])
     return es, ms
+
+
+_int_pairs = _lib.cached(_make_int_pairs)
+
+
+def int_pairs(pairs):
+    """A schedule as the two int32 arrays the entry points read (const): built once per schedule."""
+    try:
+        key = tuple((int(e), int(m)) for e, m in pairs)
+    except (TypeError, ValueError):
+        return _make_int_pairs(pairs)
+    return _int_pairs(key)
