@@ -154,6 +154,16 @@ def stream(device):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream_of(index):
+    """The current stream of device `index` as a cudaStream_t (torch's raw getter when it has one)."""
+    if _raw_stream is not None:
+        return ctypes.c_void_p(_raw_stream(index))
+    return ctypes.c_void_p(torch.cuda.current_stream(index).cuda_stream)
+
+
 def back(t, like_device):
     """Return a result to the caller's device (the reference's tensors stay where they were)."""
     return t if like_device is None or t.device == like_device else t.to(like_device)
@@ -183,12 +193,13 @@ class using:
 
 def run(name, device, *args):
     """call() with `device` current; the last argument of every entry point is the stream, appended here."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    if idx == torch.cuda.current_device():                 # the usual case: no device switch
-        call(name, *args, stream(device))
+    cur = torch.cuda.current_device()
+    idx = device.index if device.index is not None else cur
+    if idx == cur:                                          # the usual case: no device switch
+        call(name, *args, _stream_of(idx))
         return
     with torch.cuda.device(device):
-        call(name, *args, stream(device))
+        call(name, *args, _stream_of(idx))
 
 
 def cached(make):

@@ -14,6 +14,8 @@ and X once (mxq_block_quantize).
 """
 from typing import Callable, NamedTuple, Optional, Tuple
 
+import ctypes as _ctypes
+
 import torch
 
 from .. import _lib
@@ -218,9 +220,10 @@ def quantize_fused(V: torch.Tensor, spec: "_lib.MxqQuantSpec", axis: int, block_
     xshape = list(V.shape)
     xshape[axis_] = nb
     X = torch.empty(xshape, dtype=torch.float32, device=dev)
-    import ctypes
     _lib.run("mxq_block_quantize", dev, _lib.ptr(v), _lib.ptr(P), _lib.ptr(X), outer, L, inner, block_size,
-             ctypes.byref(spec))
+             _ctypes.byref(spec))
+    if home == dev:
+        return P, X
     return _lib.back(P, home), _lib.back(X, home)
 
 
