@@ -481,10 +481,13 @@ def child(only):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("MXQ_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("MXQ_REFERENCE"),
+                    help="the reference checkout to import (default: $MXQ_REFERENCE)")
     ap.add_argument("--only", nargs="*", default=[])
     ap.add_argument("--child", action="store_true")
     a = ap.parse_args()
+    if not a.child and not a.reference:
+        ap.error("give the reference checkout with --reference or $MXQ_REFERENCE")
     if a.child:
         child(set(a.only))
         return
