@@ -4,8 +4,9 @@
 //
 // Kernels (each templated on the quantizer family so the element step is inlined). The TMA-staged kernel of
 // quantize_tma.cu takes every layout it can map; these register kernels cover the rest:
-//   k_rows32   inner == 1, block == 32, len % 32 == 0, 16-byte aligned: one float4 per thread, 8 lanes per block,
-//              the block max by three xor-shuffles; fully coalesced 128-bit loads and stores.
+//   k_rows<QB> inner == 1, block a power of two from 4 to 128, len % block == 0, 16-byte aligned: one float4 per
+//              thread, QB = block / 4 lanes per block, the block max by log2(QB) xor-shuffles; fully coalesced
+//              128-bit loads and stores.
 //   k_cols_tile  inner % 4 == 0, block == 32, 16-byte aligned: one CTA per 32-row block x 256 columns; each thread
 //              keeps 8 float4 of 4 columns in registers, the four row groups' column maxima meet in shared memory,
 //              and every load and store is a coalesced 128-bit access along the rows.
@@ -100,12 +101,12 @@ struct AbsMax {
 
 constexpr int kThreads = 256;
 
-template <int FAM>
-__global__ void __launch_bounds__(kThreads) k_rows32(const float4* __restrict__ V, float4* __restrict__ P,
-                                                     float* __restrict__ X, int64_t nquads, QParams q) {
-  // a quad is 4 consecutive values; 8 quads make a block; a warp covers 4 blocks per step. The loop runs per warp
-  // (every lane takes every trip, so the full-mask shuffles always see 32 lanes); nquads is a multiple of 8, so a
-  // block is either wholly inside or wholly past the end.
+template <int FAM, int QB>
+__global__ void __launch_bounds__(kThreads) k_rows(const float4* __restrict__ V, float4* __restrict__ P,
+                                                   float* __restrict__ X, int64_t nquads, QParams q) {
+  // a quad is 4 consecutive values; QB quads (QB = 1..32, a power of two) make a block; a warp covers 32 / QB blocks
+  // per step. The loop runs per warp (every lane takes every trip, so the full-mask shuffles always see 32 lanes);
+  // nquads is a multiple of QB, so a block is either wholly inside or wholly past the end.
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int lane = threadIdx.x & 31;
   for (int64_t w = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); w < nquads; w += stride) {
@@ -115,14 +116,14 @@ __global__ void __launch_bounds__(kThreads) k_rows32(const float4* __restrict__ 
     float a = fmaxf(fmaxf(abs_f(v.x), abs_f(v.y)), fmaxf(abs_f(v.z), abs_f(v.w)));
     unsigned nan = isnan_f(v.x) | isnan_f(v.y) | isnan_f(v.z) | isnan_f(v.w);
 #pragma unroll
-    for (int s = 1; s < 8; s <<= 1) {
+    for (int s = 1; s < QB; s <<= 1) {
       a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, s));
       nan |= __shfl_xor_sync(0xffffffffu, nan, s);
     }
     float amax = nan ? qnan_f() : a;
     float x = (FAM == MXQ_FAMILY_FP32) ? 1.0f : block_scale<FAM>(amax, q);
     if (!live) continue;
-    if ((lane & 7) == 0) X[t >> 3] = x;
+    if ((lane & (QB - 1)) == 0) X[t / QB] = x;
     float4 o;
     if (FAM == MXQ_FAMILY_FP32) {
       o = v;
@@ -285,10 +286,21 @@ int launch_quant(const float* V, float* P, float* X, int64_t outer, int64_t len,
   if (r != MXQ_ERR_UNSUPPORTED) return r;
   int64_t nb = (len + block - 1) / block;
   bool al16 = ((uintptr_t)V % 16 == 0) && ((uintptr_t)P % 16 == 0);
-  if (block == 32 && inner == 1 && len % 32 == 0 && al16) {
-    int64_t nquads = outer * len / 4;
-    k_rows32<FAM><<<grid_for(nquads, kThreads, 16), kThreads, 0, st>>>(
-        reinterpret_cast<const float4*>(V), reinterpret_cast<float4*>(P), X, nquads, q);
+  const bool pow2 = block >= 4 && block <= 128 && (block & (block - 1)) == 0;
+  if (pow2 && inner == 1 && len % block == 0 && al16) {
+    // rows of whole blocks of 4..128 values: a block is QB = block / 4 lanes' float4
+    const int64_t nquads = outer * len / 4;
+    const unsigned grid = grid_for(nquads, kThreads, 16);
+    auto V4 = reinterpret_cast<const float4*>(V);
+    auto P4 = reinterpret_cast<float4*>(P);
+    switch (block) {
+      case 4: k_rows<FAM, 1><<<grid, kThreads, 0, st>>>(V4, P4, X, nquads, q); break;
+      case 8: k_rows<FAM, 2><<<grid, kThreads, 0, st>>>(V4, P4, X, nquads, q); break;
+      case 16: k_rows<FAM, 4><<<grid, kThreads, 0, st>>>(V4, P4, X, nquads, q); break;
+      case 32: k_rows<FAM, 8><<<grid, kThreads, 0, st>>>(V4, P4, X, nquads, q); break;
+      case 64: k_rows<FAM, 16><<<grid, kThreads, 0, st>>>(V4, P4, X, nquads, q); break;
+      default: k_rows<FAM, 32><<<grid, kThreads, 0, st>>>(V4, P4, X, nquads, q); break;
+    }
   } else if (block == 32 && inner > 1) {
     if (inner % 4 == 0 && al16 && (uintptr_t)X % 16 == 0) {
       int64_t tiles = outer * nb * ((inner / 4 + 63) / 64);

@@ -85,6 +85,22 @@ def test_block_layout_paths(oracle):
             assert_bits(X, Xo, f"{shape} {axis} {bs} {family} X")
 
 
+@pytest.mark.parametrize("bs", [4, 8, 16, 64, 128])
+def test_block_rows_pow2_blocks(oracle, bs):
+    """Blocks of 4 to 128 values along rows (the row kernel with bs / 4 lanes per block), with Inf, NaN and zero
+    blocks, every family; a row length that is not a whole number of blocks takes the generic kernel."""
+    rng = np.random.default_rng(bs)
+    for shape in ((24, 256), (24, 3 * bs + (4 if bs >= 8 else 1))):
+        V = (rng.standard_normal(shape) * 2.0 ** rng.uniform(-20, 20, (shape[0], 1))).astype(np.float32)
+        V[1, 3], V[2, 5], V[3, 0:bs] = np.inf, np.nan, 0.0
+        for family, fmt in (("mxquant", "MXFP6_E3M2"), ("mxgemmini", "MXFP8_E4M3"), ("ocp", "MXFP4")):
+            keep = ~nan_block_mask(V, 1, bs) if family == "mxquant" else np.ones(V.shape, bool)
+            P, X = prod.block_quantize(V, family, fmt, 1, bs)
+            Po, Xo = oracle.block_quantize(V, family, fmt, 1, bs)
+            assert_bits_where(P, Po, keep, f"{shape} {bs} {family} P")
+            assert_bits(X, Xo, f"{shape} {bs} {family} X")
+
+
 def test_block_host_streamed(monkeypatch):
     """A host tensor streams through the device in chunks (whole outer slices, or runs of blocks inside a slice,
     the last one short); the chunked result must equal the one-shot device result bit for bit."""
