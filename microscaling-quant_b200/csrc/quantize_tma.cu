@@ -6,10 +6,11 @@
 // flight per SM, and each launch ended on a partial round of 32 KB tiles.)
 //
 // Two layouts of the [outer, len, inner] view (blocks of 32 along len):
-//   ROWS (inner == 1): a tile is 32 rows x TC consecutive values of a row, i.e. TC / 32 blocks per row;
+//   ROWS (inner == 1): a tile is 32 rows x TC consecutive values of a row, i.e. TC / BS blocks per row (blocks of
+//                      BS = 16, 32 or 64);
 //   COLS (inner > 1):  a tile is one block of 32 rows (along len) x TC columns (along inner).
 // Per tile: (1) one thread per block takes the block max from shared memory and computes the block's scale and
-// reciprocal (ROWS: a thread reads its block's 8 float4 in a rotated order, so a quarter-warp hits 32 distinct
+// reciprocal (ROWS: a thread reads its block's BS / 4 float4 in a rotated order, so a quarter-warp hits distinct
 // banks; COLS: a thread walks its column), and the CTA votes whether every block is clean (finite, with a
 // power-of-two scale); (2) every thread quantizes its float4 of the tile, reading values and scales from shared
 // memory and writing P with coalesced 128-bit streaming stores -- a clean tile with the short element step.
@@ -24,7 +25,6 @@ namespace {
 
 constexpr int TR = 32, TC = 256, NT = 256;
 constexpr int C4 = TC / 4;              // float4 per tile row
-constexpr int BPR = TC / 32;            // blocks per tile row (ROWS layout)
 constexpr int RPI = NT / C4;            // tile rows per pass of the CTA in the element step
 static_assert(TC % 32 == 0 && TC <= NT && NT % C4 == 0 && TR % RPI == 0, "tile shape");
 constexpr unsigned TILE_BYTES = TR * TC * sizeof(float);   // 32 KB: below the 48 KB default, no attribute needed
@@ -235,7 +235,7 @@ __device__ __forceinline__ TileAt tile_at(int64_t tile, uint32_t ctiles, uint32_
 }
 
 // (2) for a clean tile: every thread quantizes TR / RPI float4 (float4 q = tid + NT i: row q / C4, column q % C4)
-template <int FAM, int E, int M, bool COLS, int MODE, bool VIA, class Out>
+template <int FAM, int E, int M, bool COLS, int BS, int MODE, bool VIA, class Out>
 __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out& out, const TileAt& at,
                                            int64_t outer, int64_t len, int64_t inner, int via_e, int via_m) {
   const int tid = threadIdx.x, c4 = tid % C4;
@@ -246,7 +246,7 @@ __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out
     const int row = tid / C4 + RPI * i;
     float4 v = reinterpret_cast<const float4*>(T + row * TC)[c4];
     if (!COLS) {
-      const float r = s_r[row * BPR + (c4 >> 3)];
+      const float r = s_r[row * (TC / BS) + (int)((unsigned)c4 / (BS / 4))];
       rs = make_float4(r, r, r, r);
     }
     v.x = element_clean<FAM, E, M, MODE, VIA>(__fmul_rn(v.x, rs.x), via_e, via_m);
@@ -263,17 +263,22 @@ __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out
   }
 }
 
-template <int FAM, int E, int M, bool COLS, class Out>
+// BS: the block length, 32 for COLS (a tile is one block of TR = 32 rows); 16, 32 or 64 for ROWS
+template <int FAM, int E, int M, bool COLS, int BS, class Out>
 __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtensorMap tmap, Out out, int64_t outer,
                                                   int64_t len, int64_t inner, TParams prm) {
   extern __shared__ __align__(128) float T[];               // [TR][TC]: this CTA's tile
   __shared__ __align__(8) uint64_t bar;
-  __shared__ __align__(16) float s_x[TC];                   // read as float4 (COLS): 16-byte aligned
-  __shared__ __align__(16) float s_r[TC];
+  static_assert(!COLS || BS == TR, "COLS tiles are one block of TR rows");
+  static_assert(BS >= 4 && TC % BS == 0, "ROWS blocks tile the tile row");
+  constexpr int BPR = TC / BS;                              // blocks per tile row (ROWS)
+  constexpr int NBT = COLS ? TC : TR * BPR;                 // blocks per tile
+  __shared__ __align__(16) float s_x[NBT];                  // read as float4 (COLS): 16-byte aligned
+  __shared__ __align__(16) float s_r[NBT];
 
   const int tid = threadIdx.x;
   // tile grid: ROWS -> (row tiles, column tiles) of the [outer, len] matrix; COLS -> (outer, blocks, column tiles)
-  const int64_t nb = (len + TR - 1) / TR;
+  const int64_t nb = (len + BS - 1) / BS;                  // blocks along len
   const int64_t ctiles = COLS ? (inner + TC - 1) / TC : (len + TC - 1) / TC;
   const TileAt at = tile_at<COLS>(blockIdx.x, (uint32_t)ctiles, (uint32_t)nb);
   const int64_t ct = at.ct, rest = at.rest;
@@ -315,23 +320,31 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     bad = col < inner && (mbits >= 0x7f800000u || r == 0.0f);       // padding columns do not vote
     if (col < inner) out.scale((at.o * nb + at.b) * inner + col, x);
   } else {
-    const int row = tid / BPR, blk = tid % BPR;              // TR rows x BPR blocks
-    const float4* src = reinterpret_cast<const float4*>(T + row * TC + blk * 32);
-    uint32_t mbits = 0u;                                    // max |v| as bits: a NaN pattern tops every number
+    constexpr int QB = BS / 4;                              // float4 per block
+    auto one = [&](int bi) {                                // block bi of the tile: row bi / BPR, block bi % BPR
+      const int row = bi / BPR, blk = bi % BPR;
+      const float4* src = reinterpret_cast<const float4*>(T + row * TC + blk * BS);
+      uint32_t mbits = 0u;                                  // max |v| as bits: a NaN pattern tops every number
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const float4 v = src[(i + tid) & 7];
-      mbits = max(max(mbits, f2u(v.x) & 0x7fffffffu), max(f2u(v.y) & 0x7fffffffu, f2u(v.z) & 0x7fffffffu));
-      mbits = max(mbits, f2u(v.w) & 0x7fffffffu);
+      for (int i = 0; i < QB; i++) {
+        const float4 v = src[(i + bi) & (QB - 1)];           // rotated: a quarter-warp spreads over the banks
+        mbits = max(max(mbits, f2u(v.x) & 0x7fffffffu), max(f2u(v.y) & 0x7fffffffu, f2u(v.z) & 0x7fffffffu));
+        mbits = max(mbits, f2u(v.w) & 0x7fffffffu);
+      }
+      const bool nan = mbits > 0x7f800000u;
+      const float x = block_scale<FAM, E, M>(nan ? qnan_f() : u2f(mbits), prm);
+      const float r = reciprocal_of<FAM>(x, nan);
+      s_x[bi] = x;
+      s_r[bi] = r;
+      const int64_t grow = rest * TR + row, gblk = ct * BPR + blk;
+      bad |= grow < outer && gblk < nb && (mbits >= 0x7f800000u || r == 0.0f);  // padding blocks do not vote
+      if (grow < outer && gblk < nb) out.scale(grow * nb + gblk, x);
+    };
+    if constexpr (NBT == NT) {                              // blocks of 32: one per thread
+      one(tid);
+    } else {
+      for (int bi = tid; bi < NBT; bi += NT) one(bi);
     }
-    const bool nan = mbits > 0x7f800000u;
-    const float x = block_scale<FAM, E, M>(nan ? qnan_f() : u2f(mbits), prm);
-    const float r = reciprocal_of<FAM>(x, nan);
-    s_x[tid] = x;
-    s_r[tid] = r;
-    const int64_t grow = rest * TR + row, gblk = ct * (TC / 32) + blk;
-    bad = grow < outer && gblk < nb && (mbits >= 0x7f800000u || r == 0.0f);     // padding blocks do not vote
-    if (grow < outer && gblk < nb) out.scale(grow * nb + gblk, x);
   }
   // the whole tile takes the short element step (with a via pre-rounding in q_ieee_small's range)
   const bool via = FAM == MXQ_FAMILY_MXGEMMINI && prm.via_e != 0;
@@ -341,21 +354,21 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     if constexpr (FAM == MXQ_FAMILY_MXGEMMINI) {
       if (via) {
         if (prm.rounding == 0)
-          pass_clean<FAM, E, M, COLS, 0, true>(T, s_r, out, at, outer, len, inner, prm.via_e, prm.via_m);
+          pass_clean<FAM, E, M, COLS, BS, 0, true>(T, s_r, out, at, outer, len, inner, prm.via_e, prm.via_m);
         else if (prm.rounding == 1)
-          pass_clean<FAM, E, M, COLS, 1, true>(T, s_r, out, at, outer, len, inner, prm.via_e, prm.via_m);
+          pass_clean<FAM, E, M, COLS, BS, 1, true>(T, s_r, out, at, outer, len, inner, prm.via_e, prm.via_m);
         else
-          pass_clean<FAM, E, M, COLS, 2, true>(T, s_r, out, at, outer, len, inner, prm.via_e, prm.via_m);
+          pass_clean<FAM, E, M, COLS, BS, 2, true>(T, s_r, out, at, outer, len, inner, prm.via_e, prm.via_m);
         out.finish();
         return;
       }
     }
     if (FAM == MXQ_FAMILY_MXQUANT || prm.rounding == 0)
-      pass_clean<FAM, E, M, COLS, 0, false>(T, s_r, out, at, outer, len, inner, 0, 0);
+      pass_clean<FAM, E, M, COLS, BS, 0, false>(T, s_r, out, at, outer, len, inner, 0, 0);
     else if (prm.rounding == 1)
-      pass_clean<FAM, E, M, COLS, 1, false>(T, s_r, out, at, outer, len, inner, 0, 0);
+      pass_clean<FAM, E, M, COLS, BS, 1, false>(T, s_r, out, at, outer, len, inner, 0, 0);
     else
-      pass_clean<FAM, E, M, COLS, 2, false>(T, s_r, out, at, outer, len, inner, 0, 0);
+      pass_clean<FAM, E, M, COLS, BS, 2, false>(T, s_r, out, at, outer, len, inner, 0, 0);
     out.finish();
     return;
   }
@@ -372,7 +385,7 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     const int row = tid / C4 + RPI * i;
     float4 v = reinterpret_cast<const float4*>(T + row * TC)[c4];
     if (!COLS) {
-      const int b = row * BPR + (c4 >> 3);
+      const int b = row * BPR + (int)((unsigned)c4 / (BS / 4));
       const float x = s_x[b], r = s_r[b];
       xs = make_float4(x, x, x, x);
       rs = make_float4(r, r, r, r);
@@ -395,13 +408,13 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
 // One CTA per tile: the hardware's block scheduler streams the tiles, so every SM keeps several tiles' loads in
 // flight (one 32 KB TMA load per resident CTA) while other CTAs quantize and store, and the last tiles of a launch
 // spread over the SMs a CTA at a time. Launched as a programmatic dependent (PDL) of the kernel before it.
-template <int FAM, int E, int M, class Out>
+template <int FAM, int E, int M, int BS, class Out>
 int launch(const CUtensorMap& map, bool cols, Out out, int64_t outer, int64_t len, int64_t inner,
            const TParams& prm, cudaStream_t st) {
-  const int64_t nb = (len + TR - 1) / TR;
+  const int64_t nb = (len + TR - 1) / TR;                  // COLS: blocks of TR rows
   const int64_t ntiles = cols ? outer * nb * ((inner + TC - 1) / TC) : ((outer + TR - 1) / TR) * ((len + TC - 1) / TC);
   if (ntiles >= (1ll << 31)) return MXQ_ERR_UNSUPPORTED;   // one CTA per tile; 32-bit tile coordinates
-  auto kern = cols ? k_quant_tma<FAM, E, M, true, Out> : k_quant_tma<FAM, E, M, false, Out>;
+  auto kern = cols ? k_quant_tma<FAM, E, M, true, TR, Out> : k_quant_tma<FAM, E, M, false, BS, Out>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)ntiles);
   cfg.blockDim = dim3(NT);
@@ -426,22 +439,28 @@ struct Dest {
   int* status;
 };
 
+// block: 32 for every layout and output; 16 or 64 for ROWS with float outputs (the launcher checks)
 template <int FAM, int E, int M>
 int launch_dest(const CUtensorMap& map, bool cols, const Dest& d, int64_t outer, int64_t len, int64_t inner,
-                const TParams& prm, cudaStream_t st) {
-  if (d.Pc == nullptr) return launch<FAM, E, M>(map, cols, OutF{d.P, d.X}, outer, len, inner, prm, st);
+                int64_t block, const TParams& prm, cudaStream_t st) {
+  if (d.Pc == nullptr) {
+    const OutF o{d.P, d.X};
+    if (block == 16) return launch<FAM, E, M, 16>(map, cols, o, outer, len, inner, prm, st);
+    if (block == 64) return launch<FAM, E, M, 64>(map, cols, o, outer, len, inner, prm, st);
+    return launch<FAM, E, M, 32>(map, cols, o, outer, len, inner, prm, st);
+  }
   if (FAM == MXQ_FAMILY_MXQUANT) return MXQ_ERR_UNSUPPORTED;          // the qtorch grid is not the OCP one
-  return launch<FAM, E, M>(map, cols, OutPack<E, M>{d.Pc, d.Xc, d.status}, outer, len, inner, prm, st);
+  return launch<FAM, E, M, 32>(map, cols, OutPack<E, M>{d.Pc, d.Xc, d.status}, outer, len, inner, prm, st);
 }
 
 template <int FAM>
 int launch_fmt(int e, int m, const CUtensorMap& map, bool cols, const Dest& d, int64_t outer, int64_t len,
-               int64_t inner, const TParams& prm, cudaStream_t st) {
-  if (e == 4 && m == 3) return launch_dest<FAM, 4, 3>(map, cols, d, outer, len, inner, prm, st);
-  if (e == 5 && m == 2) return launch_dest<FAM, 5, 2>(map, cols, d, outer, len, inner, prm, st);
-  if (e == 3 && m == 2) return launch_dest<FAM, 3, 2>(map, cols, d, outer, len, inner, prm, st);
-  if (e == 2 && m == 3) return launch_dest<FAM, 2, 3>(map, cols, d, outer, len, inner, prm, st);
-  if (e == 2 && m == 1) return launch_dest<FAM, 2, 1>(map, cols, d, outer, len, inner, prm, st);
+               int64_t inner, int64_t block, const TParams& prm, cudaStream_t st) {
+  if (e == 4 && m == 3) return launch_dest<FAM, 4, 3>(map, cols, d, outer, len, inner, block, prm, st);
+  if (e == 5 && m == 2) return launch_dest<FAM, 5, 2>(map, cols, d, outer, len, inner, block, prm, st);
+  if (e == 3 && m == 2) return launch_dest<FAM, 3, 2>(map, cols, d, outer, len, inner, block, prm, st);
+  if (e == 2 && m == 3) return launch_dest<FAM, 2, 3>(map, cols, d, outer, len, inner, block, prm, st);
+  if (e == 2 && m == 1) return launch_dest<FAM, 2, 1>(map, cols, d, outer, len, inner, block, prm, st);
   return MXQ_ERR_UNSUPPORTED;
 }
 
@@ -449,12 +468,15 @@ int launch_fmt(int e, int m, const CUtensorMap& map, bool cols, const Dest& d, i
 
 namespace mxq {
 
-// The TMA kernel for blocks of 32 when the layout allows a tensor map (16-byte aligned base, rows a multiple of 16
+// The TMA kernel for blocks of 32 (and 16 or 64 along rows, float outputs) when the layout allows a tensor map (16-byte aligned base, rows a multiple of 16
 // bytes, extents below 2^31); MXQ_ERR_UNSUPPORTED otherwise (the caller then takes the register kernels).
 int quantize_tma_dest(const float* V, const Dest& d, int64_t outer, int64_t len, int64_t inner, int64_t block,
                       const mxq_quant_spec& s, cudaStream_t st) {
-  if (block != 32 || s.family == MXQ_FAMILY_FP32) return MXQ_ERR_UNSUPPORTED;
   const bool cols = inner > 1;
+  // blocks of 32 in every layout; blocks of 16 or 64 along rows (ROWS tiles hold any block dividing 256) with
+  // float outputs
+  const bool rows_block = !cols && d.Pc == nullptr && (block == 16 || block == 64);
+  if ((block != 32 && !rows_block) || s.family == MXQ_FAMILY_FP32) return MXQ_ERR_UNSUPPORTED;
   const int64_t rowlen = cols ? inner : len;
   const uintptr_t out_base = d.Pc ? (uintptr_t)d.Pc : (uintptr_t)d.P;
   if ((uintptr_t)V % 16 || out_base % 16 || rowlen % 4 || outer >= (1ll << 31) || len >= (1ll << 31) ||
@@ -474,10 +496,10 @@ int quantize_tma_dest(const float* V, const Dest& d, int64_t outer, int64_t len,
   }
   TParams prm{s.rounding, s.placement, s.via_e, s.via_m, s.scale_floor, s.scale_emax};
   switch (s.family) {
-    case MXQ_FAMILY_MXQUANT: return launch_fmt<MXQ_FAMILY_MXQUANT>(s.e, s.m, map, cols, d, outer, len, inner, prm, st);
+    case MXQ_FAMILY_MXQUANT: return launch_fmt<MXQ_FAMILY_MXQUANT>(s.e, s.m, map, cols, d, outer, len, inner, block, prm, st);
     case MXQ_FAMILY_MXGEMMINI:
-      return launch_fmt<MXQ_FAMILY_MXGEMMINI>(s.e, s.m, map, cols, d, outer, len, inner, prm, st);
-    default: return launch_fmt<MXQ_FAMILY_OCP>(s.e, s.m, map, cols, d, outer, len, inner, prm, st);
+      return launch_fmt<MXQ_FAMILY_MXGEMMINI>(s.e, s.m, map, cols, d, outer, len, inner, block, prm, st);
+    default: return launch_fmt<MXQ_FAMILY_OCP>(s.e, s.m, map, cols, d, outer, len, inner, block, prm, st);
   }
 }
 
