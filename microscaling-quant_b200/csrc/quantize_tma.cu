@@ -5,10 +5,10 @@
 // through tiles with a two- or three-stage pipeline measured 11-12% slower on the same sweep: fewer loads in
 // flight per SM, and each launch ended on a partial round of 32 KB tiles.)
 //
-// Two layouts of the [outer, len, inner] view (blocks of 32 along len):
+// Two layouts of the [outer, len, inner] view (blocks of BS along len; BS = 32, or 16 / 64 with float outputs):
 //   ROWS (inner == 1): a tile is 32 rows x TC consecutive values of a row, i.e. TC / BS blocks per row (blocks of
 //                      BS = 16, 32 or 64);
-//   COLS (inner > 1):  a tile is one block of 32 rows (along len) x TC columns (along inner).
+//   COLS (inner > 1):  a tile is one block of BS rows (along len; BS = 16 or 32) x TC columns (along inner).
 // Per tile: (1) one thread per block takes the block max from shared memory and computes the block's scale and
 // reciprocal (ROWS: a thread reads its block's BS / 4 float4 in a rotated order, so a quarter-warp hits distinct
 // banks; COLS: a thread walks its column), and the CTA votes whether every block is clean (finite, with a
@@ -27,7 +27,7 @@ constexpr int TR = 32, TC = 256, NT = 256;
 constexpr int C4 = TC / 4;              // float4 per tile row
 constexpr int RPI = NT / C4;            // tile rows per pass of the CTA in the element step
 static_assert(TC % 32 == 0 && TC <= NT && NT % C4 == 0 && TR % RPI == 0, "tile shape");
-constexpr unsigned TILE_BYTES = TR * TC * sizeof(float);   // 32 KB: below the 48 KB default, no attribute needed
+// a tile is at most TR x TC floats: 32 KB, below the 48 KB default, no shared-memory attribute needed
 
 struct TParams {
   int rounding, placement, via_e, via_m;
@@ -242,7 +242,7 @@ __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out
   float4 rs;
   if (COLS) rs = *reinterpret_cast<const float4*>(s_r + c4 * 4);
 #pragma unroll 2
-  for (int i = 0; i < TR / RPI; i++) {
+  for (int i = 0; i < (COLS ? BS : TR) / RPI; i++) {
     const int row = tid / C4 + RPI * i;
     float4 v = reinterpret_cast<const float4*>(T + row * TC)[c4];
     if (!COLS) {
@@ -254,7 +254,7 @@ __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out
     v.z = element_clean<FAM, E, M, MODE, VIA>(__fmul_rn(v.z, rs.z), via_e, via_m);
     v.w = element_clean<FAM, E, M, MODE, VIA>(__fmul_rn(v.w, rs.w), via_e, via_m);
     if (COLS) {
-      const int64_t l = at.b * TR + row, col = at.ct * TC + c4 * 4;
+      const int64_t l = at.b * BS + row, col = at.ct * TC + c4 * 4;
       if (l < len && col < inner) out.template codes<true>((at.o * len + l) * inner + col, v);
     } else {
       const int64_t grow = at.rest * TR + row, col = at.ct * TC + c4 * 4;
@@ -263,13 +263,13 @@ __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out
   }
 }
 
-// BS: the block length, 32 for COLS (a tile is one block of TR = 32 rows); 16, 32 or 64 for ROWS
+// BS: the block length: 16 or 32 for COLS (a tile is one block of BS rows), 16, 32 or 64 for ROWS
 template <int FAM, int E, int M, bool COLS, int BS, class Out>
 __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtensorMap tmap, Out out, int64_t outer,
                                                   int64_t len, int64_t inner, TParams prm) {
-  extern __shared__ __align__(128) float T[];               // [TR][TC]: this CTA's tile
+  extern __shared__ __align__(128) float T[];               // [TRB][TC]: this CTA's tile
   __shared__ __align__(8) uint64_t bar;
-  static_assert(!COLS || BS == TR, "COLS tiles are one block of TR rows");
+  constexpr int TRB = COLS ? BS : TR;                       // tile rows
   static_assert(BS >= 4 && TC % BS == 0, "ROWS blocks tile the tile row");
   constexpr int BPR = TC / BS;                              // blocks per tile row (ROWS)
   constexpr int NBT = COLS ? TC : TR * BPR;                 // blocks per tile
@@ -294,8 +294,8 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
   __syncthreads();
   if (tid == 0) {
     fence_proxy_async();
-    mbar_expect_tx(&bar, TILE_BYTES);
-    if (COLS) tma_load_3d(T, &tmap, (int)(ct * TC), (int)(at.b * TR), (int)at.o, &bar);
+    mbar_expect_tx(&bar, (unsigned)(TRB * TC * sizeof(float)));
+    if (COLS) tma_load_3d(T, &tmap, (int)(ct * TC), (int)(at.b * BS), (int)at.o, &bar);
     else tma_load_2d(T, &tmap, (int)(ct * TC), (int)(rest * TR), &bar);
   }
   // every thread waits; the CTA leaves together if the (bounded) wait gave up anywhere
@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     const int64_t col = ct * TC + tid;
     uint32_t mbits = 0u;                                    // max |v| as bits: a NaN pattern tops every number
 #pragma unroll 8
-    for (int r = 0; r < TR; r++) mbits = max(mbits, f2u(T[r * TC + tid]) & 0x7fffffffu);
+    for (int r = 0; r < TRB; r++) mbits = max(mbits, f2u(T[r * TC + tid]) & 0x7fffffffu);
     const bool nan = mbits > 0x7f800000u;
     const float x = block_scale<FAM, E, M>(nan ? qnan_f() : u2f(mbits), prm);
     const float r = reciprocal_of<FAM>(x, nan);
@@ -381,7 +381,7 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     rs = *reinterpret_cast<const float4*>(s_r + c4 * 4);
   }
 #pragma unroll 2
-  for (int i = 0; i < TR / RPI; i++) {
+  for (int i = 0; i < TRB / RPI; i++) {
     const int row = tid / C4 + RPI * i;
     float4 v = reinterpret_cast<const float4*>(T + row * TC)[c4];
     if (!COLS) {
@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     v.z = element<FAM, E, M>(divide<FAM>(v.z, xs.z, rs.z), prm);
     v.w = element<FAM, E, M>(divide<FAM>(v.w, xs.w, rs.w), prm);
     if (COLS) {
-      const int64_t l = at.b * TR + row, col = ct * TC + c4 * 4;
+      const int64_t l = at.b * BS + row, col = ct * TC + c4 * 4;
       if (l < len && col < inner) out.codes((at.o * len + l) * inner + col, v);
     } else {
       const int64_t grow = rest * TR + row, col = ct * TC + c4 * 4;
@@ -411,14 +411,15 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
 template <int FAM, int E, int M, int BS, class Out>
 int launch(const CUtensorMap& map, bool cols, Out out, int64_t outer, int64_t len, int64_t inner,
            const TParams& prm, cudaStream_t st) {
-  const int64_t nb = (len + TR - 1) / TR;                  // COLS: blocks of TR rows
+  const int64_t nb = (len + BS - 1) / BS;                  // COLS: blocks of BS rows, one per tile row band
   const int64_t ntiles = cols ? outer * nb * ((inner + TC - 1) / TC) : ((outer + TR - 1) / TR) * ((len + TC - 1) / TC);
   if (ntiles >= (1ll << 31)) return MXQ_ERR_UNSUPPORTED;   // one CTA per tile; 32-bit tile coordinates
-  auto kern = cols ? k_quant_tma<FAM, E, M, true, TR, Out> : k_quant_tma<FAM, E, M, false, BS, Out>;
+  constexpr int CBS = BS <= TR ? BS : TR;                  // COLS tiles: blocks of at most TR rows (the host checks)
+  auto kern = cols ? k_quant_tma<FAM, E, M, true, CBS, Out> : k_quant_tma<FAM, E, M, false, BS, Out>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)ntiles);
   cfg.blockDim = dim3(NT);
-  cfg.dynamicSmemBytes = TILE_BYTES;
+  cfg.dynamicSmemBytes = (size_t)(cols ? CBS : TR) * TC * sizeof(float);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;     // may start while the previous kernel drains
@@ -468,15 +469,15 @@ int launch_fmt(int e, int m, const CUtensorMap& map, bool cols, const Dest& d, i
 
 namespace mxq {
 
-// The TMA kernel for blocks of 32 (and 16 or 64 along rows, float outputs) when the layout allows a tensor map (16-byte aligned base, rows a multiple of 16
+// The TMA kernel for blocks of 32 (with float outputs also 16, and 64 along rows) when the layout allows a tensor map (16-byte aligned base, rows a multiple of 16
 // bytes, extents below 2^31); MXQ_ERR_UNSUPPORTED otherwise (the caller then takes the register kernels).
 int quantize_tma_dest(const float* V, const Dest& d, int64_t outer, int64_t len, int64_t inner, int64_t block,
                       const mxq_quant_spec& s, cudaStream_t st) {
   const bool cols = inner > 1;
-  // blocks of 32 in every layout; blocks of 16 or 64 along rows (ROWS tiles hold any block dividing 256) with
-  // float outputs
-  const bool rows_block = !cols && d.Pc == nullptr && (block == 16 || block == 64);
-  if ((block != 32 && !rows_block) || s.family == MXQ_FAMILY_FP32) return MXQ_ERR_UNSUPPORTED;
+  // blocks of 32 in every layout; with float outputs also blocks of 16 (tiles of 16 rows across rows) and of 64
+  // along rows (ROWS tiles hold any block dividing 256)
+  const bool other = d.Pc == nullptr && (block == 16 || (block == 64 && !cols));
+  if ((block != 32 && !other) || s.family == MXQ_FAMILY_FP32) return MXQ_ERR_UNSUPPORTED;
   const int64_t rowlen = cols ? inner : len;
   const uintptr_t out_base = d.Pc ? (uintptr_t)d.Pc : (uintptr_t)d.P;
   if ((uintptr_t)V % 16 || out_base % 16 || rowlen % 4 || outer >= (1ll << 31) || len >= (1ll << 31) ||
@@ -486,7 +487,7 @@ int quantize_tma_dest(const float* V, const Dest& d, int64_t outer, int64_t len,
   if (cols) {
     const uint64_t dims[3] = {(uint64_t)inner, (uint64_t)len, (uint64_t)outer};
     const uint64_t strides[2] = {(uint64_t)inner * 4, (uint64_t)(len * inner) * 4};
-    const uint32_t box[3] = {TC, TR, 1};
+    const uint32_t box[3] = {TC, (uint32_t)block, 1};
     if (encode_tmap_f32(&map, V, 3, dims, strides, box) != MXQ_OK) return MXQ_ERR_UNSUPPORTED;
   } else {
     const uint64_t dims[2] = {(uint64_t)len, (uint64_t)outer};

@@ -101,6 +101,22 @@ def test_block_rows_pow2_blocks(oracle, bs):
             assert_bits(X, Xo, f"{shape} {bs} {family} X")
 
 
+def test_block_cols_16(oracle):
+    """Blocks of 16 across rows (axis 0 of a 2-D tensor, the middle axis of a 3-D one): the fused kernel's 16-row
+    tiles, a length that is not a whole number of blocks included, with Inf, NaN and zero blocks, every family."""
+    rng = np.random.default_rng(16)
+    for shape, axis in (((64, 256), 0), ((40, 128), 0), ((3, 48, 8), 1)):
+        V = (rng.standard_normal(shape) * 2.0 ** rng.uniform(-20, 20, shape)).astype(np.float32)
+        flat = V.reshape(-1)
+        flat[7], flat[100], flat[200:216] = np.inf, np.nan, 0.0
+        for family, fmt in (("mxquant", "MXFP6_E3M2"), ("mxgemmini", "MXFP8_E4M3"), ("ocp", "MXFP4")):
+            keep = ~nan_block_mask(V, axis, 16) if family == "mxquant" else np.ones(V.shape, bool)
+            P, X = prod.block_quantize(V, family, fmt, axis, 16)
+            Po, Xo = oracle.block_quantize(V, family, fmt, axis, 16)
+            assert_bits_where(P, Po, keep, f"{shape} {axis} {family} P")
+            assert_bits(X, Xo, f"{shape} {axis} {family} X")
+
+
 def test_block_host_streamed(monkeypatch):
     """A host tensor streams through the device in chunks (whole outer slices, or runs of blocks inside a slice,
     the last one short); the chunked result must equal the one-shot device result bit for bit."""
