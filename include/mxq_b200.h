@@ -6,8 +6,9 @@
  *   - `stream` is a cudaStream_t (NULL = the legacy default stream); calls are asynchronous unless stated;
  *   - the return value is MXQ_OK (0) or an MXQ_ERR_* code; mxq_last_error() returns this thread's message;
  *   - kernels never trap on data: NaN and Inf are values, and results follow the reference's rules for them.
- * Thread safety: the library keeps no mutable global state besides the per-thread error message and a per-device
- * SM-count cache filled once.
+ * Thread safety: the library's mutable global state is the per-thread error message, caches filled once under a
+ * lock (per-device SM counts, the driver's tensor-map entry point, the static scratch's per-device address), and the
+ * wait-status word (mxq_wait_status_word), which kernels only increment.
  */
 #ifndef MXQ_B200_H
 #define MXQ_B200_H
@@ -46,6 +47,11 @@ const char* mxq_last_error(void);
  * uses keep_scalar for every element; otherwise keep[i] per element (each in [0, 22]). */
 int mxq_round_bits(const int64_t* bits, const int64_t* keep, int32_t keep_scalar, int64_t* out, int64_t n,
                    int32_t mode, void* stream);
+/* mxq/rounding/ties_away.py:5-6, rne.py:6-8, truncate.py:5-6 bits(bits, drop, mask, half): one mode's rounding of
+ * int64 patterns with the caller's drop / mask / half, each an array of n values or (NULL) its scalar; the int64
+ * result is not reduced to 32 bits (round_bits does that). A drop outside [0, 63] shifts by 63, as torch's >>. */
+int mxq_round_pattern(const int64_t* bits, const int64_t* drop, int64_t drop_s, const int64_t* mask, int64_t mask_s,
+                      const int64_t* half, int64_t half_s, int64_t* out, int64_t n, int32_t mode, void* stream);
 /* mxq/rounding/__init__.py:58-61 round_int */
 int mxq_round_int_f32(const float* k, float* out, int64_t n, int32_t mode, void* stream);
 int mxq_round_int_f64(const double* k, double* out, int64_t n, int32_t mode, void* stream);
@@ -216,7 +222,9 @@ int mxq_block_lut_quantize(const float* V, float* P_lut, float* X, int64_t rows,
  * 16 MiB (one per device) instead of the caller, so the call allocates nothing. Sizes whose workspace
  * (mxq_block_lut_workspace) exceeds 16 MiB are rejected with MXQ_ERR_VALUE. Every call on a device shares the
  * array: calls whose work overlaps on the GPU (other streams, or other host threads, without ordering between
- * them) race on it. Nothing in the array needs to start at zero. */
+ * them) race on it. Nothing in the array needs to start at zero. The array's device address is looked up once per
+ * device and kept for the life of the process, so this entry point must not be called on a device after
+ * cudaDeviceReset (or any other teardown of its primary context) in the same process. */
 int mxq_block_lut_quantize_static(const float* V, float* P_lut, float* X, int64_t rows, int64_t cols, int32_t axis,
                                   int64_t block, const mxq_quant_spec* spec, int32_t group, int32_t max_iters,
                                   int32_t* status, void* stream);
@@ -225,6 +233,18 @@ int mxq_block_lut_quantize_static(const float* V, float* P_lut, float* X, int64_
 /* No reference counterpart: the number of bounded shared-memory waits (mbarrier) that gave up in the TMA-staged
  * kernels on the current device since the library was loaded. Always 0 in a correct run; synchronous. */
 int mxq_device_timeouts(uint32_t* out);
+/* No reference counterpart: the address of the wait-status word, a 32-bit counter in pinned, mapped host memory
+ * (allocated on first use, shared by every device) that a TMA-staged kernel increments when a bounded wait gives up
+ * -- the tile it was loading is then written as NaN codes and NaN scales (the compact form sets status bit 4
+ * instead). The host reads it with a plain load and no synchronisation; it counts the kernels that have finished.
+ * A caller checks it after its calls and clears it (stores 0) once it has handled the event. */
+int mxq_wait_status_word(uint32_t** out);
+/* No reference counterpart; for tests of the timeout path only: mxq_block_quantize of a rows x cols V (blocks of 32
+ * along rows, mxgemmini MXFP8_E4M3) through the TMA kernel with its loads never issued and waits of wait_rounds
+ * (1..65536) rounds, so every tile's wait runs out with nothing in flight; P and X come out NaN and the wait-status
+ * word and the device counter rise by one per 32 x 256 tile. cols a multiple of 32, V and P 16-byte aligned. */
+int mxq_testing_wait_timeout(const float* V, float* P, float* X, int64_t rows, int64_t cols, uint32_t wait_rounds,
+                             void* stream);
 
 #ifdef __cplusplus
 }

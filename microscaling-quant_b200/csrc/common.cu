@@ -72,7 +72,37 @@ int encode_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t
   return MXQ_OK;
 }
 
+unsigned* wait_status_word() {
+  static std::mutex mu;
+  static unsigned* word = nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (word == nullptr) {
+    void* p = nullptr;
+    if (check_cuda(cudaHostAlloc(&p, 64, cudaHostAllocMapped | cudaHostAllocPortable), "wait-status word"))
+      return nullptr;
+    void* d = nullptr;
+    if (check_cuda(cudaHostGetDevicePointer(&d, p, 0), "wait-status word: device address") || d != p) {
+      // unified addressing gives mapped host memory one address on the host and every device; the kernels are
+      // handed the host address, so anything else is refused
+      if (d != p) set_error(MXQ_ERR_CUDA, "wait-status word: mapped host memory has a different device address");
+      cudaFreeHost(p);
+      return nullptr;
+    }
+    *static_cast<volatile unsigned*>(p) = 0u;
+    word = static_cast<unsigned*>(p);
+  }
+  return word;
+}
+
 }  // namespace mxq
+
+extern "C" int mxq_wait_status_word(uint32_t** out) {
+  if (!out) return mxq::set_error(MXQ_ERR_VALUE, "wait_status_word: null output");
+  unsigned* w = mxq::wait_status_word();
+  if (!w) return MXQ_ERR_CUDA;
+  *out = reinterpret_cast<uint32_t*>(w);
+  return MXQ_OK;
+}
 
 extern "C" const char* mxq_version(void) { return "mxq_b200 0.1.0 (sm_100a)"; }
 

@@ -70,6 +70,15 @@ int check_arith(const mxq_arith* a, const char* what) {
 
 extern "C" {
 
+int mxq_round_pattern(const int64_t* bits, const int64_t* drop, int64_t drop_s, const int64_t* mask, int64_t mask_s,
+                      const int64_t* half, int64_t half_s, int64_t* out, int64_t n, int32_t mode, void* stream) {
+  if (int r = check_mode(mode, "rounding bits")) return r;
+  return launch_map(n, stream, "rounding bits", [=] __device__(int64_t i) {
+    out[i] = round_pattern_i64(bits[i], drop ? drop[i] : drop_s, mask ? mask[i] : mask_s, half ? half[i] : half_s,
+                               mode);
+  });
+}
+
 int mxq_round_bits(const int64_t* bits, const int64_t* keep, int32_t keep_scalar, int64_t* out, int64_t n,
                    int32_t mode, void* stream) {
   if (int r = check_mode(mode, "round_bits")) return r;

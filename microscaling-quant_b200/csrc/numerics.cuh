@@ -264,14 +264,20 @@ MXQ_HD float exp2_torch(float t) {
 
 // ------------------------------------------------------------------------------ rounding primitives
 // mxq/rounding/__init__.py:51-55 round_bits on an int64 holding any integer; keep in [0, 22]
+// the three modules' bits(bits, drop, mask, half) on int64 (no reduction to 32 bits); a shift outside [0, 63] fills
+// with the sign, as torch's >> does
+MXQ_HD int64_t round_pattern_i64(int64_t bits, int64_t drop, int64_t mask, int64_t half, int mode) {
+  if (mode == RM_TIES_AWAY) return (bits + half) & ~mask;                                   // ties_away.py:5-6
+  if (mode == RM_RNE) {                                                                     // rne.py:6-8
+    const int sh = (drop < 0 || drop > 63) ? 63 : (int)drop;
+    return (bits + half - 1 + ((bits >> sh) & 1)) & ~mask;
+  }
+  return bits & ~mask;                                                                      // truncate.py:5-6
+}
 MXQ_HD int64_t round_bits_i64(int64_t bits, int keep, int mode) {
   int drop = 23 - keep;
   int64_t mask = ((int64_t)1 << drop) - 1, half = (int64_t)1 << (drop - 1);
-  int64_t r;
-  if (mode == RM_TIES_AWAY) r = (bits + half) & ~mask;                         // ties_away.py:5-6
-  else if (mode == RM_RNE) r = (bits + half - 1 + ((bits >> drop) & 1)) & ~mask;   // rne.py:6-8
-  else r = bits & ~mask;                                                        // truncate.py:5-6
-  return r & 0xffffffffll;
+  return round_pattern_i64(bits, drop, mask, half, mode) & 0xffffffffll;
 }
 // mxq/rounding/__init__.py:58-61 round_int on an integer-valued quantity
 MXQ_HD float round_int_f(float k, int mode) {

@@ -32,6 +32,9 @@ static_assert(TC % 32 == 0 && TC <= NT && NT % C4 == 0 && TR % RPI == 0, "tile s
 struct TParams {
   int rounding, placement, via_e, via_m;
   float scale_floor, scale_emax;
+  unsigned* status_word;   // the host-mapped wait-status word (wait_status_word())
+  unsigned wait_rounds;    // try_wait rounds before the tile's wait gives up (kWaitLimit)
+  int skip_load;           // 1 only in mxq_testing_wait_timeout: the load is never issued, so the wait runs out
 };
 
 template <int E, int M>
@@ -134,6 +137,7 @@ struct OutF {
   __device__ __forceinline__ void codes(int64_t idx, float4 v) { __stcs(reinterpret_cast<float4*>(P + idx), v); }
   __device__ __forceinline__ void scale(int64_t idx, float x) { X[idx] = x; }
   __device__ __forceinline__ void finish() {}
+  __device__ __forceinline__ void lost() {}                // the tile's NaN codes and scales say it
 };
 
 // an OCP element code's bit pattern (sign at bit E + M); `bad` set for what the format lacks (Inf, and NaN in FP6 /
@@ -211,6 +215,9 @@ struct OutPack {
     const int bits = (bad_code ? 1 : 0) | (bad_scale ? 2 : 0);
     if (bits) atomicOr(status, bits);
   }
+  __device__ __forceinline__ void lost() {
+    if (threadIdx.x == 0) atomicOr(status, 4);
+  }
 };
 
 // A tile's coordinates, from its index by 32-bit division once per tile: column tile ct, and rest = the row tile
@@ -263,6 +270,38 @@ __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out
   }
 }
 
+// A tile whose load never arrived: NaN for each of its codes and scales (the same index arithmetic as the normal
+// path, no shared-memory reads), then the output's own mark of a lost tile
+template <bool COLS, int BS, class Out>
+__device__ __forceinline__ void lose_tile(Out& out, const TileAt& at, int64_t outer, int64_t len, int64_t inner,
+                                          int64_t nb) {
+  const int tid = threadIdx.x, c4 = tid % C4;
+  const float q = qnan_f();
+  const float4 q4 = make_float4(q, q, q, q);
+  for (int i = 0; i < (COLS ? BS : TR) / RPI; i++) {
+    const int row = tid / C4 + RPI * i;
+    if (COLS) {
+      const int64_t l = at.b * BS + row, col = at.ct * TC + c4 * 4;
+      if (l < len && col < inner) out.codes((at.o * len + l) * inner + col, q4);
+    } else {
+      const int64_t grow = at.rest * TR + row, col = at.ct * TC + c4 * 4;
+      if (grow < outer && col < len) out.codes(grow * len + col, q4);
+    }
+  }
+  if (COLS) {
+    const int64_t col = at.ct * TC + tid;
+    if (tid < TC && col < inner) out.scale((at.o * nb + at.b) * inner + col, q);
+  } else {
+    constexpr int BPR = TC / BS;
+    for (int bi = tid; bi < TR * BPR; bi += NT) {
+      const int64_t grow = at.rest * TR + bi / BPR, gblk = at.ct * BPR + bi % BPR;
+      if (grow < outer && gblk < nb) out.scale(grow * nb + gblk, q);
+    }
+  }
+  out.finish();
+  out.lost();
+}
+
 // BS: the block length: 16 or 32 for COLS (a tile is one block of BS rows), 16, 32 or 64 for ROWS
 template <int FAM, int E, int M, bool COLS, int BS, class Out>
 __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtensorMap tmap, Out out, int64_t outer,
@@ -295,12 +334,22 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
   if (tid == 0) {
     fence_proxy_async();
     mbar_expect_tx(&bar, (unsigned)(TRB * TC * sizeof(float)));
-    if (COLS) tma_load_3d(T, &tmap, (int)(ct * TC), (int)(at.b * BS), (int)at.o, &bar);
-    else tma_load_2d(T, &tmap, (int)(ct * TC), (int)(rest * TR), &bar);
+    if (!prm.skip_load) {
+      if (COLS) tma_load_3d(T, &tmap, (int)(ct * TC), (int)(at.b * BS), (int)at.o, &bar);
+      else tma_load_2d(T, &tmap, (int)(ct * TC), (int)(rest * TR), &bar);
+    }
   }
-  // every thread waits; the CTA leaves together if the (bounded) wait gave up anywhere
-  if (!__syncthreads_and(mbar_wait(&bar, 0u))) {
-    out.finish();
+  // every thread waits (bounded); if the wait gave up anywhere the tile is lost: the event is counted once, a load
+  // that was issued gets a second bounded wait so that the CTA does not leave with a copy into its shared memory in
+  // flight, and the tile's codes and scales are written as NaN (the compact form also sets status bit 4), so a
+  // lost tile cannot pass for a quantized one
+  if (!__syncthreads_and(mbar_try_wait_rounds(&bar, 0u, prm.wait_rounds))) {
+    if (tid == 0) {
+      note_wait_timeout(prm.status_word);
+      if (!prm.skip_load) mbar_try_wait_rounds(&bar, 0u, prm.wait_rounds);
+    }
+    __syncthreads();
+    lose_tile<COLS, BS>(out, at, outer, len, inner, nb);
     return;
   }
 
@@ -411,15 +460,18 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
 template <int FAM, int E, int M, int BS, class Out>
 int launch(const CUtensorMap& map, bool cols, Out out, int64_t outer, int64_t len, int64_t inner,
            const TParams& prm, cudaStream_t st) {
+  if (cols && BS > TR) return MXQ_ERR_UNSUPPORTED;         // a COLS tile is one block of at most TR rows
   const int64_t nb = (len + BS - 1) / BS;                  // COLS: blocks of BS rows, one per tile row band
   const int64_t ntiles = cols ? outer * nb * ((inner + TC - 1) / TC) : ((outer + TR - 1) / TR) * ((len + TC - 1) / TC);
   if (ntiles >= (1ll << 31)) return MXQ_ERR_UNSUPPORTED;   // one CTA per tile; 32-bit tile coordinates
-  constexpr int CBS = BS <= TR ? BS : TR;                  // COLS tiles: blocks of at most TR rows (the host checks)
-  auto kern = cols ? k_quant_tma<FAM, E, M, true, CBS, Out> : k_quant_tma<FAM, E, M, false, BS, Out>;
+  void (*kern)(const CUtensorMap, Out, int64_t, int64_t, int64_t, TParams) = k_quant_tma<FAM, E, M, false, BS, Out>;
+  if constexpr (BS <= TR) {                                // only blocks that fit a COLS tile instantiate one
+    if (cols) kern = k_quant_tma<FAM, E, M, true, BS, Out>;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)ntiles);
   cfg.blockDim = dim3(NT);
-  cfg.dynamicSmemBytes = (size_t)(cols ? CBS : TR) * TC * sizeof(float);
+  cfg.dynamicSmemBytes = (size_t)(cols ? BS : TR) * TC * sizeof(float);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;     // may start while the previous kernel drains
@@ -472,7 +524,8 @@ namespace mxq {
 // The TMA kernel for blocks of 32 (with float outputs also 16, and 64 along rows) when the layout allows a tensor map (16-byte aligned base, rows a multiple of 16
 // bytes, extents below 2^31); MXQ_ERR_UNSUPPORTED otherwise (the caller then takes the register kernels).
 int quantize_tma_dest(const float* V, const Dest& d, int64_t outer, int64_t len, int64_t inner, int64_t block,
-                      const mxq_quant_spec& s, cudaStream_t st) {
+                      const mxq_quant_spec& s, cudaStream_t st, int test_skip_load = 0,
+                      unsigned wait_rounds = kWaitLimit) {
   const bool cols = inner > 1;
   // blocks of 32 in every layout; with float outputs also blocks of 16 (tiles of 16 rows across rows) and of 64
   // along rows (ROWS tiles hold any block dividing 256)
@@ -495,7 +548,10 @@ int quantize_tma_dest(const float* V, const Dest& d, int64_t outer, int64_t len,
     const uint32_t box[2] = {TC, TR};
     if (encode_tmap_f32(&map, V, 2, dims, strides, box) != MXQ_OK) return MXQ_ERR_UNSUPPORTED;
   }
-  TParams prm{s.rounding, s.placement, s.via_e, s.via_m, s.scale_floor, s.scale_emax};
+  unsigned* word = wait_status_word();
+  if (word == nullptr) return MXQ_ERR_CUDA;                 // the reason is recorded
+  TParams prm{s.rounding, s.placement, s.via_e, s.via_m, s.scale_floor, s.scale_emax, word, wait_rounds,
+              test_skip_load};
   switch (s.family) {
     case MXQ_FAMILY_MXQUANT: return launch_fmt<MXQ_FAMILY_MXQUANT>(s.e, s.m, map, cols, d, outer, len, inner, block, prm, st);
     case MXQ_FAMILY_MXGEMMINI:
@@ -515,6 +571,25 @@ int quantize_tma_packed(const float* V, uint8_t* Pc, uint8_t* Xc, int* status, i
 }
 
 }  // namespace mxq
+
+// Test-only: block.mxgemmini MXFP8_E4M3 along the rows of a rows x cols V through the TMA kernel with its loads never
+// issued and waits of `wait_rounds` rounds, so every tile's wait runs out (nothing is in flight when the CTAs
+// leave). The tiles come out as NaN and the wait-status word and the device counter rise by one per tile.
+extern "C" int mxq_testing_wait_timeout(const float* V, float* P, float* X, int64_t rows, int64_t cols,
+                                        uint32_t wait_rounds, void* stream) {
+  MXQ_REQUIRE(rows > 0 && cols > 0 && cols % 32 == 0, MXQ_ERR_VALUE, "testing_wait_timeout: bad sizes");
+  MXQ_REQUIRE(wait_rounds >= 1 && wait_rounds <= (1u << 16), MXQ_ERR_VALUE, "testing_wait_timeout: wait_rounds");
+  mxq_quant_spec s{};
+  s.family = MXQ_FAMILY_MXGEMMINI;
+  s.e = 4;
+  s.m = 3;
+  s.rounding = MXQ_RM_TIES_AWAY;
+  s.scale_floor = 1e-38f;
+  const int r = mxq::quantize_tma_dest(V, Dest{P, X, nullptr, nullptr, nullptr}, rows, cols, 1, 32, s,
+                                       mxq::as_stream(stream), 1, wait_rounds);
+  MXQ_REQUIRE(r != MXQ_ERR_UNSUPPORTED, MXQ_ERR_VALUE, "testing_wait_timeout: the layout has no TMA path");
+  return r;
+}
 
 // Number of bounded shared-memory waits that gave up in the staged kernels since the library was loaded on the
 // current device (0 in every correct run); synchronous.

@@ -1,10 +1,11 @@
 // Tensor Memory Accelerator (TMA) plumbing for sm_100a: tensor-map encoding on the host (through the driver entry
 // point, no libcuda link) and the device-side mbarrier / cp.async.bulk.tensor wrappers the staged kernels use.
 //
-// Every wait on an mbarrier is bounded: after kWaitLimit unsuccessful try_wait rounds (each round the hardware
+// Every wait on an mbarrier is bounded: after a limit of unsuccessful try_wait rounds (each round the hardware
 // suspends the thread for a bounded time) the wait gives up, counts the event in the library's timeout counter
-// (read with mxq_device_timeouts) and the kernel returns instead of hanging. A TMA load always delivers its whole
-// box (out-of-range elements zero-filled), so the expected byte counts are exact and the bound is a safety net.
+// (read with mxq_device_timeouts), raises the host-mapped wait-status word (read without a device synchronisation
+// with mxq_wait_status_word) and the kernel returns instead of hanging. A TMA load always delivers its whole box
+// (out-of-range elements zero-filled), so the expected byte counts are exact and the bound is a safety net.
 #pragma once
 #include <cuda.h>
 #include <stdint.h>
@@ -17,6 +18,13 @@ namespace mxq {
 // box `box`; zero fill out of range, no swizzle. Returns MXQ_OK or an MXQ_ERR_* with the reason recorded.
 int encode_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
                     const uint32_t* box);
+
+// The wait-status word: one 32-bit counter in pinned, mapped, portable host memory, allocated on first use (any
+// device; the same address serves every device), which a kernel whose bounded wait gave up increments with a
+// system-scope atomic. The host reads it with a plain load, so a caller can check it on every call without
+// synchronising; it sees the kernels that have finished. nullptr (with the reason recorded) if the allocation
+// failed.
+unsigned* wait_status_word();
 
 // per translation unit (no relocatable device code): each TU that stages through TMA owns a counter and reports it
 static __device__ unsigned int g_wait_timeouts = 0;
@@ -42,10 +50,10 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(bytes)
                : "memory");
 }
-// true when the phase with the given parity has completed; false after the bounded number of rounds
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
+// true when the phase with the given parity has completed; false after `rounds` unsuccessful rounds
+__device__ __forceinline__ bool mbar_try_wait_rounds(uint64_t* bar, unsigned parity, unsigned rounds) {
   const unsigned addr = smem_addr(bar);
-  for (unsigned it = 0; it < kWaitLimit; it++) {
+  for (unsigned it = 0; it < rounds; it++) {
     unsigned done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -54,8 +62,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
         : "memory");
     if (done) return true;
   }
-  atomicAdd(&g_wait_timeouts, 1u);
   return false;
+}
+// count a wait that gave up: the device counter and the host-mapped status word (if any)
+__device__ __forceinline__ void note_wait_timeout(unsigned* status_word) {
+  atomicAdd(&g_wait_timeouts, 1u);
+  if (status_word) {
+    atomicAdd_system(status_word, 1u);
+    __threadfence_system();
+  }
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(

@@ -46,6 +46,7 @@ class MxqAnchorSpec(ctypes.Structure):
 # entry point -> argument types (the return type of every entry point is int32 status)
 _SIGS = {
     "mxq_round_bits": [P, P, I32, P, I64, I32, P],
+    "mxq_round_pattern": [P, P, I64, P, I64, P, I64, P, I64, I32, P],
     "mxq_round_int_f32": [P, P, I64, I32, P],
     "mxq_round_int_f64": [P, P, I64, I32, P],
     "mxq_bf16": [P, P, I64, P],
@@ -87,6 +88,8 @@ _SIGS = {
     "mxq_lut_finder": [P, P, P, I64, I64, I32, I32, I32, P, P],
     "mxq_lut_format_tables": [I32, I32, P, P, P, P],
     "mxq_device_timeouts": [P],
+    "mxq_wait_status_word": [P],
+    "mxq_testing_wait_timeout": [P, P, P, I64, I64, ctypes.c_uint32, P],
 }
 
 
@@ -192,14 +195,47 @@ class using:
 
 
 def run(name, device, *args):
-    """call() with `device` current; the last argument of every entry point is the stream, appended here."""
+    """call() with `device` current; the last argument of every entry point is the stream, appended here. Raises
+    RuntimeError if a bounded wait of an earlier kernel has given up (check_waits)."""
     cur = torch.cuda.current_device()
     idx = device.index if device.index is not None else cur
     if idx == cur:                                          # the usual case: no device switch
         call(name, *args, _stream_of(idx))
-        return
-    with torch.cuda.device(device):
-        call(name, *args, _stream_of(idx))
+    else:
+        with torch.cuda.device(device):
+            call(name, *args, _stream_of(idx))
+    check_waits()
+
+
+# ------------------------------------------------------------------------------------------ wait status
+_wait_word = None
+
+
+def wait_word():
+    """The library's wait-status word (pinned, mapped host memory) as a ctypes uint32 view: the number of bounded
+    TMA waits that gave up in kernels that have finished. Read without synchronising."""
+    global _wait_word
+    if _wait_word is None:
+        addr = ctypes.POINTER(ctypes.c_uint32)()
+        call("mxq_wait_status_word", ctypes.byref(addr))
+        _wait_word = ctypes.c_uint32.from_address(ctypes.addressof(addr.contents))
+    return _wait_word
+
+
+def check_waits():
+    """Raise RuntimeError if any TMA-staged kernel that has finished gave up waiting for its tile. Such a tile is
+    written as NaN codes and scales, so every result computed since is suspect; the error repeats on every call
+    until clear_waits()."""
+    w = _wait_word
+    if w is not None and w.value:
+        raise RuntimeError(f"mxq_b200: {w.value} bounded TMA wait(s) gave up in an earlier kernel (the tiles were "
+                           "written as NaN): results since then are undefined; call mxq._lib.clear_waits() once "
+                           "handled")
+
+
+def clear_waits():
+    """Reset the wait-status word to 0 (after a timeout has been handled)."""
+    wait_word().value = 0
 
 
 def cached(make):

@@ -203,6 +203,7 @@ def _quantize_streamed(V, spec, axis_, outer, L, inner, nb, block_size, dev):
                 free[s] = torch.cuda.Event()
                 free[s].record(d2h)
         d2h.synchronize()
+    _lib.check_waits()
     return P, X
 
 
@@ -213,6 +214,8 @@ def quantize_fused(V: torch.Tensor, spec: "_lib.MxqQuantSpec", axis: int, block_
     _check_reshape(V, axis_, block_size)
     home = _lib.home(V)
     dev = _lib.device_for(V)
+    if _lib._wait_word is None:                             # the kernel's wait-status word, checked by every call
+        _lib.wait_word()
     if not V.is_cuda and V.numel() * 4 >= STREAM_MIN_BYTES:
         return _quantize_streamed(V, spec, axis_, outer, L, inner, nb, block_size, dev)
     v = _lib.on(V, dev)
@@ -270,6 +273,9 @@ def quantize_packed(V: torch.Tensor, spec: "_lib.MxqQuantSpec", axis: int, block
     _lib.run("mxq_block_quantize_packed", dev, _lib.ptr(v), _lib.ptr(codes), _lib.ptr(scales), outer, L, inner,
              block_size, ctypes.byref(spec), _lib.ptr(st))
     bits = int(st.item())
+    if bits & 4:
+        raise RuntimeError("compact form: a tile's load did not arrive within the kernel's bounded wait; the codes "
+                           "are undefined")
     if bits & 1:
         raise ValueError("compact form: a code is Inf or NaN, which this element format cannot hold")
     if bits & 2:

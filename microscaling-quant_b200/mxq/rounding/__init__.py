@@ -9,7 +9,6 @@ from typing import Union
 import torch
 
 from .. import _lib
-from . import ties_away, rne, truncate
 
 MODES = ("ties_away", "rne", "truncate")
 _CODE = {"ties_away": 0, "rne": 1, "truncate": 2}
@@ -45,6 +44,30 @@ def round_bits(bits: torch.Tensor, keep: Union[int, torch.Tensor], mode: str) ->
     return _lib.back(out, home)
 
 
+def _pattern(bits: torch.Tensor, drop, mask, half, mode: str) -> torch.Tensor:
+    """One mode's bits(bits, drop, mask, half) (ties_away.py:5-6, rne.py:6-8, truncate.py:5-6): int64 patterns
+    rounded with the caller's drop / mask / half (ints or int64 tensors broadcast against `bits`), the int64
+    result not reduced to 32 bits. One kernel (mxq_round_pattern)."""
+    code = mode_code(mode)
+    home = _lib.home(bits)
+    dev = _lib.device_for(bits, drop, mask, half)
+    parts = [bits, drop, mask, half]
+    shape = torch.broadcast_shapes(*(tuple(t.shape) for t in parts if isinstance(t, torch.Tensor)))
+    args = []
+    for i, t in enumerate(parts):
+        if isinstance(t, torch.Tensor):
+            args.append((_lib.on(t, dev, torch.int64).expand(shape).contiguous(), 0))
+        elif i == 0:
+            args.append((torch.full(shape, int(t), dtype=torch.int64, device=dev), 0))
+        else:
+            args.append((None, int(t)))
+    out = torch.empty(shape, dtype=torch.int64, device=dev)
+    (b, _), (d, ds), (m, ms), (h, hs) = args
+    _lib.run("mxq_round_pattern", dev, _lib.ptr(b), _lib.ptr(d), ds, _lib.ptr(m), ms, _lib.ptr(h), hs, _lib.ptr(out),
+             out.numel(), code)
+    return _lib.back(out, home)
+
+
 def round_int(k: torch.Tensor, mode: str) -> torch.Tensor:
     """An integer-valued float tensor rounded to an integer (mxq/rounding/__init__.py:58-61); float32 or float64."""
     code = mode_code(mode)
@@ -68,3 +91,6 @@ def bf16(x: torch.Tensor) -> torch.Tensor:
     out = torch.empty_like(t)
     _lib.run("mxq_bf16", dev, _lib.ptr(t), _lib.ptr(out), t.numel())
     return _lib.back(out, home)
+
+
+from . import ties_away, rne, truncate  # noqa: E402  (the mode modules use _pattern and round_int above)
