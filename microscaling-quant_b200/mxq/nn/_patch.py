@@ -1,25 +1,32 @@
-"""patch(model, rules): which Scheme each nn.Linear (and each attention core) runs through
-(mxq/nn/_patch.py:123-287).
+"""patch(model, rules): which Scheme each nn.Linear (and each attention core) of a model runs through
+(mxq/nn/_patch.py:123-287 of the reference; same API, rules, checks, messages and printed table).
 
-    rules = [("lm_head", None),                 # a layer name, * wildcards; None leaves the layer as it is
-             ("*.mlp.down_proj", FP6),          # a Scheme
-             (is_attention, None),              # a function (name, module, parent) -> bool
-             (nn.Linear, FP8),                  # a layer type
+    rules = [("lm_head", None),                        # a layer name, * wildcards; None leaves the layer as it is
+             ("*.mlp.down_proj", FP6),                 # a Scheme
+             (is_attention, None),                     # a function (name, module, parent) -> bool
+             (nn.Linear, FP8),                         # a layer type
              ("model.layers.*.self_attn", (QK, PV))]   # a pair of Schemes: that attention module's core
-    handle = patch(model, rules)                # first matching rule wins
-    handle.revert()
-    patch(model, rules, dry_run=True)           # print the table, change nothing
+    handle = patch(model, rules)                       # the first rule that matches a layer decides it
+    handle.revert()                                    # everything patch changed, undone
+    patch(model, rules, dry_run=True)                  # print the table, change nothing
 
-Before anything is replaced every Scheme runs once on a tiny matmul (and every core on a tiny attention), so a bad
-schedule or format fails here. A rule that chooses nothing raises. A layer reachable under several names is
-replaced at every attribute holding it; two names of one attribute asking for different rules raise.
+How it works here. `_Survey` walks the model once, keeping every name under which a module is reachable, and lists
+the Linear layers and the attention modules (those holding q_proj and k_proj) with their parents. `_decide` gives
+each its rule and checks the choice as a whole: every rule must choose something, an attribute reached under
+several names must get one rule, an attention module reached under several names too. Before the model is
+touched, every Scheme runs once on a tiny matmul (and every core on a tiny attention), so a bad schedule or format
+fails here. The changes are then made one by one, each recording how to undo itself in the Handle's log;
+`revert` plays the log backwards.
+
 vector="bf16" (or {"softmax": ..., "rmsnorm": ...}) rounds the vector ops' steps to bf16: softmax runs in attend
-(attention modules without a core rule get the EXACT core), and every *RMSNorm forward is replaced after a check
-that the unrounded replacement reproduces the module's own output bit for bit.
+(attention modules without a core rule get the EXACT core, since sdpa's fused kernel has no step to round), and
+every *RMSNorm forward is replaced after a check that the unrounded replacement reproduces the module's own output
+bit for bit.
 """
+from dataclasses import dataclass
 from fnmatch import fnmatchcase
 from functools import partial
-from typing import Callable, List, Optional, Sequence, Tuple, Union
+from typing import Callable, Dict, List, Optional, Sequence, Tuple, Union
 
 import torch
 from torch import nn
@@ -35,211 +42,266 @@ Selector = Union[str, type, Callable[[str, nn.Module, nn.Module], bool]]
 Rule = Tuple[Selector, Union[None, Scheme, Tuple[Scheme, Scheme]]]
 
 
-def _is_core(value) -> bool:
-    return isinstance(value, tuple) and len(value) == 2 and all(isinstance(s, Scheme) for s in value)
+def is_attention(name: str, module: nn.Module, parent: nn.Module) -> bool:
+    """Is this Linear one of an attention module's projections? True when its parent holds both q_proj and k_proj
+    (the test MXQuant's eval_complete.py uses, so a rule list written with it keeps MXQuant's layer set)."""
+    return _attention_module(parent)
 
 
-def _holds_core(module: nn.Module) -> bool:
+def _attention_module(module: nn.Module) -> bool:
     return hasattr(module, "q_proj") and hasattr(module, "k_proj")
 
 
-def is_attention(name: str, module: nn.Module, parent: nn.Module) -> bool:
-    """Is this Linear one of an attention module's projections? (its parent holds q_proj and k_proj)"""
-    return hasattr(parent, "q_proj") and hasattr(parent, "k_proj")
+def _core_pair(value) -> bool:
+    """A rule value that chooses an attention core: (qk Scheme, pv Scheme)."""
+    return isinstance(value, tuple) and len(value) == 2 and all(isinstance(s, Scheme) for s in value)
 
 
-def _smoke(scheme: Scheme) -> None:
+def _selects(selector: Selector, name: str, module: nn.Module, parent: nn.Module) -> bool:
+    if isinstance(selector, type):
+        return isinstance(module, selector)
+    if isinstance(selector, str):
+        return fnmatchcase(name, selector)
+    return bool(selector(name, module, parent))
+
+
+# -------------------------------------------------------------------------------------------- survey
+@dataclass
+class _Seen:
+    """One module under one of its names; `rule` is the index of the rule that chose it (None: no rule)."""
+    name: str
+    module: nn.Module
+    parent: nn.Module
+    rule: Optional[int] = None
+
+    @property
+    def attr(self) -> str:
+        return self.name.rsplit(".", 1)[-1]
+
+
+class _Survey:
+    """Every name under which each module is reachable (a module held twice is listed twice), split into the
+    Linear layers, the attention modules and the RMSNorm modules."""
+
+    def __init__(self, model: nn.Module):
+        named = dict()
+        order = []
+        for name, module in model.named_modules(remove_duplicate=False):
+            named[name] = module
+            order.append((name, module))
+        def parent(name):
+            return named[name.rsplit(".", 1)[0] if "." in name else ""]
+        self.linears = [_Seen(n, m, parent(n)) for n, m in order if n and isinstance(m, nn.Linear)]
+        self.attention = [_Seen(n, m, parent(n)) for n, m in order if n and _attention_module(m)]
+        norms: Dict[int, Tuple[str, nn.Module]] = {}
+        for n, m in order:
+            if n and type(m).__name__.endswith("RMSNorm") and id(m) not in norms:
+                norms[id(m)] = (n, m)
+        self.norms = list(norms.values())
+
+
+def _decide(rules: Sequence[Rule], survey: _Survey) -> None:
+    """Give every surveyed Linear and attention module its rule (first match of its kind), then refuse a choice
+    that cannot be carried out as asked."""
+    for i, rule in enumerate(rules):
+        if len(rule) != 2 or not (rule[1] is None or isinstance(rule[1], Scheme) or _core_pair(rule[1])):
+            raise ValueError(f"rule {i} must be (selector, Scheme or None or (qk Scheme, pv Scheme)), got {rule!r}")
+    kinds = {False: [], True: []}                          # is a core rule -> rule indices, in order
+    for i, (_, value) in enumerate(rules):
+        kinds[_core_pair(value)].append(i)
+    for seen, candidates in ((survey.linears, kinds[False]), (survey.attention, kinds[True])):
+        for s in seen:
+            s.rule = next((i for i in candidates if _selects(rules[i][0], s.name, s.module, s.parent)), None)
+
+    idle = [i for i in kinds[False] if i not in {s.rule for s in survey.linears}]
+    if idle:
+        raise ValueError(f"rules {idle} choose no Linear layer (misspelt, or hidden behind an earlier rule): "
+                         f"{[rules[i][0] for i in idle]}")
+    idle = [i for i in kinds[True] if i not in {s.rule for s in survey.attention}]
+    if idle:
+        raise ValueError(f"rules {idle} choose no attention module (one holding q_proj and k_proj): "
+                         f"{[rules[i][0] for i in idle]}")
+    # an attention module chosen under one of its names must be chosen the same way under all of them
+    by_module: Dict[int, List[_Seen]] = {}
+    for s in survey.attention:
+        by_module.setdefault(id(s.module), []).append(s)
+    for group in by_module.values():
+        if any(s.rule is not None for s in group) and len({s.rule for s in group}) > 1:
+            raise ValueError(f"{[s.name for s in group]} are the same attention module but match different rules; "
+                             "one of them has to go")
+    # a Linear runs from an attribute of its parent; every name reaching that attribute must agree
+    for group in _sites(survey.linears).values():
+        if len({s.rule for s in group}) > 1:
+            raise ValueError(f"{[s.name for s in group]} are the same layer but match different rules "
+                             f"{[s.rule for s in group]}; one of them has to go")
+
+
+def _sites(linears: List[_Seen]) -> Dict[Tuple[int, str], List[_Seen]]:
+    """The Linear layers grouped by the attribute they are held in: (id of parent, attribute name)."""
+    sites: Dict[Tuple[int, str], List[_Seen]] = {}
+    for s in linears:
+        sites.setdefault((id(s.parent), s.attr), []).append(s)
+    return sites
+
+
+# ------------------------------------------------------------------------------------------ dry runs
+def _try_scheme(scheme: Scheme) -> None:
+    """One tiny matmul: two whole LUT groups of columns, three blocks of contraction (so the scale check runs)."""
     g = torch.Generator().manual_seed(0)
-    n, K = 2 * scheme.rows, 3 * scheme.block_size          # two whole LUT groups, three blocks
-    scheme.matmul(torch.randn(K, n, generator=g), torch.randn(K, n, generator=g))
+    cols, depth = 2 * scheme.rows, 3 * scheme.block_size
+    scheme.matmul(torch.randn(depth, cols, generator=g), torch.randn(depth, cols, generator=g))
 
 
-def _smoke_core(qk: Scheme, pv: Scheme) -> None:
+def _try_core(qk: Scheme, pv: Scheme) -> None:
+    """One tiny grouped-query attention: whole key blocks and whole LUT groups."""
     g = torch.Generator().manual_seed(0)
-    t = 2 * max(qk.block_size, pv.block_size) * max(qk.rows, pv.rows)
-    q, k, v = (torch.randn(1, h, t, 32, generator=g) for h in (2, 1, 1))
+    tokens = 2 * max(qk.block_size, pv.block_size) * max(qk.rows, pv.rows)
+    q, k, v = (torch.randn(1, heads, tokens, 32, generator=g) for heads in (2, 1, 1))
     attend(q, k, v, None, 32 ** -0.5, qk, pv)
 
 
-def _is_rmsnorm(module: nn.Module) -> bool:
-    return type(module).__name__.endswith("RMSNorm")
-
-
-def _eps(module: nn.Module) -> float:
-    for attr in ("variance_epsilon", "eps"):
-        if isinstance(getattr(module, attr, None), float):
-            return getattr(module, attr)
-    raise ValueError(f"{type(module).__name__}: no float variance_epsilon or eps attribute")
-
-
-def _check_rmsnorm(name: str, module: nn.Module) -> float:
+def _norm_eps(name: str, module: nn.Module) -> float:
+    """The module's epsilon, after checking that rmsnorm(·, precision=None) is its forward, bit for bit."""
     weight = getattr(module, "weight", None)
     if not isinstance(weight, torch.Tensor) or weight.ndim != 1:
         raise ValueError(f"{name} ({type(module).__name__}): no 1-D weight, not the RMSNorm mxq knows")
-    eps = _eps(module)
-    g = torch.Generator().manual_seed(0)
-    x = (torch.randn(3, weight.shape[0], generator=g) * 3).to(device=weight.device, dtype=weight.dtype)
+    eps = next((getattr(module, a) for a in ("variance_epsilon", "eps") if isinstance(getattr(module, a, None), float)),
+               None)
+    if eps is None:
+        raise ValueError(f"{type(module).__name__}: no float variance_epsilon or eps attribute")
+    probe = torch.randn(3, weight.shape[0], generator=torch.Generator().manual_seed(0)) * 3
+    probe = probe.to(device=weight.device, dtype=weight.dtype)
     with torch.no_grad():
-        theirs, ours = module(x), rmsnorm(x, weight, eps, None)
-    if theirs.dtype != ours.dtype or not torch.equal(theirs, ours):
+        own, mine = module(probe), rmsnorm(probe, weight, eps, None)
+    if own.dtype != mine.dtype or not torch.equal(own, mine):
         raise ValueError(f"{name} ({type(module).__name__}) does not compute weight · x / sqrt(mean(x²) + eps) the way "
                          "transformers' LlamaRMSNorm does; vector rmsnorm cannot replace it")
     return eps
 
 
-def _rmsnorm_forward(module: nn.Module, eps: float, precision: str, x: torch.Tensor) -> torch.Tensor:
+def _norm_forward(module: nn.Module, eps: float, precision: str, x: torch.Tensor) -> torch.Tensor:
     return rmsnorm(x, module.weight, eps, precision)
 
 
-def _set_attention(model: nn.Module, name: str) -> None:
+def _attention_impl(model: nn.Module, name: str) -> None:
     if hasattr(model, "set_attn_implementation"):
         model.set_attn_implementation(name)
     else:
         model.config._attn_implementation = name
 
 
-def _matches(selector: Selector, name: str, module: nn.Module, parent: nn.Module) -> bool:
-    if isinstance(selector, str):
-        return fnmatchcase(name, selector)
-    if isinstance(selector, type):
-        return isinstance(module, selector)
-    return bool(selector(name, module, parent))
-
-
+# -------------------------------------------------------------------------------------------- handle
 class Handle:
-    """What patch did: `table` rows (layer name, in, out, rule index or None, Scheme name or None); `cores` rows
-    (attention module name, rule index or None, (qk name, pv name) or None)."""
+    """What patch did. `table`: one row per Linear name, (name, in, out, rule index or None, Scheme name or None);
+    `cores`: one row per attention module name, (name, rule index or None, (qk name, pv name) or None); `vector`:
+    the resolved vector setting; `norms`: the RMSNorm modules whose forward was replaced. `revert()` undoes every
+    change, last first."""
 
-    def __init__(self, model, table, replaced, cores=None, cored=None, previous=None, vector=None, norms=None,
-                 normed=None):
-        self._model, self.table, self._replaced = model, table, replaced
-        self.cores, self._cored, self._previous = cores or [], cored or [], previous
-        self.vector, self.norms, self._normed = vector or resolve(None), norms or [], normed or []
+    def __init__(self, table, cores, vector, norms):
+        self.table, self.cores, self.vector, self.norms = table, cores, vector, norms
+        self._undo: List[Callable[[], None]] = []
+
+    def _did(self, undo: Callable[[], None]) -> None:
+        self._undo.append(undo)
 
     def revert(self) -> None:
-        for parent, leaf, original in self._replaced:
-            setattr(parent, leaf, original)
-        self._replaced = []
-        for module in self._cored:
-            del module._mxq_core
-            if hasattr(module, "_mxq_vector"):
-                del module._mxq_vector
-        if self._cored:
-            _set_attention(self._model, self._previous)
-        self._cored = []
-        for module in self._normed:
-            del module.forward
-        self._normed = []
+        while self._undo:
+            self._undo.pop()()
 
     def __str__(self) -> str:
-        width = max([len(r[0]) for r in self.table] + [len(r[0]) for r in self.cores] + [5])
-        lines = [f"{'layer':{width}s}  {'in':>6s} {'out':>6s}  rule  scheme"]
-        for name, k, n, rule, scheme in self.table:
-            lines.append(f"{name:{width}s}  {k:6d} {n:6d}  {'-' if rule is None else rule:>4}  "
-                         f"{'no rule' if rule is None else (scheme or 'left as is')}")
-        if any(names is not None for _, _, names in self.cores):
-            lines.append(f"{'attention core':{width}s}  {'':13s}  rule  Q·Kᵀ, P·V")
+        w = max([5] + [len(r[0]) for r in self.table] + [len(r[0]) for r in self.cores])
+        mark = lambda rule: "-" if rule is None else rule                     # noqa: E731
+        out = [f"{'layer':{w}s}  {'in':>6s} {'out':>6s}  rule  scheme"]
+        for name, fan_in, fan_out, rule, scheme in self.table:
+            what = "no rule" if rule is None else (scheme or "left as is")
+            out.append(f"{name:{w}s}  {fan_in:6d} {fan_out:6d}  {mark(rule):>4}  {what}")
+        if any(names is not None for *_, names in self.cores):
+            out.append(f"{'attention core':{w}s}  {'':13s}  rule  Q·Kᵀ, P·V")
             for name, rule, names in self.cores:
-                lines.append(f"{name:{width}s}  {'':13s}  {'-' if rule is None else rule:>4}  "
-                             f"{'sdpa (no rule)' if names is None else ', '.join(names)}"
-                             f"{'  (vector softmax)' if rule is None and names is not None else ''}")
+                what = "sdpa (no rule)" if names is None else ", ".join(names)
+                if rule is None and names is not None:
+                    what += "  (vector softmax)"
+                out.append(f"{name:{w}s}  {'':13s}  {mark(rule):>4}  {what}")
         if any(self.vector.values()):
-            n = {"softmax": sum(names is not None for _, _, names in self.cores), "rmsnorm": len(self.norms)}
-            lines.append("vector  " + ", ".join(f"{op} {p or 'as transformers'}" + (f" ({n[op]} modules)" if p else "")
-                                                for op, p in self.vector.items()))
-        return "\n".join(lines)
+            count = {"softmax": sum(names is not None for *_, names in self.cores), "rmsnorm": len(self.norms)}
+            parts = []
+            for op, precision in self.vector.items():
+                parts.append(f"{op} {precision or 'as transformers'}" + (f" ({count[op]} modules)" if precision else ""))
+            out.append("vector  " + ", ".join(parts))
+        return "\n".join(out)
 
 
+# --------------------------------------------------------------------------------------------- patch
 def patch(model: nn.Module, rules: Sequence[Rule], chunk: Optional[int] = None, dry_run: bool = False,
           cache_weights: bool = True, vector=None) -> Handle:
+    """Route the model's Linear layers (and attention cores) through the Schemes the rules choose; see the module
+    docstring. Returns a Handle (printed, with nothing changed, when dry_run)."""
     vector = resolve(vector)
-    for i, rule in enumerate(rules):
-        if len(rule) != 2 or not (rule[1] is None or isinstance(rule[1], Scheme) or _is_core(rule[1])):
-            raise ValueError(f"rule {i} must be (selector, Scheme or None or (qk Scheme, pv Scheme)), got {rule!r}")
-    linear_rules = [i for i, (_, v) in enumerate(rules) if not _is_core(v)]
-    core_rules = [i for i, (_, v) in enumerate(rules) if _is_core(v)]
-
-    walk = list(model.named_modules(remove_duplicate=False))           # a module held twice is seen under both
-    holder = {name: module for name, module in walk}
-
-    def parent_of(name):
-        return holder[name.rpartition(".")[0]]
-
-    chosen = [(name, mod, parent_of(name),
-               next((i for i in linear_rules if _matches(rules[i][0], name, mod, parent_of(name))), None))
-              for name, mod in walk if name and isinstance(mod, nn.Linear)]
-    cores = [(name, mod, next((i for i in core_rules if _matches(rules[i][0], name, mod, parent_of(name))), None))
-             for name, mod in walk if name and _holds_core(mod)]
-    unused = [i for i in linear_rules if all(hit != i for *_, hit in chosen)]
-    if unused:
-        raise ValueError(f"rules {unused} choose no Linear layer (misspelt, or hidden behind an earlier rule): "
-                         f"{[rules[i][0] for i in unused]}")
-    unused = [i for i in core_rules if all(hit != i for *_, hit in cores)]
-    if unused:
-        raise ValueError(f"rules {unused} choose no attention module (one holding q_proj and k_proj): "
-                         f"{[rules[i][0] for i in unused]}")
-    for module in {id(m): m for _, m, hit in cores if hit is not None}.values():
-        if len({hit for _, m, hit in cores if m is module}) > 1:
-            raise ValueError(f"{[n for n, m, _ in cores if m is module]} are the same attention module but match "
-                             "different rules; one of them has to go")
-
-    sites: dict = {}                                                  # one attribute = one place a layer runs
-    for row in chosen:
-        name, _, parent, _ = row
-        sites.setdefault((id(parent), name.rpartition(".")[2]), []).append(row)
-    for rows_ in sites.values():
-        if len({r[3] for r in rows_}) > 1:
-            raise ValueError(f"{[r[0] for r in rows_]} are the same layer but match different rules "
-                             f"{[r[3] for r in rows_]}; one of them has to go")
-
-    if vector["softmax"] and not cores:
+    survey = _Survey(model)
+    _decide(rules, survey)
+    if vector["softmax"] and not survey.attention:
         raise ValueError("vector softmax: the model has no attention module (one holding q_proj and k_proj)")
-    norms = list({id(m): (n, m) for n, m in walk if n and _is_rmsnorm(m)}.values()) if vector["rmsnorm"] else []
+    norms = survey.norms if vector["rmsnorm"] else []
     if vector["rmsnorm"] and not norms:
         raise ValueError("vector rmsnorm: the model has no module whose class name ends in RMSNorm")
 
-    for i in linear_rules:                                            # fail now, not mid-run
-        if rules[i][1] is not None:
-            _smoke(rules[i][1])
-    for i in core_rules:
-        _smoke_core(*rules[i][1])
-    if vector["softmax"] and any(hit is None for *_, hit in cores):
-        _smoke_core(EXACT, EXACT)
-    eps = [_check_rmsnorm(n, m) for n, m in norms]
+    def core(rule):                                          # the (qk, pv) an attention module runs; None: sdpa
+        if rule is not None:
+            return rules[rule][1]
+        return (EXACT, EXACT) if vector["softmax"] else None
 
-    table = [(name, m.in_features, m.out_features, hit,
-              None if hit is None or rules[hit][1] is None else rules[hit][1].name) for name, m, _, hit in chosen]
+    # everything that could fail runs before the model is touched
+    for selector, value in rules:
+        if isinstance(value, Scheme):
+            _try_scheme(value)
+    for selector, value in rules:
+        if _core_pair(value):
+            _try_core(*value)
+    if vector["softmax"] and any(s.rule is None for s in survey.attention):
+        _try_core(EXACT, EXACT)
+    eps = [_norm_eps(n, m) for n, m in norms]
 
-    def core_of(hit):
-        return rules[hit][1] if hit is not None else (EXACT, EXACT) if vector["softmax"] else None
+    def scheme_name(rule):
+        return None if rule is None or rules[rule][1] is None else rules[rule][1].name
 
-    core_table = [(name, hit, None if core_of(hit) is None else tuple(s.name for s in core_of(hit)))
-                  for name, _, hit in cores]
-    replaced = []
-    if not dry_run:
-        for rows_ in sites.values():
-            name, module, parent, hit = rows_[0]
-            if hit is None or rules[hit][1] is None:
-                continue
-            leaf = name.rpartition(".")[2]
-            setattr(parent, leaf, MXLinear(module, rules[hit][1], chunk, cache_weights))
-            replaced.append((parent, leaf, module))
-    cored, previous = [], None
-    if not dry_run and any(core_of(hit) is not None for *_, hit in cores):
-        register()
-        previous = model.config._attn_implementation
-        for _, module, hit in {id(m): (n, m, h) for n, m, h in cores if core_of(h) is not None}.values():
-            module._mxq_core = core_of(hit)
-            if vector["softmax"]:
-                module._mxq_vector = vector["softmax"]
-            cored.append(module)
-        _set_attention(model, _CORE)
-    normed = []
-    if not dry_run:
-        for (_, module), e in zip(norms, eps):
-            module.forward = partial(_rmsnorm_forward, module, e, vector["rmsnorm"])
-            normed.append(module)
-    handle = Handle(model, table, replaced, core_table, cored, previous, vector, [n for n, _ in norms], normed)
+    table = [(s.name, s.module.in_features, s.module.out_features, s.rule, scheme_name(s.rule))
+             for s in survey.linears]
+    cores = [(s.name, s.rule, None if core(s.rule) is None else tuple(x.name for x in core(s.rule)))
+             for s in survey.attention]
+    handle = Handle(table, cores, vector, [n for n, _ in norms])
     if dry_run:
         print(handle)
+        return handle
+
+    for group in _sites(survey.linears).values():
+        s = group[0]
+        if s.rule is None or rules[s.rule][1] is None:
+            continue
+        setattr(s.parent, s.attr, MXLinear(s.module, rules[s.rule][1], chunk, cache_weights))
+        handle._did(partial(setattr, s.parent, s.attr, s.module))
+
+    routed = {}                                              # id -> (module, core), one entry per module
+    for s in survey.attention:
+        if core(s.rule) is not None:
+            routed[id(s.module)] = (s.module, core(s.rule))
+    if routed:
+        register()
+        before = model.config._attn_implementation
+        for module, pair in routed.values():
+            module._mxq_core = pair
+            if vector["softmax"]:
+                module._mxq_vector = vector["softmax"]
+            handle._did(partial(_drop_core, module))
+        _attention_impl(model, _CORE)
+        handle._did(partial(_attention_impl, model, before))
+
+    for (name, module), e in zip(norms, eps):
+        module.forward = partial(_norm_forward, module, e, vector["rmsnorm"])
+        handle._did(partial(delattr, module, "forward"))     # the class's own forward again
     return handle
+
+
+def _drop_core(module: nn.Module) -> None:
+    del module._mxq_core
+    if hasattr(module, "_mxq_vector"):
+        del module._mxq_vector

@@ -16,6 +16,9 @@ Fixtures (all numpy .npz, float32 results compared bit for bit, NaN positions on
     lut.npz           lut.tables / pick / lookup / finder / encode / values and block.lut.quantize
     nn.npz            Scheme.matmul, MXLinear.forward and attend on small shapes
     model.npz         a small random-init Llama patched as config 5: logits, and every MXLinear's input / output
+    api.npz           the rounding modules, block.compose with the reference's own steps and the blocking helpers,
+                      schedule.load / fixed, the vector ops and vector="bf16" through patch, attend on decode / GQA /
+                      multi-chunk causal shapes, patch's tables and errors, mxq.nn.torchao.MXQConfig
 """
 import argparse
 import json
@@ -477,6 +480,270 @@ def child(only):
         out["scheme/A"], out["scheme/B"], out["scheme/Y"] = N(A), N(B), N(hw.matmul(A, B))
         np.savez_compressed(os.path.join(HERE, "nn.npz"), **out)
         print("nn.npz:", len(out), "arrays", flush=True)
+
+
+    # ------------------------------------------------------------------------- the rest of the public API
+    if want("api"):
+        api(np, torch, T, N)
+
+
+def api(np, torch, T, N):
+    """api.npz: the rounding modules' bits / integer forms, block.compose with scale_factor / element_quant
+    callables and the blocking helpers, schedule.load / fixed (results and error messages), the vector ops and
+    vector="bf16" through patch, attend on decode / GQA / multi-chunk causal shapes, patch's dry-run table and
+    errors, and mxq.nn.torchao.MXQConfig (imported with a stand-in for the absent torchao: only its base class and
+    handler registry are touched)."""
+    import tempfile
+    import types
+    from functools import partial
+    from mxq import block, matmul, rounding, scale_factor, schedule
+    from mxq.block import _driver
+    from mxq.element_quant import float_em, microsoft
+    out, msgs = {}, {}
+
+    # rounding.{rne,ties_away,truncate}.bits / integer
+    rng = np.random.default_rng(21)
+    bits = np.concatenate([hard_corpus(np, 500).view(np.uint32).astype(np.int64),
+                           np.array([0xFFFFFFFF, 0xFFFFFFF0, 0x7FFFFFFF, 0xFFFF8000, 0xFFFFFFFF << 4, -1, -2 ** 40,
+                                     2 ** 40 + 12345, 0x80000000, 0x7F7FFFFF], np.int64),
+                           rng.integers(-2 ** 45, 2 ** 45, 500)])
+    out["rbits/bits"] = bits
+    keep = rng.integers(0, 23, bits.size)
+    out["rbits/keep"] = keep
+    bt = torch.tensor(bits)
+    for name, mod in (("rne", rounding.rne), ("ties_away", rounding.ties_away), ("truncate", rounding.truncate)):
+        for k in (0, 3, 7, 10, 22):
+            drop = 23 - k
+            out[f"rbits/{name}/{k}"] = N(mod.bits(bt, drop, (1 << drop) - 1, 1 << (drop - 1)))
+        d, m, h = rounding._drop(bt, torch.tensor(keep))
+        out[f"rbits/{name}/tensor"] = N(mod.bits(bt, d, m, h))
+        kk = np.concatenate([(rng.standard_normal(400) * 40).astype(np.float32), np.arange(-20, 20) / 4])
+        out["rint/in"] = kk.astype(np.float32)
+        out[f"rint/{name}/f32"] = N(mod.integer(T(kk)))
+        out[f"rint/{name}/f64"] = N(mod.integer(T(kk, torch.float64) * 1.5))
+
+    # block.compose with the reference's own steps, and the blocking helpers
+    V3 = (rng.standard_normal((3, 45, 6)) * 2.0 ** rng.uniform(-12, 12, (3, 1, 6))).astype(np.float32)
+    V3[0, :32, 0] = 0.0
+    V3[1, 5, 2] = np.float32(2.0 ** -140)
+    out["compose/V"] = V3
+    steps = {
+        "mxquant_hwfloor": (partial(scale_factor.mxquant, floor=2.0 ** -23),
+                            partial(float_em.quantize, e=4, m=3, rounding_mode="ties_away", grid="qtorch")),
+        "ocp_microsoft": (partial(scale_factor.ocp, emax=8), partial(microsoft.quantize, fmt="MXFP8_E4M3")),
+        "mxquant_ocp_rne": (scale_factor.mxquant, partial(float_em.quantize, e=3, m=2, rounding_mode="rne",
+                                                           grid="ocp")),
+        "below_top": (partial(scale_factor.ocp_below_top, emax=4),
+                      partial(microsoft.quantize, fmt="MXFP6_E3M2", rounding_mode="nearest")),
+        "no_clip": (partial(scale_factor.ocp_no_clip, fmt="MXFP6_E2M3"), partial(microsoft.quantize, fmt="MXFP6_E2M3")),
+        "ieee_truncate": (partial(scale_factor.ocp, emax=15, scale_bits=5),
+                          partial(float_em.quantize, e=5, m=2, rounding_mode="truncate", grid="ieee")),
+        "no_scale": (None, partial(float_em.quantize, e=4, m=3, rounding_mode="rne", grid="ocp")),
+        "no_elem": (scale_factor.mxquant, None),
+        "neither": (None, None),
+    }
+    for name, (sc, el) in steps.items():
+        for axis, bs in ((0, 32), (1, 32), (1, 16), (2, 4), (-1, 3), (1, 7)):
+            P, X = block.compose(T(V3), scale=sc, elem=el, axis=axis, block_size=bs)
+            out[f"compose/{name}/{axis}/{bs}/P"], out[f"compose/{name}/{axis}/{bs}/X"] = N(P), N(X)
+    for axis, bs in ((0, 32), (1, 16), (1, 7), (2, 4)):
+        b = _driver.to_blocks(T(V3), axis, bs)
+        out[f"blocks/{axis}/{bs}/data"] = N(b.data)
+        out[f"blocks/{axis}/{bs}/codes"] = N(_driver.codes_from_blocks(b.data * 2 + 1, b))
+        out[f"blocks/{axis}/{bs}/scales"] = N(_driver.scales_from_blocks(b.data.abs().amax(-1, keepdim=True), b))
+        Xb = _driver.scales_from_blocks(b.data.abs().amax(-1, keepdim=True), b)
+        out[f"blocks/{axis}/{bs}/dequantize"] = N(block.dequantize(T(V3), Xb, axis=axis, block_size=bs))
+
+    # schedule.load / fixed
+    hw = "\n".join(f"{i},{e},{m}" for i, (e, m) in enumerate(schedule.HW_FINAL))
+    csvs = {
+        "header3": "position,e,m\n" + hw + "\n",
+        "plain3": hw + "\n",
+        "four": "pos,B,e,m\n" + "\n".join(f"{15 - i}, 32 ,{e},{m}" for i, (e, m) in enumerate(schedule.HW_FINAL[::-1])),
+        "skips": "# lanes\n" + "\n".join(f"{i},{e},{m}\n{i},x" for i, (e, m) in enumerate(schedule.HW_FINAL)) + "\n,,\n",
+        "rows8": "\n".join(f"{i},4,{3 + i}" for i in range(8)),
+        "twice": hw + "\n3,4,4\n",
+        "outside": hw + "\n16,4,4\n",
+        "negative": hw + "\n-1,4,4\n",
+        "missing": "\n".join(f"{i},4,4" for i in range(16) if i not in (2, 11)),
+        "empty": "",
+        "header_only": "position,e,m\n",
+    }
+    msgs["schedule/csv"] = csvs
+    with tempfile.TemporaryDirectory() as d:
+        for name, text in csvs.items():
+            path = os.path.join(d, name + ".csv")
+            with open(path, "w") as f:
+                f.write(text)
+            rows = 8 if name == "rows8" else 16
+            try:
+                msgs[f"schedule/{name}"] = {"ok": [list(x) for x in schedule.load(path, rows=rows)], "rows": rows}
+            except ValueError as e:
+                msgs[f"schedule/{name}"] = {"error": str(e).replace(path, "<path>"), "rows": rows}
+    msgs["schedule/fixed"] = [list(x) for x in schedule.fixed(5, 6, rows=4)]
+
+    # the vector ops, and attend on more shapes
+    from mxq import Scheme
+    from mxq.nn import attend, _vector
+    S = (rng.standard_normal((6, 40)) * 4).astype(np.float32)
+    S[2, 30:] = np.finfo(np.float32).min
+    out["vector/S"] = S
+    out["vector/softmax_bf16"] = N(_vector.softmax(T(S), "bf16"))
+    xr = (rng.standard_normal((5, 64)) * 3).astype(np.float32)
+    wr = (1 + rng.standard_normal(64) * 0.1).astype(np.float32)
+    out["vector/x"], out["vector/w"] = xr, wr
+    out["vector/rmsnorm_bf16"] = N(_vector.rmsnorm(T(xr), T(wr), 1e-6, "bf16"))
+    out["vector/rmsnorm_none"] = N(_vector.rmsnorm(T(xr), T(wr), 1e-6, None))
+    q8 = partial(block.mxgemmini.quantize, fmt="MXFP8_E4M3", axis=0)
+    hw_s = Scheme("hw", a=q8, b=q8, reduce=partial(matmul.systolic, arith=matmul.MXGEMMINI(), schedule=schedule.HW_FINAL))
+    g = torch.Generator().manual_seed(22)
+    fmin = torch.finfo(torch.float32).min
+    shapes = {
+        "decode": (2, 4, 1, 23, 2, None),                    # B, H, Tq, Tk, Hkv, chunk
+        "gqa4": (1, 8, 12, 12, 2, None),
+        "causal_chunks": (2, 4, 64, 64, 2, 16),
+        "padded_chunks": (2, 2, 40, 40, 1, 8),
+    }
+    for name, (B, H, Tq, Tk, Hkv, ch) in shapes.items():
+        qa = torch.randn(B, H, Tq, 32, generator=g)
+        ka = torch.randn(B, Hkv, Tk, 32, generator=g)
+        va = torch.randn(B, Hkv, Tk, 32, generator=g)
+        mask = torch.triu(torch.full((Tq, Tk), fmin), diagonal=Tk - Tq + 1)[None, None].repeat(B, 1, 1, 1)
+        if name == "padded_chunks":
+            mask[1, :, :, :9] = fmin                         # left padding of batch row 1
+        for k_, t in (("q", qa), ("k", ka), ("v", va), ("mask", mask)):
+            out[f"attend/{name}/{k_}"] = N(t)
+        out[f"attend/{name}/o"] = N(attend(qa, ka, va, mask, 32 ** -0.5, hw_s, hw_s, chunk=ch))
+        out[f"attend/{name}/o_bf16"] = N(attend(qa, ka, va, mask, 32 ** -0.5, hw_s, hw_s, chunk=ch, vector="bf16"))
+
+    # vector="bf16" through patch, and patch's dry-run table and errors
+    from mxq.nn import patch, is_attention
+    from transformers import LlamaConfig, LlamaForCausalLM
+    import contextlib
+    import io
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=96, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=16, vocab_size=128, max_position_embeddings=64,
+                      initializer_range=0.02)
+    ids = torch.randint(0, 128, (2, 24), generator=torch.Generator().manual_seed(23))
+    out["model/ids"] = N(ids)
+    settings = {"bf16": ([("lm_head", None), ("model.layers.*.self_attn", (hw_s, hw_s)), (torch.nn.Linear, hw_s)],
+                         "bf16"),
+                "rmsnorm": ([("lm_head", None), (torch.nn.Linear, hw_s)], {"rmsnorm": "bf16"}),
+                "softmax_exact": ([("lm_head", None), (is_attention, None), (torch.nn.Linear, hw_s)],
+                                  {"softmax": "bf16"})}
+    for name, (rules, vec) in settings.items():
+        torch.manual_seed(0)
+        model = LlamaForCausalLM(cfg).float().eval()
+        buf = io.StringIO()
+        with contextlib.redirect_stdout(buf):
+            patch(model, rules, dry_run=True, vector=vec)
+        msgs[f"patch/{name}/dry_run"] = buf.getvalue()
+        handle = patch(model, rules, vector=vec)
+        with torch.no_grad():
+            out[f"model/{name}/logits"] = N(model(ids).logits)
+        handle.revert()
+        with torch.no_grad():
+            out[f"model/{name}/logits_reverted"] = N(model(ids).logits)
+
+    class Twice(torch.nn.Module):                            # one Linear held in two places
+        def __init__(self):
+            super().__init__()
+            self.a = torch.nn.Linear(32, 16)
+            self.b = self.a
+            self.c = torch.nn.Linear(16, 8)
+            self.att = torch.nn.Module()                     # an attention module: it holds q_proj and k_proj
+            self.att.q_proj = torch.nn.Linear(32, 32)
+            self.att.k_proj = torch.nn.Linear(32, 32)
+    errors = {
+        "bad_rule": lambda m: patch(m, [("a", "fp8")]),
+        "no_linear": lambda m: patch(m, [("nothing.*", hw_s), (torch.nn.Linear, None)]),
+        "hidden": lambda m: patch(m, [(torch.nn.Linear, None), ("c", hw_s)]),
+        "two_rules": lambda m: patch(m, [("a", hw_s), ("b", None), (torch.nn.Linear, None)]),
+        "no_core": lambda m: patch(m, [("x", (hw_s, hw_s))]),
+        "softmax_no_attention": lambda m: patch(m, [], vector="bf16"),
+        "vector_spelling": lambda m: patch(m, [], vector={"softmax": "fp16"}),
+    }
+    class Shared(torch.nn.Module):                           # a whole subtree held twice: one attribute, two names
+        def __init__(self):
+            super().__init__()
+            self.x = Twice()
+            self.y = self.x
+    errors["same_site"] = lambda m: patch(Shared(), [("x.c", hw_s), ("y.c", None), (torch.nn.Linear, None)])
+    errors["same_core"] = lambda m: patch(Shared(), [("x.att", (hw_s, hw_s)), (torch.nn.Linear, None)])
+    for name, fn in errors.items():
+        try:
+            fn(Twice())
+            msgs[f"patch_error/{name}"] = None
+        except ValueError as e:
+            msgs[f"patch_error/{name}"] = str(e)
+    buf = io.StringIO()
+    with contextlib.redirect_stdout(buf):
+        patch(Twice(), [("c", None), (torch.nn.Linear, hw_s)], dry_run=True)
+    msgs["patch/twice/dry_run"] = buf.getvalue()
+    buf = io.StringIO()
+    with contextlib.redirect_stdout(buf):
+        patch(Shared(), [("*.c", None), ("*.att", (hw_s, hw_s)), (is_attention, None), (torch.nn.Linear, hw_s)],
+              dry_run=True, vector={"rmsnorm": None, "softmax": "bf16"})
+    msgs["patch/shared/dry_run"] = buf.getvalue()
+
+    # mxq.nn.torchao.MXQConfig, with a stand-in for torchao's two names (base class, handler registry)
+    stub_core = types.ModuleType("torchao.core.config")
+
+    class AOBaseConfig:
+        pass
+    stub_core.AOBaseConfig = AOBaseConfig
+    stub_tm = types.ModuleType("torchao.quantization.transform_module")
+    stub_tm.register_quantize_module_handler = lambda cls: (lambda fn: fn)
+    for mname, mod in (("torchao", types.ModuleType("torchao")), ("torchao.core", types.ModuleType("torchao.core")),
+                       ("torchao.core.config", stub_core),
+                       ("torchao.quantization", types.ModuleType("torchao.quantization")),
+                       ("torchao.quantization.transform_module", stub_tm)):
+        sys.modules[mname] = mod
+    from mxq.nn import torchao as mt
+    from mxq.nn import MXLinear
+    lin = torch.nn.Linear(64, 24)
+    with torch.no_grad():
+        lin.weight.copy_(torch.randn(24, 64, generator=g) * 0.2)
+        lin.bias.copy_(torch.randn(24, generator=g))
+    x = torch.randn(2, 8, 64, generator=g)
+    out["torchao/W"], out["torchao/b"], out["torchao/x"] = N(lin.weight), N(lin.bias), N(x)
+    configs = {
+        "default": {},
+        "e2m3_truncate": {"fmt": "MXFP6_E2M3", "rounding_mode": "truncate", "scale_floor": 1e-38},
+        "prod44_nofloor": {"prod": (4, 4), "prod_floor": None, "ladder": [[8, 7]] * 16},
+        "exact": {"reduce": "exact"},
+        "lut": {"fmt": "MXFP6_E3M2", "lut": {"group": 1, "max_iters": 5}},
+        "size8": {"size": 8, "ladder": [[4, 6]] * 8, "block_size": 32, "chunk": 3},
+        "via": {"fmt": "MXFP4", "via": [3, 1]},
+    }
+    for name, kw in configs.items():
+        c = mt.MXQConfig(**kw)
+        msgs[f"torchao/{name}/dict"] = c.to_dict()
+        s = c.scheme("cpu")
+        msgs[f"torchao/{name}/scheme"] = {"name": s.name, "rows": s.rows, "block_size": s.block_size}
+        out[f"torchao/{name}/y"] = N(MXLinear(lin, s, chunk=c.chunk)(x))
+    bad = {
+        "fp32": {"fmt": "FP32"}, "reduce": {"reduce": "fast"}, "prod": {"prod": [4]},
+        "ladder_len": {"ladder": [[4, 4]] * 15}, "prod_floor": {"prod_floor": 1.5},
+        "block": {"block_size": 24}, "compiled": {"compiled": 1}, "chunk": {"chunk": 0},
+        "lut_keys": {"fmt": "MXFP6_E3M2", "lut": {"group": 1}}, "lut_fmt": {"fmt": "MXFP4", "lut": {"group": 1, "max_iters": 2}},
+        "lut_via": {"fmt": "MXFP6_E3M2", "via": [3, 1], "lut": {"group": 1, "max_iters": 2}},
+        "ladder_entry": {"ladder": [[4, 4]] * 15 + [[4, 0]]}, "from_dict_type": None,
+    }
+    for name, kw in bad.items():
+        try:
+            if kw is None:
+                mt.MXQConfig.from_dict({"_type": "Other", "_data": {}})
+            else:
+                mt.MXQConfig(**kw)
+            msgs[f"torchao_error/{name}"] = None
+        except ValueError as e:
+            msgs[f"torchao_error/{name}"] = str(e)
+    rt = mt.MXQConfig.from_dict({"_type": "MXQConfig", "_data": mt.MXQConfig(fmt="MXFP8_E5M2").to_dict()})
+    msgs["torchao/roundtrip"] = rt.to_dict()
+    out["msgs"] = np.array(json.dumps(msgs))
+    np.savez_compressed(os.path.join(HERE, "api.npz"), **out)
+    print("api.npz:", len(out), "arrays", flush=True)
 
 
 def main():
