@@ -7,17 +7,24 @@ Headline ("quantize GB/s"): the block-quantizer sweep.
 8192 x 8192 matrix -- N(0,1) x 2^U[-20,20] per row, 1% exact zeros, 0.1% float32-subnormal values -- with each of
 block.mxquant / block.mxgemmini / block.ocp, each of the five MX formats, along axis 0 and axis 1: 30 fused kernel
 launches. Throughput counts the algorithmic bytes of the reference's contract, 8.125 B per element (read V, write
-P, write X once per 32 elements). Every rank quantizes its own row shard (weak scaling, no collective).
+P, write X once per 32 elements). Under torchrun every rank quantizes its own 8192-row shard of an (N * 8192)-row
+matrix (weak scaling, no collective); the timed loop has nothing between launches, and each launch's own duration
+comes from a separate, untimed pass with CUDA events around every launch.
 
-Beside it, in the same JSON line, `systolic`: config 3's 4096^3 MXFP8_E4M3 systolic GEMM (MXGEMMINI / HW_FINAL,
-operands quantized by block.mxgemmini) in emulated GMAC/s, each rank reducing its own 4096-column panel of B;
-`reducers`: config 3's reducers (systolic MXGEMMINI and MXQUANT(4,3), adder tree, anchor tree) timed alone.
-
-`e2e` runs the same sweep through the public API with a pinned host V: every call streams V through the device in
-chunks and returns host P and X (copies in, kernels and copies out overlapped on three streams), all inside the
-timed region. `cpu_baseline` times the CPU oracle (oracle/, a C restatement of the reference algorithm; the
-reference itself is Python and does not travel) on the same matrix, swept twice (about 10 s on 16 cores).
-`--impl reference` is the reference arm: the oracle on all host cores, rank 0 only, same metric and unit.
+Beside it, in the same JSON line:
+  `parity`     the whole sweep (30 runs, P and X) compared bit for bit with the CPU oracle (oracle/, a C restatement
+               of the reference) on the same matrix, inside the cpu_baseline leg (rank 0, N = 1)
+  `sharded`    north_star's partitioning, strong scaling: ONE matrix / GEMM / operand / batch split across the N ranks
+               by mxq.shard and reassembled by one NCCL all_gather_into_tensor inside the timed region -- config 2
+               by rows, config 3's 4096^3 systolic GEMM by column panels of B, config 4's lut.tables by column groups,
+               config 5's batch of 8 by rows -- with the gather's bytes and time, and rank 0's bit-for-bit check of
+               the gathered result against its own whole-problem run
+  `systolic`, `reducers`   config 3's reducers, each with a roofline against a fixed, spec-derived issue-slot count
+               per emulated MAC (REDUCER_FLOORS)
+  `configs_1_4`, `packed`, `dequantize`, `model`
+  `e2e`        the sweep through the public API with a pinned host V per rank: every call streams V through the device
+               in chunks and returns host P and X (copies in, kernels and copies out overlapped on three streams)
+`--impl reference` is the reference arm: the CPU oracle on all host cores, rank 0 only, same metric, unit and config.
 """
 import argparse
 import datetime
@@ -43,6 +50,28 @@ BYTES_PER_ELEM = 8.125
 GEMM = 4096
 METRIC = "bit-exact MX block-quantize GB/s (config 2 sweep: 3 quantizers x 5 formats x 2 axes)"
 HW_FINAL = [(4, 4)] * 8 + [(4, 5)] * 2 + [(4, 6)] * 5 + [(8, 7)]
+LEVELS = [(4, 4), (4, 5), (4, 6), (8, 7)]
+
+# Issue slots per emulated MAC of each reducer datapath: the exact short forms of the kernels (their headers prove
+# them) counted from the arithmetic's definition, every float32 multiply / add paired on sm_100's packed FP32
+# instructions (half a slot per MAC), integer and compare / select steps one slot each, operand loads, register
+# moves and the per-block work (scales, tile add: 1/16 of a MAC or less) not counted. A lower bound on the
+# instructions, so MAC/s = 148 SMs x 4 schedulers x 32 lanes x clock / slots is an upper bound on the rate.
+REDUCER_FLOORS = {
+    # product 0.5 + 3-bit truncation mask 1 + snap onto the lane 1.0 + exact add 0.5 + lane RNE (exponent mask,
+    # offset add, two adds: 1 + 1 + 1.0)
+    "systolic MXGEMMINI/HW_FINAL": 6.0,
+    # product 0.5 + qtorch rounding of the product (add, mask) 2 + fake-subnormal snap 1.0 and its compare / select 2
+    # + lane add 0.5 + the lane's qtorch rounding 2 + its snap 1.0 and compare / select 2
+    "systolic MXQUANT(4,3)/HW_FINAL": 11.0,
+    # per 16 MACs: 16 products 8 + 16 masks 16; level 1: 8 folded snap-and-adds (3 adds each) 12 and 8 RNEs (2 integer
+    # + 2 adds each) 16 + 8; level 2: 4 adds 2 + 4 RNEs 8 + 4; level 3: 2 adds 1 + 2 RNEs 4 + 2; level 4: one add
+    # 0.5 and a bf16 pair conversion 0.5 -> 82 / 16
+    "adder_tree MXGEMMINI [(4,4),(4,5),(4,6),(8,7)]": 82.0 / 16.0,
+    # label sum 1 + label max 1 + product 0.5 + truncation mask 1 + scaling to the grid 0.5 + the keep step (sign
+    # mask 1, round-toward-zero add and subtract 1.0) + the exact sum 0.5
+    "anchor_tree MXGEMMINI (defaults)": 6.5,
+}
 
 
 def peaks():
@@ -50,9 +79,14 @@ def peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         p = json.load(open(path))
-        return float(p["hbm_gbs"]), "measured"
+        return {"hbm_gbs": float(p["hbm_gbs"]), "sm_max_mhz": float(p.get("sm_max_mhz", 1965.0)), "kind": "measured"}
     except Exception:
-        return 6650.0, "fallback"
+        return {"hbm_gbs": 6650.0, "sm_max_mhz": 1965.0, "kind": "fallback"}
+
+
+def issue_peak_macs(slots_per_mac, mhz):
+    """MAC/s when every SM scheduler issues one warp instruction per clock: 148 x 4 x 32 x clock / slots."""
+    return 148 * 4 * 32 * mhz * 1e6 / slots_per_mac
 
 
 def synthetic(rows, cols, seed, device=None):
@@ -69,6 +103,14 @@ def synthetic(rows, cols, seed, device=None):
     return V.contiguous()
 
 
+def headline_config(world):
+    """The `config` of the JSON line, the same for both arms."""
+    return {"workload": "config 2: block.{mxquant,mxgemmini,ocp}.quantize x 5 MX formats x axis {0,1} on an "
+                        "8192x8192 fp32 matrix per GPU", "rows_per_gpu": ROWS, "cols": COLS, "launches_per_step": 30,
+            "bytes_per_element": BYTES_PER_ELEM, "l2": "inputs (256 MiB per matrix) larger than L2; no flush",
+            "parallelism": f"rows x{world}"}
+
+
 class Clocks:
     """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
 
@@ -81,7 +123,7 @@ class Clocks:
              "clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.reader = threading.Thread(target=lambda: self.lines.extend(self.proc.stdout), daemon=True)
             self.reader.start()
@@ -128,180 +170,221 @@ def traffic_table():
 
 
 # ------------------------------------------------------------------------------------------------ GPU arm
-def run_gpu(args):
-    import torch
-    import torch.distributed as dist
-    import mxq
-    from mxq import block, matmul, schedule
+class Ranks:
+    """This process's place in the job and the device-side timing helpers (every rank runs the same collectives in
+    the same order)."""
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    def __init__(self):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=self.dev)
+        self.stream = torch.cuda.current_stream(self.dev)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
 
-    def max_over_ranks(x):
-        if world == 1:
+    def max(self, x):
+        if self.world == 1:
             return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t = self.torch.tensor([x], dtype=self.torch.float64, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
-    quant = {"mxquant": block.mxquant.quantize, "mxgemmini": block.mxgemmini.quantize, "ocp": block.ocp.quantize}
-    V = synthetic(ROWS, COLS, 1000 + rank, dev)             # this rank's row shard of the global matrix
-    runs = [(f, fmt, ax) for f in FAMILIES for fmt in FORMATS for ax in (0, 1)]
+    def all(self, ok):
+        """True on every rank when `ok` is true on every rank."""
+        if self.world == 1:
+            return bool(ok)
+        t = self.torch.tensor([0 if ok else 1], dtype=self.torch.int32, device=self.dev)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return int(t.item()) == 0
+
+    def timed(self, fn, steps):
+        """fn() once untimed, then `steps` calls between CUDA events on the launching stream, barriers on both
+        sides; the max over ranks of the mean ms per call."""
+        torch = self.torch
+        fn()
+        self.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        for _ in range(steps):
+            fn()
+        e1.record(self.stream)
+        self.barrier()
+        return self.max(e0.elapsed_time(e1)) / steps
+
+    def check_waits(self, leg):
+        from mxq import _lib
+        self.torch.cuda.synchronize()
+        _lib.check_waits()
+        return leg
+
+
+def same_bits(a, b):
+    """Bit-identical device tensors (float32 or int64), shape included."""
+    import torch
+    if a.shape != b.shape or a.dtype != b.dtype:
+        return False
+    if a.dtype == torch.float32:
+        return bool(torch.equal(a.view(torch.int32), b.view(torch.int32)))
+    return bool(torch.equal(a, b))
+
+
+def leg_sweep(R, args, quant, V, runs):
+    """The headline: `steps` sweeps back to back between two events, nothing between the launches; then an
+    untimed pass with events around every launch for each kernel's own duration."""
+    torch = R.torch
 
     def step():
         for f, fmt, ax in runs:
             quant[f](V, fmt, axis=ax)
 
-    # -- device-resident sweep: per-launch CUDA events on the launching stream, then the whole timed loop
-    stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
         step()
-    # per-launch durations: events around every launch of the first `nev` timed steps, on the launching stream
-    nev = min(args.steps, 20)
+    R.barrier()
+    est = R.timed(step, 2)                                     # ms per step, for the pre-roll below
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(R.local) as clk:
+        for _ in range(int(300 / max(est, 1e-3)) + 1):          # ~0.3 s of untimed sweeps while the sampler starts,
+            step()                                             # so every clock sample is taken under load
+        R.barrier()
+        start.record(R.stream)
+        for _ in range(args.steps):
+            step()
+        end.record(R.stream)
+        R.barrier()
+    ms = R.max(start.elapsed_time(end))
+    # the untimed pass: per-launch events (on the launching stream)
+    nev = max(1, min(args.steps, 20))
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in runs]
            for _ in range(nev)]
-    barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(local) as clk:
-        barrier()
-        start.record(stream)
-        for s in range(args.steps):
-            if s < nev:
-                for (f, fmt, ax), (e0, e1) in zip(runs, evs[s]):
-                    e0.record(stream)
-                    quant[f](V, fmt, axis=ax)
-                    e1.record(stream)
-            else:
-                step()
-        end.record(stream)
-        barrier()
-    ms = max_over_ranks(start.elapsed_time(end))
-    per = {run: sum(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(nev)) / nev
-           for i, run in enumerate(runs)}
-    ms_step = ms / args.steps
-    elems = ROWS * COLS
-    total_bytes = BYTES_PER_ELEM * elems * len(runs) * world
-    value = total_bytes / (ms_step * 1e-3) / 1e9
+    for s in range(nev):
+        for (f, fmt, ax), (e0, e1) in zip(runs, evs[s]):
+            e0.record(R.stream)
+            quant[f](V, fmt, axis=ax)
+            e1.record(R.stream)
+    R.barrier()
+    per = {run: sum(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(nev)) / nev for i, run in enumerate(runs)}
+    R.check_waits("sweep")
+    return ms / args.steps, per, clk.summary()
 
-    # dominant kernel: the (family, axis) pair with the largest share of the sweep
-    by_kernel = {}
-    for (f, fmt, ax), t in per.items():
-        by_kernel.setdefault((f, ax), []).append(t)
-    dom, dom_ms = max(((k, sum(v)) for k, v in by_kernel.items()), key=lambda kv: kv[1])
-    dom_avg = dom_ms / len(by_kernel[dom])
-    hbm, peak_kind = peaks()
-    achieved = BYTES_PER_ELEM * elems / (dom_avg * 1e-3) / 1e9
-    kname = f"{dom[0]}/axis{dom[1]}"
-    tr = traffic_table().get(kname)
 
-    # -- the compact form: the OCP-grid families' sweep writing byte codes and E8M0 scales, through the C ABI (the
-    # Python call reads its status word after every launch; the bench reads one at the end)
+def leg_packed(R, args, V):
+    """The compact form: the OCP-grid families' sweep writing byte codes and E8M0 scales, through the C ABI."""
     import ctypes
+    torch = R.torch
     from mxq import _lib
     from mxq.block import mxgemmini as _mg, ocp as _oc
     pk_runs = [(f, fmt, ax) for f in ("mxgemmini", "ocp") for fmt in FORMATS for ax in (0, 1)]
-    pk_st = torch.zeros(1, dtype=torch.int32, device=dev)
-    pk_out = {}
+    st = torch.zeros(1, dtype=torch.int32, device=R.dev)
+    out = {}
     for f, fmt, ax in pk_runs:
         spec = (_mg.spec(fmt) if f == "mxgemmini" else _oc.spec(fmt))
         fe = spec.e + spec.m
-        codes = torch.empty((ROWS, COLS // 2 if fe == 3 else COLS), dtype=torch.uint8, device=dev)
-        scales = torch.empty((ROWS // 32, COLS) if ax == 0 else (ROWS, COLS // 32), dtype=torch.uint8, device=dev)
+        codes = torch.empty((ROWS, COLS // 2 if fe == 3 else COLS), dtype=torch.uint8, device=R.dev)
+        scales = torch.empty((ROWS // 32, COLS) if ax == 0 else (ROWS, COLS // 32), dtype=torch.uint8, device=R.dev)
         lay = (1, ROWS, COLS) if ax == 0 else (ROWS, COLS, 1)
-        pk_out[(f, fmt, ax)] = (spec, codes, scales, lay, fe)
+        out[(f, fmt, ax)] = (spec, codes, scales, lay, fe)
 
-    def pk_step():
+    def step():
         for run in pk_runs:
-            spec, codes, scales, lay, _ = pk_out[run]
+            spec, codes, scales, lay, _ = out[run]
             _lib.call("mxq_block_quantize_packed", _lib.ptr(V), _lib.ptr(codes), _lib.ptr(scales), *lay, 32,
-                      ctypes.byref(spec), _lib.ptr(pk_st), ctypes.c_void_p(stream.cuda_stream))
+                      ctypes.byref(spec), _lib.ptr(st), ctypes.c_void_p(R.stream.cuda_stream))
 
     for _ in range(args.warmup):
-        pk_step()
-    barrier()
-    pk_steps = max(1, min(args.steps, 100))
-    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    p0.record(stream)
-    for _ in range(pk_steps):
-        pk_step()
-    p1.record(stream)
-    barrier()
-    if int(pk_st.item()):
-        raise RuntimeError("bench: the compact sweep reported a value the form cannot hold")
-    pk_ms = max_over_ranks(p0.elapsed_time(p1)) / pk_steps
-    pk_bytes = sum(elems * (4 + (0.5 if pk_out[r][4] == 3 else 1.0) + 1 / 32) for r in pk_runs) * world
-    packed = {"workload": "compact form: block.{mxgemmini,ocp}.quantize_packed x 5 MX formats x axis {0,1} on the "
-                          "same matrix (uint8 OCP codes, FP4 two a byte, E8M0 scale bytes), C ABI",
-              "GB/s": round(pk_bytes / (pk_ms * 1e-3) / 1e9, 1),
-              "Gelem/s": round(elems * len(pk_runs) * world / (pk_ms * 1e-3) / 1e9, 1),
-              "float32 path Gelem/s": round(elems * len(runs) * world / (ms_step * 1e-3) / 1e9, 1),
-              "ms_per_step": round(pk_ms, 4), "launches_per_step": len(pk_runs), "steps": pk_steps,
-              "bytes_per_element": "4 read + 1 code (FP4 0.5) + 1/32 scale"}
-    # -- the way back: dequantize (P, X) and the compact form's unpack / dequantize_packed, two formats x two axes
-    def timed(fn, reps):
-        fn()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(reps):
-            fn()
-        e1.record(stream)
-        e1.synchronize()
-        return e0.elapsed_time(e1) / reps
-    back = {"workload": "block.dequantize of the float32 codes, block.unpack and block.dequantize_packed of the "
-                        "compact form, on the sweep's matrix (mxgemmini codes)",
-            "bytes_per_element": "dequantize 8.125; unpack code + 4 + 1.125/32; dequantize_packed code + 4 + 1/32"}
+        step()
+    steps = max(1, min(args.steps, 100))
+    ms = R.timed(step, steps)
+    if int(st.item()):
+        raise RuntimeError(f"bench: the compact sweep reported status {int(st.item())}")
+    R.check_waits("packed")
+    elems = ROWS * COLS
+    nbytes = sum(elems * (4 + (0.5 if out[r][4] == 3 else 1.0) + 1 / 32) for r in pk_runs) * R.world
+    return out, {"workload": "compact form: block.{mxgemmini,ocp}.quantize_packed x 5 MX formats x axis {0,1} on the "
+                             "same matrix (uint8 OCP codes, FP4 two a byte, E8M0 scale bytes), C ABI",
+                 "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                 "Gelem/s": round(elems * len(pk_runs) * R.world / (ms * 1e-3) / 1e9, 1),
+                 "ms_per_step": round(ms, 4), "launches_per_step": len(pk_runs), "steps": steps,
+                 "bytes_per_element": "4 read + 1 code (FP4 0.5) + 1/32 scale"}
+
+
+def leg_dequantize(R, args, quant, V, packed_out):
+    """The way back: dequantize (P, X) and the compact form's unpack / dequantize_packed."""
+    from mxq import block
+    elems = ROWS * COLS
+    res = {"workload": "block.dequantize of the float32 codes, block.unpack and block.dequantize_packed of the "
+                       "compact form, on the sweep's matrix (mxgemmini codes)",
+           "bytes_per_element": "dequantize 8.125; unpack code + 4 + 1.125/32; dequantize_packed code + 4 + 1/32"}
     reps = max(1, min(args.steps, 50))
     for fmt in ("MXFP8_E4M3", "MXFP4"):
         for ax in (0, 1):
-            spec, codes, scales, lay, fe = pk_out[("mxgemmini", fmt, ax)]
+            spec, codes, scales, lay, fe = packed_out[("mxgemmini", fmt, ax)]
             cb = 0.5 if fe == 3 else 1.0
             P, X = quant["mxgemmini"](V, fmt, axis=ax)
-            t_dq = timed(lambda: block.dequantize(P, X, axis=ax), reps)
-            t_un = timed(lambda: block.unpack(codes, scales, fmt), reps)
-            t_dp = timed(lambda: block.dequantize_packed(codes, scales, fmt, axis=ax), reps)
-            back[f"{fmt}/axis{ax}"] = {
-                "dequantize GB/s": round(BYTES_PER_ELEM * elems / (t_dq * 1e-3) / 1e9, 1),
-                "unpack GB/s": round((cb + 4 + 1.125 / 32) * elems / (t_un * 1e-3) / 1e9, 1),
-                "dequantize_packed GB/s": round((cb + 4 + 1 / 32) * elems / (t_dp * 1e-3) / 1e9, 1)}
+            t_dq = R.timed(lambda: block.dequantize(P, X, axis=ax), reps)
+            t_un = R.timed(lambda: block.unpack(codes, scales, fmt), reps)
+            t_dp = R.timed(lambda: block.dequantize_packed(codes, scales, fmt, axis=ax), reps)
+            res[f"{fmt}/axis{ax}"] = {
+                "dequantize GB/s": round(BYTES_PER_ELEM * elems * R.world / (t_dq * 1e-3) / 1e9, 1),
+                "unpack GB/s": round((cb + 4 + 1.125 / 32) * elems * R.world / (t_un * 1e-3) / 1e9, 1),
+                "dequantize_packed GB/s": round((cb + 4 + 1 / 32) * elems * R.world / (t_dp * 1e-3) / 1e9, 1)}
             del P, X
-    del pk_out
+    return res
 
-    # -- end to end through the public API with host tensors: each call streams its pinned host V through the
-    # device and returns pinned host P, X (copies in and out on their own streams, overlapping the kernels); the
-    # call returns once the results are on the host, so the host clock brackets the whole transfer
+
+def leg_e2e(R, quant, V, runs):
+    """The sweep through the public API with this rank's pinned host V; the calls return with P and X on the host,
+    so the host clock brackets the whole transfer (max over ranks)."""
     Vh = V.cpu().pin_memory()
-    e2e_steps = max(1, min(3, args.steps))
+    steps = 2
 
-    def e2e_step():
+    def step():
         for f, fmt, ax in runs:
             quant[f](Vh, fmt, axis=ax)
 
-    e2e_step()
-    barrier()
+    step()
+    R.barrier()
     t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        e2e_step()
-    barrier()
-    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3) / e2e_steps
-    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
-    h2d = 4 * elems * len(runs) * world                     # whole job, like value
-    d2h = (4 * elems + 4 * elems // 32) * len(runs) * world
+    for _ in range(steps):
+        step()
+    R.barrier()
+    ms = R.max((time.perf_counter() - t0) * 1e3) / steps
+    elems = ROWS * COLS
+    total = BYTES_PER_ELEM * elems * len(runs) * R.world
+    return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": 4 * elems * len(runs) * R.world,
+            "d2h_bytes_per_step": (4 * elems + 4 * elems // 32) * len(runs) * R.world, "ms_per_step": round(ms, 3)}
 
-    # -- config 3: the systolic GEMM, one 4096-column panel per rank
-    gsteps = max(1, args.gemm_steps)
-    gen = torch.Generator(device=dev).manual_seed(7)
-    A = torch.randn(GEMM, GEMM, generator=gen, device=dev)
-    B = torch.randn(GEMM, GEMM, generator=torch.Generator(device=dev).manual_seed(8 + rank), device=dev)
+
+def gemm_operands(R, seed_b=8):
+    torch = R.torch
+    A = torch.randn(GEMM, GEMM, generator=torch.Generator(device=R.dev).manual_seed(7), device=R.dev)
+    B = torch.randn(GEMM, GEMM, generator=torch.Generator(device=R.dev).manual_seed(seed_b), device=R.dev)
+    return A, B
+
+
+def reducer_roofline(name, gmacs, mhz):
+    slots = REDUCER_FLOORS[name]
+    peak = issue_peak_macs(slots, mhz) / 1e9
+    return {"bound": "issue", "slots_per_mac": round(slots, 4), "achieved": round(gmacs, 1),
+            "peak": round(peak, 1), "unit": "GMAC/s", "frac": round(gmacs / peak, 4),
+            "clock_mhz": mhz, "peak_kind": "148 SMs x 4 schedulers x 32 lanes x clock / slots_per_mac"}
+
+
+def leg_reducers(R, args, mhz):
+    """config 3: the 4096^3 systolic GEMM with its quantization (per rank: its own B, weak), and the four reducers
+    alone on both operand formats, each against its issue-slot roofline."""
+    from mxq import block, matmul, schedule
+    A, B = gemm_operands(R, 8 + R.rank)
     arith = matmul.MXGEMMINI()
 
     def gemm():
@@ -309,182 +392,317 @@ def run_gpu(args):
         P_B, X_B = block.mxgemmini.quantize(B, "MXFP8_E4M3", axis=0)
         return matmul.systolic(P_A, X_A, P_B, X_B, arith, schedule.HW_FINAL)
 
-    for _ in range(max(1, args.warmup // 2)):
-        gemm()
-    barrier()
-    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    g0.record(stream)
-    for _ in range(gsteps):
-        gemm()
-    g1.record(stream)
-    barrier()
-    gms = max_over_ranks(g0.elapsed_time(g1)) / gsteps
-    gmacs = GEMM ** 3 * world / (gms * 1e-3) / 1e9
-
-    # -- config 3's reducers on both operand formats (reducer kernel alone, CUDA events)
-    def timed(fn, steps):
-        fn()
-        barrier()
-        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        for _ in range(steps):
-            fn()
-        t1.record(stream)
-        barrier()
-        return max_over_ranks(t0.elapsed_time(t1)) / steps
-
-    red_out = {}
+    gms = R.timed(gemm, max(1, args.gemm_steps))
+    gmacs = GEMM ** 3 * R.world / (gms * 1e-3) / 1e9
+    systolic = {"metric": "bit-exact MX systolic-emulated GMAC/s", "value": round(gmacs, 2), "unit": "GMAC/s",
+                "workload": f"config 3: quantize A, B ({GEMM}x{GEMM} MXFP8_E4M3, block.mxgemmini) + systolic "
+                            f"MXGEMMINI/HW_FINAL {GEMM}^3 per GPU", "ms_per_gemm": round(gms, 3),
+                "steps": max(1, args.gemm_steps),
+                "roofline": reducer_roofline("systolic MXGEMMINI/HW_FINAL", gmacs / R.world, mhz)}
+    reds = {"workload": f"config 3: {GEMM}^3 per GPU on MXFP8_E4M3 and MXFP6_E2M3 codes, reducer alone",
+            "steps": args.reducer_steps}
     for fmt in ("MXFP8_E4M3", "MXFP6_E2M3") if args.reducer_steps > 0 else ():
         P_A, X_A = block.mxgemmini.quantize(A, fmt, axis=0)
         P_B, X_B = block.mxgemmini.quantize(B, fmt, axis=0)
-        reducers = {
+        fns = {
             "systolic MXGEMMINI/HW_FINAL": lambda: matmul.systolic(P_A, X_A, P_B, X_B, arith, schedule.HW_FINAL),
             "systolic MXQUANT(4,3)/HW_FINAL": lambda: matmul.systolic(P_A, X_A, P_B, X_B, matmul.MXQUANT(4, 3),
                                                                       schedule.HW_FINAL),
-            "adder_tree MXGEMMINI [(4,4),(4,5),(4,6),(8,7)]": lambda: matmul.adder_tree(
-                P_A, X_A, P_B, X_B, arith, [(4, 4), (4, 5), (4, 6), (8, 7)]),
+            "adder_tree MXGEMMINI [(4,4),(4,5),(4,6),(8,7)]": lambda: matmul.adder_tree(P_A, X_A, P_B, X_B, arith,
+                                                                                        LEVELS),
             "anchor_tree MXGEMMINI (defaults)": lambda: matmul.anchor_tree(P_A, X_A, P_B, X_B, arith),
         }
-        for name, fn in reducers.items():
-            rms = timed(fn, args.reducer_steps)
-            red_out[f"{fmt} {name}"] = {"GMAC/s": round(GEMM ** 3 * world / (rms * 1e-3) / 1e9, 1),
-                                        "ms": round(rms, 3)}
+        for name, fn in fns.items():
+            rms = R.timed(fn, args.reducer_steps)
+            g = GEMM ** 3 * R.world / (rms * 1e-3) / 1e9
+            reds[f"{fmt} {name}"] = {"GMAC/s": round(g, 1), "ms": round(rms, 3),
+                                     "roofline": reducer_roofline(name, g / R.world, mhz)}
         del P_A, X_A, P_B, X_B
+    R.check_waits("reducers")
+    return systolic, reds
 
-    # -- config 1: the PR1 systolic GEMM (quantize x^T and W^T, systolic), 256 x 512 x 512
-    extra = {}
-    if args.extra_steps > 0:
-        x = torch.randn(256, 512, generator=torch.Generator(device=dev).manual_seed(11), device=dev)
-        W = torch.randn(512, 512, generator=torch.Generator(device=dev).manual_seed(12), device=dev)
 
-        def pr1():
-            PA1, XA1 = block.mxgemmini.quantize(x.t().contiguous(), "MXFP8_E4M3", axis=0)
-            PB1, XB1 = block.mxgemmini.quantize(W.t().contiguous(), "MXFP8_E4M3", axis=0)
-            return matmul.systolic(PA1, XA1, PB1, XB1, arith, schedule.HW_FINAL)
+def leg_configs_1_4(R, args):
+    """config 1 (the PR1 GEMM, whole call) and config 4 (the LUT path on a 4096 x 4096 operand per rank)."""
+    torch = R.torch
+    from mxq import block, lut, matmul, schedule
+    out = {}
+    arith = matmul.MXGEMMINI()
+    x = torch.randn(256, 512, generator=torch.Generator(device=R.dev).manual_seed(11), device=R.dev)
+    W = torch.randn(512, 512, generator=torch.Generator(device=R.dev).manual_seed(12), device=R.dev)
 
-        ms1 = timed(pr1, 20 * args.extra_steps)
-        extra["config 1: PR1 systolic 256x512x512 (quantize x^T, W^T + systolic)"] = {
-            "GMAC/s": round(256 * 512 * 512 * world / (ms1 * 1e-3) / 1e9, 1), "us": round(ms1 * 1e3, 1)}
+    def pr1():
+        PA1, XA1 = block.mxgemmini.quantize(x.t().contiguous(), "MXFP8_E4M3", axis=0)
+        PB1, XB1 = block.mxgemmini.quantize(W.t().contiguous(), "MXFP8_E4M3", axis=0)
+        return matmul.systolic(PA1, XA1, PB1, XB1, arith, schedule.HW_FINAL)
 
-        # -- config 4: the LUT path on a 4096 x 4096 operand, column j ~ N(0, sigma_j^2), sigma_j = 2^U[-8, 8]
-        from mxq import lut
-        g4 = torch.Generator(device=dev).manual_seed(13 + rank)
-        V4 = torch.randn(4096, 4096, generator=g4, device=dev) * torch.exp2(
-            torch.rand(1, 4096, generator=g4, device=dev) * 16 - 8)
-        n4 = V4.numel()
-        for fmt in ("MXFP6_E3M2", "MXFP8_E4M3"):
-            for G in (1, 3):
-                ms4 = timed(lambda: block.lut.quantize(V4, fmt, 0, 32, rounding_mode="rne", scale_floor=2.0 ** -23,
-                                                       group=G, max_iters=50), args.extra_steps)
-                extra[f"config 4: block.lut {fmt} G={G}"] = {
-                    "GB/s": round(BYTES_PER_ELEM * n4 * world / (ms4 * 1e-3) / 1e9, 1), "ms": round(ms4, 3)}
-        P4 = block.mxgemmini.quantize(V4, "MXFP6_E3M2", 0, 32, rounding_mode="rne", scale_floor=2.0 ** -23)[0]
-        T4 = lut.tables(P4, "MXFP6_E3M2", group=1, max_iters=50)
-        C4 = lut.encode(P4, "MXFP6_E3M2")
-        for name, fn, bpe in (("lut.tables", lambda: lut.tables(P4, "MXFP6_E3M2", group=1, max_iters=50), 4),
-                              ("lut.pick", lambda: lut.pick(P4, T4, group=1), 12),
-                              ("lut.finder", lambda: lut.finder(C4, T4, "MXFP6_E3M2", group=1), 16)):
-            ms4 = timed(fn, args.extra_steps)
-            extra[f"config 4: {name} MXFP6_E3M2 G=1"] = {
-                "GB/s": round(bpe * n4 * world / (ms4 * 1e-3) / 1e9, 1), "ms": round(ms4, 3)}
-        del V4, P4, T4, C4
+    ms1 = R.timed(pr1, 20 * args.extra_steps)
+    out["config 1: PR1 systolic 256x512x512 (quantize x^T, W^T + systolic)"] = {
+        "GMAC/s": round(256 * 512 * 512 * R.world / (ms1 * 1e-3) / 1e9, 1), "us": round(ms1 * 1e3, 1)}
+    V4 = config4_operand(R, 13 + R.rank)
+    n4 = V4.numel()
+    for fmt in ("MXFP6_E3M2", "MXFP8_E4M3"):
+        for G in (1, 3):
+            ms4 = R.timed(lambda: block.lut.quantize(V4, fmt, 0, 32, rounding_mode="rne", scale_floor=2.0 ** -23,
+                                                     group=G, max_iters=50), args.extra_steps)
+            out[f"config 4: block.lut {fmt} G={G}"] = {
+                "GB/s": round(BYTES_PER_ELEM * n4 * R.world / (ms4 * 1e-3) / 1e9, 1), "ms": round(ms4, 3)}
+    P4 = block.mxgemmini.quantize(V4, "MXFP6_E3M2", 0, 32, rounding_mode="rne", scale_floor=2.0 ** -23)[0]
+    T4 = lut.tables(P4, "MXFP6_E3M2", group=1, max_iters=50)
+    C4 = lut.encode(P4, "MXFP6_E3M2")
+    for name, fn, bpe in (("lut.tables", lambda: lut.tables(P4, "MXFP6_E3M2", group=1, max_iters=50), 4),
+                          ("lut.pick", lambda: lut.pick(P4, T4, group=1), 12),
+                          ("lut.finder", lambda: lut.finder(C4, T4, "MXFP6_E3M2", group=1), 16)):
+        ms4 = R.timed(fn, args.extra_steps)
+        out[f"config 4: {name} MXFP6_E3M2 G=1"] = {
+            "GB/s": round(bpe * n4 * R.world / (ms4 * 1e-3) / 1e9, 1), "ms": round(ms4, 3)}
+    R.check_waits("configs 1 and 4")
+    return out
 
-    # -- config 5: the MXLinear-patched Llama decoder (random init, std 0.02), 8 x 1024 tokens per GPU, one forward
-    model_out = None
-    if args.model_steps > 0:
-        from functools import partial
-        from transformers import LlamaConfig, LlamaForCausalLM
-        from mxq import Scheme
-        from mxq.nn import patch
-        cfg = LlamaConfig(hidden_size=2048, intermediate_size=5632, num_hidden_layers=16, num_attention_heads=16,
-                          num_key_value_heads=16, head_dim=128, vocab_size=32000, max_position_embeddings=1024,
-                          initializer_range=0.02)
-        torch.manual_seed(0)
-        with torch.device(dev):
-            model = LlamaForCausalLM(cfg).float().eval()
-        q8 = partial(block.mxgemmini.quantize, fmt="MXFP8_E4M3", axis=0)
-        sch = Scheme("hw_fp8", a=q8, b=q8, reduce=partial(matmul.systolic, arith=arith, schedule=schedule.HW_FINAL))
-        handle = patch(model, [("lm_head", None), ("model.layers.*.self_attn", (sch, sch)), (torch.nn.Linear, sch)])
-        ids = torch.randint(0, 32000, (8, 1024), generator=torch.Generator(device=dev).manual_seed(14 + rank),
-                            device=dev)
-        with torch.no_grad():
-            msm = timed(lambda: model(ids).logits, args.model_steps)
-        macs = 8 * 1024 * 16 * (4 * 2048 * 2048 + 3 * 2048 * 5632) + 8 * 16 * 16 * 2 * 1024 * 1024 * 128
-        model_out = {"workload": "config 5: MXLinear-patched Llama (16 layers, hidden 2048, 16 heads x 128, FFN 5632, "
-                                 "vocab 32000), batch 8 x 1024 tokens per GPU, one forward, every Linear but lm_head "
-                                 "and the attention core through mxgemmini MXFP8_E4M3 + systolic MXGEMMINI/HW_FINAL",
-                     "tokens/s": round(8 * 1024 * world / (msm * 1e-3), 1),
-                     "emulated GMAC/s": round(macs * world / (msm * 1e-3) / 1e9, 1), "s_per_forward": round(msm / 1e3, 3),
-                     "steps": args.model_steps}
-        handle.revert()
-        del model, handle, ids
-        torch.cuda.empty_cache()
+
+def config4_operand(R, seed):
+    """config 4's V: 4096 x 4096, column j ~ N(0, sigma_j^2), sigma_j = 2^U[-8, 8]."""
+    torch = R.torch
+    g = torch.Generator(device=R.dev).manual_seed(seed)
+    return torch.randn(4096, 4096, generator=g, device=R.dev) * torch.exp2(
+        torch.rand(1, 4096, generator=g, device=R.dev) * 16 - 8)
+
+
+def llama(R):
+    """config 5's model: the MXLinear-patched Llama decoder (random init, std 0.02)."""
+    from functools import partial
+    from transformers import LlamaConfig, LlamaForCausalLM
+    from mxq import Scheme, block, matmul, schedule
+    from mxq.nn import patch
+    torch = R.torch
+    cfg = LlamaConfig(hidden_size=2048, intermediate_size=5632, num_hidden_layers=16, num_attention_heads=16,
+                      num_key_value_heads=16, head_dim=128, vocab_size=32000, max_position_embeddings=1024,
+                      initializer_range=0.02)
+    torch.manual_seed(0)
+    with torch.device(R.dev):
+        model = LlamaForCausalLM(cfg).float().eval()
+    q8 = partial(block.mxgemmini.quantize, fmt="MXFP8_E4M3", axis=0)
+    sch = Scheme("hw_fp8", a=q8, b=q8, reduce=partial(matmul.systolic, arith=matmul.MXGEMMINI(),
+                                                       schedule=schedule.HW_FINAL))
+    handle = patch(model, [("lm_head", None), ("model.layers.*.self_attn", (sch, sch)), (torch.nn.Linear, sch)])
+    return model, handle
+
+
+def leg_sharded(R, args, quant, runs):
+    """north_star's partitioning, strong scaling, through mxq.shard: one problem split over the ranks and gathered
+    by NCCL inside the timed region. Every rank builds the same inputs from the same seeds; rank 0 checks the
+    gathered outputs bit for bit against its own whole-problem run (an untimed pass)."""
+    torch = R.torch
+    from mxq import block, lut, matmul, schedule, shard
+    out = {"workload": "one problem split across the ranks by mxq.shard, reassembled by all_gather_into_tensor "
+                       "(NCCL) in the timed region; gather_ms = total - compute-only (gather=False) time"}
+    steps = max(1, min(args.steps, 10))
+
+    # config 2: one 8192 x 8192 matrix, rows split (whole blocks along axis 0, whole rows along axis 1)
+    V = synthetic(ROWS, COLS, 1000, R.dev)
+
+    def sweep(gather):
+        for f, fmt, ax in runs:
+            shard.quantize(quant[f], V, fmt, axis=ax, gather=gather)
+
+    t_all = R.timed(lambda: sweep(True), steps)
+    t_cmp = R.timed(lambda: sweep(False), steps)
+    ok = True
+    for f, fmt, ax in runs:                                   # the parity pass: every rank gathers, rank 0 checks
+        P, X = shard.quantize(quant[f], V, fmt, axis=ax)
+        if R.rank == 0:
+            Pw, Xw = quant[f](V, fmt, axis=ax)
+            ok &= same_bits(P, Pw) and same_bits(X, Xw)
+        del P, X
+    ok = R.all(ok)
+    gbytes = sum((ROWS * COLS + ROWS * COLS // 32) * 4 for _ in runs) * (R.world - 1) / max(1, R.world)
+    out["config 2: sweep, rows split"] = {
+        "GB/s": round(BYTES_PER_ELEM * ROWS * COLS * len(runs) / (t_all * 1e-3) / 1e9, 1),
+        "ms_per_step": round(t_all, 3), "compute_ms": round(t_cmp, 3), "gather_ms": round(t_all - t_cmp, 3),
+        "gather_bytes_received_per_rank": int(gbytes), "parity_vs_one_gpu": ok}
+    del V
+
+    # config 3: the 4096^3 systolic GEMM (MXGEMMINI / HW_FINAL), column panels of B
+    A, B = gemm_operands(R)
+    arith = matmul.MXGEMMINI()
+    P_A, X_A = block.mxgemmini.quantize(A, "MXFP8_E4M3", axis=0)
+    P_B, X_B = block.mxgemmini.quantize(B, "MXFP8_E4M3", axis=0)
+
+    def gemm(gather):
+        return shard.reduce(matmul.systolic, P_A, X_A, P_B, X_B, arith, schedule.HW_FINAL, gather=gather)
+
+    g_steps = max(1, args.gemm_steps)
+    t_all = R.timed(lambda: gemm(True), g_steps)
+    t_cmp = R.timed(lambda: gemm(False), g_steps)
+    Y = gemm(True)
+    ok = same_bits(Y, matmul.systolic(P_A, X_A, P_B, X_B, arith, schedule.HW_FINAL)) if R.rank == 0 else True
+    ok = R.all(ok)
+    out["config 3: systolic 4096^3, column panels"] = {
+        "GMAC/s": round(GEMM ** 3 / (t_all * 1e-3) / 1e9, 1), "ms": round(t_all, 3), "compute_ms": round(t_cmp, 3),
+        "gather_ms": round(t_all - t_cmp, 3),
+        "gather_bytes_received_per_rank": int(GEMM * GEMM * 4 * (R.world - 1) / R.world), "parity_vs_one_gpu": ok}
+    del A, B, P_A, X_A, P_B, X_B, Y
+
+    # config 4: lut.tables by column groups (E3M2, G = 1 and 3)
+    V4 = config4_operand(R, 13)
+    P4 = block.mxgemmini.quantize(V4, "MXFP6_E3M2", 0, 32, rounding_mode="rne", scale_floor=2.0 ** -23)[0]
+    for G in (1, 3):
+        def tabs(gather):
+            return shard.lut_tables(lut.tables, P4, "MXFP6_E3M2", group=G, max_iters=50, gather=gather)
+        t_all = R.timed(lambda: tabs(True), max(1, args.extra_steps))
+        t_cmp = R.timed(lambda: tabs(False), max(1, args.extra_steps))
+        T = tabs(True)
+        ok = same_bits(T, lut.tables(P4, "MXFP6_E3M2", group=G, max_iters=50)) if R.rank == 0 else True
+        ok = R.all(ok)
+        out[f"config 4: lut.tables MXFP6_E3M2 G={G}, column groups"] = {
+            "GB/s": round(4 * P4.numel() / (t_all * 1e-3) / 1e9, 1), "ms": round(t_all, 3),
+            "compute_ms": round(t_cmp, 3), "gather_ms": round(t_all - t_cmp, 3), "parity_vs_one_gpu": ok}
+    del V4, P4
+    R.check_waits("sharded")
+    return out
+
+
+def leg_model(R, args):
+    """config 5: batch 8 x 1024 tokens split across the ranks by batch row (mxq.shard.rows), logits gathered; rank
+    0 recomputes the last batch row on its own and compares (the north star's 1e-6 relative: the unquantized glue's
+    kernels may sum in another order for another batch size)."""
+    torch = R.torch
+    from mxq import shard
+    model, handle = llama(R)
+    ids = torch.randint(0, 32000, (8, 1024), generator=torch.Generator(device=R.dev).manual_seed(14), device=R.dev)
+    with torch.no_grad():
+        fwd = lambda x: model(x).logits                                    # noqa: E731
+        ms = R.timed(lambda: shard.rows(fwd, ids), args.model_steps)
+        logits = shard.rows(fwd, ids)
+        rel = 0.0
+        if R.rank == 0:
+            last = fwd(ids[-1:])
+            rel = float((logits[-1:] - last).abs().max() / last.abs().max())
+    ok = R.all(rel <= 1e-6)
+    macs = 8 * 1024 * 16 * (4 * 2048 * 2048 + 3 * 2048 * 5632) + 8 * 16 * 16 * 2 * 1024 * 1024 * 128
+    res = {"workload": "config 5: MXLinear-patched Llama (16 layers, hidden 2048, 16 heads x 128, FFN 5632, vocab "
+                       "32000), one forward of batch 8 x 1024 tokens split across the ranks by batch row, logits "
+                       "gathered; every Linear but lm_head and the attention core through mxgemmini MXFP8_E4M3 + "
+                       "systolic MXGEMMINI/HW_FINAL (causal key blocks skipped per query chunk)",
+           "tokens/s": round(8 * 1024 / (ms * 1e-3), 1), "emulated GMAC/s": round(macs / (ms * 1e-3) / 1e9, 1),
+           "s_per_forward": round(ms / 1e3, 3), "steps": args.model_steps, "scaling": "strong",
+           "gather_bytes_received_per_rank": int(8 * 1024 * 32000 * 4 * (R.world - 1) / R.world),
+           "last_row_alone_rel_diff": rel, "parity_within_1e-6": ok}
+    handle.revert()
+    del model, handle, ids, logits
+    torch.cuda.empty_cache()
+    R.check_waits("model")
+    return res
+
+
+def run_gpu(args):
+    import torch
+    from mxq import block
+    R = Ranks()
+    quant = {"mxquant": block.mxquant.quantize, "mxgemmini": block.mxgemmini.quantize, "ocp": block.ocp.quantize}
+    runs = [(f, fmt, ax) for f in FAMILIES for fmt in FORMATS for ax in (0, 1)]
+    V = synthetic(ROWS, COLS, 1000 + R.rank, R.dev)            # this rank's row shard of the global matrix
+
+    ms_step, per, clocks = leg_sweep(R, args, quant, V, runs)
+    elems = ROWS * COLS
+    value = BYTES_PER_ELEM * elems * len(runs) * R.world / (ms_step * 1e-3) / 1e9
+    by_kernel = {}
+    for (f, fmt, ax), t in per.items():
+        by_kernel.setdefault((f, ax), []).append(t)
+    dom, dom_ms = max(((k, sum(v)) for k, v in by_kernel.items()), key=lambda kv: kv[1])
+    dom_avg = dom_ms / len(by_kernel[dom])
+    pk = peaks()
+    achieved = BYTES_PER_ELEM * elems / (dom_avg * 1e-3) / 1e9
+    kname = f"{dom[0]}/axis{dom[1]}"
+
+    packed_out, packed = leg_packed(R, args, V)
+    back = leg_dequantize(R, args, quant, V, packed_out)
+    del packed_out
+    e2e = leg_e2e(R, quant, V, runs)
+    mhz = clocks.get("sm_mhz") or pk["sm_max_mhz"]
+    systolic, reducers = leg_reducers(R, args, mhz)
+    extra = leg_configs_1_4(R, args) if args.extra_steps > 0 else {}
+    sharded = leg_sharded(R, args, quant, runs) if args.sharded else None
+    model = leg_model(R, args) if args.model_steps > 0 else None
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(args.cpu_rows, args.cpu_repeats)
-    clocks = clk.summary()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
+    if R.rank == 0 and R.world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(V, quant, runs, args.cpu_repeats)
+    if R.world > 1:
+        R.dist.barrier()
+        R.dist.destroy_process_group()
+    if R.rank != 0:
         return
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": R.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded config-2 distribution, generated on device)",
-        "config": {"workload": "config 2: block.{mxquant,mxgemmini,ocp}.quantize x 5 MX formats x axis {0,1} on an "
-                               "8192x8192 fp32 matrix per GPU", "rows_per_gpu": ROWS, "cols": COLS,
-                   "launches_per_step": len(runs), "bytes_per_element": BYTES_PER_ELEM,
-                   "l2": "inputs (256 MiB per matrix) larger than L2; no flush", "parallelism": f"rows x{world}"},
-        "roofline": {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1), "peak": hbm,
-                     "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                     "traffic": tr},
+        "config": headline_config(R.world),
+        "roofline": {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
+                     "peak_kind": f"{pk['kind']} hbm_gbs", "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                     "traffic": traffic_table().get(kname),
+                     "timing": "each launch between CUDA events in an untimed pass after the timed loop"},
         "kernels": {f"{f}/{fmt}/axis{ax}": round(BYTES_PER_ELEM * elems / (t * 1e-3) / 1e9, 1)
                     for (f, fmt, ax), t in sorted(per.items())},
-        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": round(e2e_ms, 3)},
+        "e2e": e2e,
         "gpu_launches": len(runs) * args.steps,
         "clocks": clocks,
-        "systolic": {"metric": "bit-exact MX systolic-emulated GMAC/s", "value": round(gmacs, 2), "unit": "GMAC/s",
-                     "workload": f"config 3: quantize A, B ({GEMM}x{GEMM} MXFP8_E4M3, block.mxgemmini) + "
-                                 f"systolic MXGEMMINI/HW_FINAL {GEMM}^3 per GPU", "ms_per_gemm": round(gms, 3),
-                     "steps": gsteps},
-        "reducers": {"workload": f"config 3: {GEMM}^3 per GPU on MXFP8_E4M3 and MXFP6_E2M3 codes, reducer alone",
-                     "steps": args.reducer_steps, **red_out},
+        "systolic": systolic,
+        "reducers": reducers,
         "configs_1_4": {"workload": "config 1 (PR1 GEMM, whole call) and config 4 (LUT path, 4096 x 4096 per GPU); "
                                     "GB/s counts 8.125 B/element for block.lut, 4 tables, 12 pick, 16 finder",
                         "steps": args.extra_steps, **extra},
-        "model": model_out,
+        "sharded": sharded,
+        "model": model,
         "packed": packed,
         "dequantize": back,
     }
     if cpu is not None:
-        line["cpu_baseline"] = cpu
+        line["cpu_baseline"], line["parity"] = cpu
     print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------------------------------- CPU oracle
-def cpu_sweep_sample(rows, threads, repeats=1):
-    """The sweep, `repeats` times, on a `rows` x 8192 slice with the CPU oracle; returns (GB/s, seconds)."""
+def cpu_sweep_sample(Vh, threads):
+    """The sweep once on the host matrix Vh with the CPU oracle; returns (GB/s, seconds)."""
     import oracle
-    V = synthetic(rows, COLS, 1000).numpy()
     t0 = time.perf_counter()
-    for _ in range(repeats):
-        for f in FAMILIES:
-            for fmt in FORMATS:
-                for ax in (0, 1):
-                    oracle.block_quantize(V, f, fmt, ax, threads=threads)
+    for f in FAMILIES:
+        for fmt in FORMATS:
+            for ax in (0, 1):
+                oracle.block_quantize(Vh, f, fmt, ax, threads=threads)
     dt = time.perf_counter() - t0
-    return BYTES_PER_ELEM * V.size * 30 * repeats / dt / 1e9, dt
+    return BYTES_PER_ELEM * Vh.size * 30 / dt / 1e9, dt
 
 
-def cpu_baseline(rows, repeats):
+def cpu_baseline(V, quant, runs, repeats):
+    """The CPU oracle on the GPU's own matrix (copied to the host), all host threads, the sweep `repeats` times;
+    the first time through, each run's oracle P and X are compared bit for bit with the GPU's (the parity flag)."""
+    import oracle
+    import torch
     threads = os.cpu_count() or 1
-    gbs, dt = cpu_sweep_sample(rows, threads, repeats)
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"the same 30-run sweep, {repeats}x, on a {rows}x{COLS} matrix ({dt:.1f} s), CPU oracle (C "
-                      "restatement of the reference algorithm), float32, all host threads"}
+    Vh = V.cpu().numpy()
+    oracle_s, bad = 0.0, []
+    for f, fmt, ax in runs:
+        t0 = time.perf_counter()
+        Po, Xo = oracle.block_quantize(Vh, f, fmt, ax, threads=threads)
+        oracle_s += time.perf_counter() - t0
+        P, X = quant[f](V, fmt, axis=ax)
+        torch.cuda.synchronize()
+        P, X = P.cpu().numpy(), X.cpu().numpy()
+        if not (np.array_equal(P.view(np.uint32), Po.view(np.uint32)) and
+                np.array_equal(X.view(np.uint32), Xo.view(np.uint32))):
+            bad.append(f"{f}/{fmt}/axis{ax}")
+        del Po, Xo, P, X
+    for _ in range(max(0, repeats - 1)):
+        oracle_s += cpu_sweep_sample(Vh, threads)[1]
+    gbs = BYTES_PER_ELEM * Vh.size * 30 * max(1, repeats) / oracle_s / 1e9
+    cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+           "sample": f"the same 30-run sweep, {max(1, repeats)}x, on the GPU's own 8192x8192 matrix ({oracle_s:.1f} s),"
+                     " CPU oracle (C restatement of the reference algorithm), float32, all host threads"}
+    parity = {"checked": "all 30 runs of the timed sweep, P and X, the whole 8192x8192 matrix, against the CPU oracle",
+              "bit_exact": not bad, "mismatched_runs": bad}
+    return cpu, parity
 
 
 def run_reference(args):
@@ -493,26 +711,25 @@ def run_reference(args):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
+    Vh = synthetic(args.ref_rows, COLS, 1000).numpy()
     for _ in range(args.warmup):
-        cpu_sweep_sample(args.ref_rows, threads)
+        cpu_sweep_sample(Vh, threads)
     t0 = time.perf_counter()
-    per = []
     for _ in range(args.steps):
-        gbs, dt = cpu_sweep_sample(args.ref_rows, threads)
-        per.append(dt)
+        cpu_sweep_sample(Vh, threads)
     total = time.perf_counter() - t0
     value = BYTES_PER_ELEM * args.ref_rows * COLS * 30 * args.steps / total / 1e9
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
-        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1e3 * total / args.steps, 2), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded config-2 distribution)",
-        "config": {"workload": "config 2: block.{mxquant,mxgemmini,ocp}.quantize x 5 MX formats x axis {0,1}",
-                   "rows_per_step": args.ref_rows, "cols": COLS, "parallelism": "host threads"},
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * total / args.steps, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded config-2 distribution)", "config": headline_config(world),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"each step: the 30-run sweep on a {args.ref_rows}x{COLS} row slice with the CPU "
-                                   "oracle (the reference is pure Python/torch and is not installed on the GPU box; "
-                                   "its measured CPU rate is 0.03-1.5 GB/s per quantizer)"},
+                         "sample": f"each step: the 30-run sweep on a {args.ref_rows}x{COLS} row sample of the "
+                                   "workload with the CPU oracle, all host threads (the reference is pure "
+                                   "Python/torch and is not installed on the GPU box; its measured CPU rate is "
+                                   "0.03-1.5 GB/s per quantizer)"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -528,7 +745,7 @@ def main():
     ap.add_argument("--reducer-steps", type=int, default=1, help="timed runs of each config-3 reducer (0: skip)")
     ap.add_argument("--extra-steps", type=int, default=3, help="timed runs of configs 1 and 4 (0: skip)")
     ap.add_argument("--model-steps", type=int, default=1, help="timed forwards of the config-5 model (0: skip)")
-    ap.add_argument("--cpu-rows", type=int, default=ROWS, help="rows of the CPU-baseline matrix")
+    ap.add_argument("--no-sharded", dest="sharded", action="store_false", help="skip the strong-scaling leg")
     ap.add_argument("--cpu-repeats", type=int, default=2, help="sweeps of the CPU-baseline matrix")
     ap.add_argument("--ref-rows", type=int, default=256, help="rows per reference-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
