@@ -360,9 +360,33 @@ def leg_e2e(R, quant, V, runs):
     ms = R.max((time.perf_counter() - t0) * 1e3) / steps
     elems = ROWS * COLS
     total = BYTES_PER_ELEM * elems * len(runs) * R.world
-    return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "h2d_bytes_per_step": 4 * elems * len(runs) * R.world,
-            "d2h_bytes_per_step": (4 * elems + 4 * elems // 32) * len(runs) * R.world, "ms_per_step": round(ms, 3)}
+    h2d = 4 * elems * len(runs) * R.world
+    d2h = (4 * elems + 4 * elems // 32) * len(runs) * R.world
+    # the ceiling: the same bytes as plain pinned copies, host to device and back at once on two streams, every rank
+    # at the same time (no kernel), host clock, max over ranks
+    torch = R.torch
+    Ph = torch.empty_like(Vh, pin_memory=True)
+    Vd, Pd = torch.empty_like(V), torch.empty_like(V)
+    s_in, s_out = torch.cuda.Stream(R.dev), torch.cuda.Stream(R.dev)
+    reps = 10
+    R.barrier()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        with torch.cuda.stream(s_in):
+            Vd.copy_(Vh, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            Ph.copy_(Pd, non_blocking=True)
+    s_in.synchronize()
+    s_out.synchronize()
+    R.barrier()
+    cms = R.max((time.perf_counter() - t0) * 1e3) / reps
+    ceiling = (4 * elems + 4 * elems) * R.world / (cms * 1e-3) / 1e9          # bytes moved per second, whole job
+    moved = (h2d + d2h) / (ms * 1e-3) / 1e9
+    return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3),
+            "pcie": {"moved_GB/s": round(moved, 1), "ceiling_GB/s": round(ceiling, 1),
+                     "frac": round(moved / ceiling, 3),
+                     "ceiling_kind": "pinned copies in and out at once on every rank, no kernel, host clock"}}
 
 
 def gemm_operands(R, seed_b=8):
@@ -447,10 +471,45 @@ def leg_configs_1_4(R, args):
                                                      group=G, max_iters=50), args.extra_steps)
             out[f"config 4: block.lut {fmt} G={G}"] = {
                 "GB/s": round(BYTES_PER_ELEM * n4 * R.world / (ms4 * 1e-3) / 1e9, 1), "ms": round(ms4, 3)}
+    # the same calls through the C ABI, back to back with preallocated outputs and one status read at the end: the
+    # device's rate, without the Python call's preparation and its synchronous status check
+    import ctypes
+    from mxq import _lib
+    from mxq.block import mxgemmini as _mg
+    Pw, Xw = torch.empty_like(V4), torch.empty((4096 // 32, 4096), dtype=torch.float32, device=R.dev)
+    st = torch.zeros(1, dtype=torch.int32, device=R.dev)
+    stream = ctypes.c_void_p(R.stream.cuda_stream)
+    for fmt in ("MXFP6_E3M2", "MXFP8_E4M3"):
+        spec = _mg.spec(fmt, "rne", 2.0 ** -23)
+        for G in (1, 3):
+            ws = torch.empty(_lib.lib().mxq_block_lut_workspace(4096, 4096, 0, G), dtype=torch.uint8, device=R.dev)
+            call = lambda: _lib.call("mxq_block_lut_quantize", _lib.ptr(V4), _lib.ptr(Pw), _lib.ptr(Xw), 4096, 4096,  # noqa: E731
+                                     0, 32, ctypes.byref(spec), G, 50, _lib.ptr(ws), ws.numel(), _lib.ptr(st), stream)
+            ms4 = R.timed(call, max(10, args.extra_steps))
+            if int(st.item()):
+                raise RuntimeError("bench: block.lut reported an off-grid code")
+            out[f"config 4: block.lut {fmt} G={G} (C ABI, back to back)"] = {
+                "GB/s": round(BYTES_PER_ELEM * n4 * R.world / (ms4 * 1e-3) / 1e9, 1), "ms": round(ms4, 4)}
     P4 = block.mxgemmini.quantize(V4, "MXFP6_E3M2", 0, 32, rounding_mode="rne", scale_floor=2.0 ** -23)[0]
     T4 = lut.tables(P4, "MXFP6_E3M2", group=1, max_iters=50)
     C4 = lut.encode(P4, "MXFP6_E3M2")
+    Tw, Iw = torch.empty_like(T4), torch.empty((4096, 4096), dtype=torch.int64, device=R.dev)
+    for name, fn, bpe in (
+            ("lut.tables", lambda: _lib.call("mxq_lut_tables", _lib.ptr(P4), _lib.ptr(Tw), 4096, 4096, 4096, 1, 1, 50,
+                                             3, 2, _lib.ptr(st), stream), 4),
+            ("lut.pick", lambda: _lib.call("mxq_lut_pick", _lib.ptr(P4), _lib.ptr(T4), _lib.ptr(Iw), 4096, 4096, 4096,
+                                           1, 1, 16, stream), 12),
+            ("lut.finder", lambda: _lib.call("mxq_lut_finder", _lib.ptr(C4), _lib.ptr(T4), _lib.ptr(Iw), 4096, 4096, 1,
+                                             3, 2, _lib.ptr(st), stream), 16)):
+        ms4 = R.timed(fn, max(10, args.extra_steps))
+        if int(st.item()):
+            raise RuntimeError(f"bench: {name} reported a bad value")
+        out[f"config 4: {name} MXFP6_E3M2 G=1 (C ABI, back to back)"] = {
+            "GB/s": round(bpe * n4 * R.world / (ms4 * 1e-3) / 1e9, 1), "ms": round(ms4, 4)}
+    del Pw, Xw, Tw, Iw
     for name, fn, bpe in (("lut.tables", lambda: lut.tables(P4, "MXFP6_E3M2", group=1, max_iters=50), 4),
+                          ("lut.tables max_iters=0 (histogram and seeds, no Lloyd pass)",
+                           lambda: lut.tables(P4, "MXFP6_E3M2", group=1, max_iters=0), 4),
                           ("lut.pick", lambda: lut.pick(P4, T4, group=1), 12),
                           ("lut.finder", lambda: lut.finder(C4, T4, "MXFP6_E3M2", group=1), 16)):
         ms4 = R.timed(fn, args.extra_steps)
@@ -595,38 +654,50 @@ def leg_model(R, args):
     return res
 
 
+LEGS = ("sweep", "packed", "e2e", "reducers", "configs_1_4", "sharded", "model")
+
+
 def run_gpu(args):
     import torch
     from mxq import block
     R = Ranks()
+    legs = set(args.legs.split(",")) if args.legs else set(LEGS)
     quant = {"mxquant": block.mxquant.quantize, "mxgemmini": block.mxgemmini.quantize, "ocp": block.ocp.quantize}
     runs = [(f, fmt, ax) for f in FAMILIES for fmt in FORMATS for ax in (0, 1)]
     V = synthetic(ROWS, COLS, 1000 + R.rank, R.dev)            # this rank's row shard of the global matrix
-
-    ms_step, per, clocks = leg_sweep(R, args, quant, V, runs)
     elems = ROWS * COLS
-    value = BYTES_PER_ELEM * elems * len(runs) * R.world / (ms_step * 1e-3) / 1e9
-    by_kernel = {}
-    for (f, fmt, ax), t in per.items():
-        by_kernel.setdefault((f, ax), []).append(t)
-    dom, dom_ms = max(((k, sum(v)) for k, v in by_kernel.items()), key=lambda kv: kv[1])
-    dom_avg = dom_ms / len(by_kernel[dom])
     pk = peaks()
-    achieved = BYTES_PER_ELEM * elems / (dom_avg * 1e-3) / 1e9
-    kname = f"{dom[0]}/axis{dom[1]}"
 
-    packed_out, packed = leg_packed(R, args, V)
-    back = leg_dequantize(R, args, quant, V, packed_out)
-    del packed_out
-    e2e = leg_e2e(R, quant, V, runs)
+    value = ms_step = achieved = kname = None
+    per, clocks = {}, {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no timed sweep"]}
+    if "sweep" in legs:
+        ms_step, per, clocks = leg_sweep(R, args, quant, V, runs)
+        value = BYTES_PER_ELEM * elems * len(runs) * R.world / (ms_step * 1e-3) / 1e9
+        by_kernel = {}
+        for (f, fmt, ax), t in per.items():
+            by_kernel.setdefault((f, ax), []).append(t)
+        dom, dom_ms = max(((k, sum(v)) for k, v in by_kernel.items()), key=lambda kv: kv[1])
+        achieved = BYTES_PER_ELEM * elems / (dom_ms / len(by_kernel[dom]) * 1e-3) / 1e9
+        kname = f"{dom[0]}/axis{dom[1]}"
+
+    packed = back = e2e = systolic = reducers = sharded = model = None
+    if "packed" in legs:
+        packed_out, packed = leg_packed(R, args, V)
+        back = leg_dequantize(R, args, quant, V, packed_out)
+        del packed_out
+    if "e2e" in legs:
+        e2e = leg_e2e(R, quant, V, runs)
     mhz = clocks.get("sm_mhz") or pk["sm_max_mhz"]
-    systolic, reducers = leg_reducers(R, args, mhz)
-    extra = leg_configs_1_4(R, args) if args.extra_steps > 0 else {}
-    sharded = leg_sharded(R, args, quant, runs) if args.sharded else None
-    model = leg_model(R, args) if args.model_steps > 0 else None
+    if "reducers" in legs:
+        systolic, reducers = leg_reducers(R, args, mhz)
+    extra = leg_configs_1_4(R, args) if args.extra_steps > 0 and "configs_1_4" in legs else {}
+    if args.sharded and "sharded" in legs:
+        sharded = leg_sharded(R, args, quant, runs)
+    if args.model_steps > 0 and "model" in legs:
+        model = leg_model(R, args)
 
     cpu = None
-    if R.rank == 0 and R.world == 1 and not args.no_cpu_baseline:
+    if R.rank == 0 and R.world == 1 and not args.no_cpu_baseline and "sweep" in legs:
         cpu = cpu_baseline(V, quant, runs, args.cpu_repeats)
     if R.world > 1:
         R.dist.barrier()
@@ -634,14 +705,16 @@ def run_gpu(args):
     if R.rank != 0:
         return
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": R.world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+        "metric": METRIC, "value": None if value is None else round(value, 2), "unit": "GB/s", "n_gpus": R.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None if ms_step is None else round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded config-2 distribution, generated on device)",
         "config": headline_config(R.world),
-        "roofline": {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
-                     "peak_kind": f"{pk['kind']} hbm_gbs", "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
-                     "traffic": traffic_table().get(kname),
-                     "timing": "each launch between CUDA events in an untimed pass after the timed loop"},
+        "roofline": None if achieved is None else {
+            "bound": "hbm", "kernel": kname, "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
+            "peak_kind": f"{pk['kind']} hbm_gbs", "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+            "traffic": traffic_table().get(kname),
+            "timing": "each launch between CUDA events in an untimed pass after the timed loop"},
         "kernels": {f"{f}/{fmt}/axis{ax}": round(BYTES_PER_ELEM * elems / (t * 1e-3) / 1e9, 1)
                     for (f, fmt, ax), t in sorted(per.items())},
         "e2e": e2e,
@@ -749,6 +822,7 @@ def main():
     ap.add_argument("--cpu-repeats", type=int, default=2, help="sweeps of the CPU-baseline matrix")
     ap.add_argument("--ref-rows", type=int, default=256, help="rows per reference-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--legs", default="", help=f"comma-separated subset of {','.join(LEGS)} (default: all)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

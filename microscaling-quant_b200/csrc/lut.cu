@@ -5,10 +5,13 @@
 // Layout: an operand is addressed as element (k, j) = P[k * sk + j * sj], so the row-major K x n operand (sk = n,
 // sj = 1) and the transposed one of an axis-1 quantization (sk = 1, sj = K) are read in place.
 //
-// tables: one CTA per panel of column groups (at most 32 columns, sized so the grid covers every SM about twice). The
-// CTA histograms its panel's codes by grid rank in shared memory, then one warp per group fits the table
-// (kmeans.py:46-122) with the work spread over its lanes (k_lut_tables). Every sum is exact (codes times counts), so
-// no summation order changes a bit.
+// tables: a thread-block cluster per panel of column groups (32 columns, or one group when a group is wider). The
+// cluster's CTAs split the panel's rows and histogram their codes by grid rank in their own shared memory; after a
+// cluster barrier each CTA sums its share of the panel's groups over all the cluster's histograms through
+// distributed shared memory, and one warp per group fits the table (kmeans.py:46-122) with the work spread over its
+// lanes (k_lut_tables). Every sum is exact (integer counts, codes times counts), so no summation order changes a
+// bit.
+#include <cooperative_groups.h>
 #include <algorithm>
 #include <mutex>
 #include <vector>
@@ -17,6 +20,7 @@
 #include "numerics.cuh"
 
 using namespace mxq;
+namespace cg = cooperative_groups;
 
 namespace {
 
@@ -202,8 +206,9 @@ __device__ __forceinline__ double dedupe_lanes(double v, double* scratch) {
   return v;
 }
 
-// The tables (kmeans.py:46-122). A CTA per panel of gpc column groups: (1) the panel's codes histogrammed by grid
-// rank in shared memory; then one warp per group: (2) prefix sums of counts and of counts x values over the sorted
+// The tables (kmeans.py:46-122). A cluster of cs CTAs per panel of gpc column groups: (1) the panel's codes
+// histogrammed by grid rank, each CTA its rows into its own shared memory, then group gl merged across the cluster by
+// CTA gl % cs; then one warp per group: (2) prefix sums of counts and of counts x values over the sorted
 // codes (exact in float64: integers times grid values); the centres -- the present codes when there are at most 16,
 // else the quantile seeds, deduplicated, and weighted Lloyd passes until two passes agree to numpy.allclose or
 // max_iters have run; (3) each centre snapped to the nearest finder-safe value; (4) padded and sorted.
@@ -214,29 +219,35 @@ __device__ __forceinline__ double dedupe_lanes(double v, double* scratch) {
 // are differences of the prefix sums. That equals the reference's argmin over all 16 centres whenever consecutive
 // centres are at least 2^-33 apart (distances below 2^17 then never round to a tie across a centre); a pass that
 // finds two closer centres assigns code by code instead.
-__global__ void __launch_bounds__(NT) k_lut_tables(const float* __restrict__ P, int64_t K, int64_t n, int64_t sk,
+__global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ P, int64_t K, int64_t n, int64_t sk,
                                                    int64_t sj, int G, int gpc, int max_iters,
                                                    const __grid_constant__ TableParams tp, float* __restrict__ T,
                                                    int* __restrict__ status) {
-  extern __shared__ int counts[];                           // [gpc][nv]
+  extern __shared__ int counts[];                           // [gpc][nv]: this CTA's rows; then merged, own groups
   __shared__ double pw[NW][MAXV + 1], pwx[NW][MAXV + 1];     // prefix: counts, counts x values
   __shared__ double scratch[NW][LUT], fsum[NW][LUT], fw[NW][LUT];
   __shared__ float sgrid[MAXV];
   __shared__ unsigned char member[NW][MAXV];
   __shared__ int bad;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int cs = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nv = tp.nv;
   const unsigned lt = (1u << lane) - 1u;
   const int64_t ng = (n + ((int64_t)1 << G) - 1) >> G;
-  const int64_t g0 = (int64_t)blockIdx.x * gpc;
+  const int64_t g0 = (int64_t)(blockIdx.x / cs) * gpc;       // the cluster's panel of groups
   const int64_t j0 = g0 << G, jend = (g0 + gpc) << G, j1 = jend < n ? jend : n;
   const int64_t W = j1 - j0;
+  const int64_t kper = (K + cs - 1) / cs;                    // this CTA's rows of the panel
+  const int64_t kbeg = (int64_t)rank * kper < K ? (int64_t)rank * kper : K;
+  const int64_t kend = kbeg + kper < K ? kbeg + kper : K;
   for (int i = tid; i < gpc * nv; i += NT) counts[i] = 0;
   for (int i = tid; i < nv; i += NT) sgrid[i] = tp.grid[i];
   if (tid == 0) bad = 0;
   __syncthreads();
 
   // 1. counts of each distinct code per group (kmeans.py:58-64); consecutive threads read consecutive memory
-  const int64_t total = K * W;
+  const int64_t Kc = kend - kbeg;                           // rows of this CTA
+  const int64_t total = Kc * W;
   const bool kfast = sk == 1;
   bool mybad = false;
   constexpr int BATCH = 8;                                  // loads in flight per thread
@@ -254,15 +265,15 @@ __global__ void __launch_bounds__(NT) k_lut_tables(const float* __restrict__ P, 
       int gc[4];
 #pragma unroll
       for (int i = 0; i < 4; i++) gc[i] = (4 * q + i) >> G;
-      for (int64_t k0 = r; k0 < K; k0 += (int64_t)rows_per_pass * BATCH) {
+      for (int64_t k0 = kbeg + r; k0 < kend; k0 += (int64_t)rows_per_pass * BATCH) {
         float4 v[BATCH];
 #pragma unroll
         for (int u = 0; u < BATCH; u++)
-          v[u] = k0 + (int64_t)u * rows_per_pass < K ? src[(k0 + (int64_t)u * rows_per_pass) * (sk / 4)]
-                                                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          v[u] = k0 + (int64_t)u * rows_per_pass < kend ? src[(k0 + (int64_t)u * rows_per_pass) * (sk / 4)]
+                                                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
         for (int u = 0; u < BATCH; u++) {
-          if (k0 + (int64_t)u * rows_per_pass >= K) break;
+          if (k0 + (int64_t)u * rows_per_pass >= kend) break;
           count(v[u].x, gc[0]);
           count(v[u].y, gc[1]);
           count(v[u].z, gc[2]);
@@ -270,10 +281,10 @@ __global__ void __launch_bounds__(NT) k_lut_tables(const float* __restrict__ P, 
         }
       }
     }
-  } else {
-  // element e = (kfast ? jj * K + k : k * W + jj) walked without a division per element: the position (major,
+  } else if (total > 0) {
+  // element e = (kfast ? jj * Kc + k : k * W + jj) walked without a division per element: the position (major,
   // minor) advances by NT elements as (NT / R, NT % R) with R the minor extent, plus a carry
-  const int64_t R = kfast ? K : W, dmaj = NT / R, dmin = NT % R;
+  const int64_t R = kfast ? Kc : W, dmaj = NT / R, dmin = NT % R;
   int64_t maj = tid / R, mnr = tid % R;
   for (int64_t e0 = tid; e0 < total; e0 += (int64_t)NT * BATCH) {
     float v[BATCH];
@@ -283,7 +294,7 @@ __global__ void __launch_bounds__(NT) k_lut_tables(const float* __restrict__ P, 
       const int64_t e = e0 + (int64_t)u * NT;
       const int64_t k = kfast ? mnr : maj, jj = kfast ? maj : mnr;
       gcol[u] = e < total ? (int)(jj >> G) : -1;
-      v[u] = e < total ? P[k * sk + (j0 + jj) * sj] : 0.0f;
+      v[u] = e < total ? P[(kbeg + k) * sk + (j0 + jj) * sj] : 0.0f;
       maj += dmaj;
       mnr += dmin;
       if (mnr >= R) {
@@ -297,13 +308,24 @@ __global__ void __launch_bounds__(NT) k_lut_tables(const float* __restrict__ P, 
   }
   }
   if (mybad) bad = 1;
-  __syncthreads();
-  if (bad) {
-    if (tid == 0) atomicExch(status, 1);
-    return;
+  // the cluster's CTAs meet: every histogram of the panel is complete (cluster barriers order shared memory across
+  // the cluster); CTA r merges groups r, r + cs, ... from all of them into its own rows, then they meet again so no
+  // CTA leaves while another still reads its histograms. Every thread of every CTA reaches both barriers.
+  cluster.sync();
+  if (bad && tid == 0) atomicExch(status, 1);
+  if (cs > 1) {
+    for (int i = tid; i < gpc * nv; i += NT) {
+      const int gl = i / nv;
+      if (gl % cs != rank) continue;
+      int sum = 0;
+      for (int q = 0; q < cs; q++) sum += cluster.map_shared_rank(counts, q)[i];
+      counts[i] = sum;                                      // only this CTA reads row gl of its own histogram
+    }
   }
+  cluster.sync();
+  if (bad) return;                                          // every CTA saw its own flag before the barrier
 
-  for (int gl = warp; gl < gpc; gl += NW) {
+  for (int gl = rank + cs * warp; gl < gpc; gl += cs * NW) {
     const int64_t g = g0 + gl;
     if (g >= ng) break;
     const int* cnt = counts + gl * nv;
@@ -592,10 +614,14 @@ __global__ void k_lut_finder(const int64_t* __restrict__ codes, const float* __r
   }
 }
 
-// Column forms of pick and finder for a row-major K x n operand with 16-entry tables: thread j walks rows
-// [k0, k1) of column j with its group's table in registers, so the table is read (and, for the finder, encoded)
-// once per column instead of once per element; consecutive threads read consecutive columns.
-constexpr int CT = 256;
+// Column forms of pick and finder for a row-major K x n operand with 16-entry tables; consecutive threads take
+// consecutive columns and walk rows, so every warp reads and writes whole row segments.
+//   pick: a CTA owns a panel of CT = 256 columns (one per thread) and a slice of rows; the panel's tables are
+//         staged once per CTA (a copy), the search runs on them in shared memory.
+//   finder: a CTA owns a panel of PW = 32 columns (lane l of every warp is column l) and its 8 warps take the rows
+//         in turn, because each CTA first evaluates the answer for every (group, code) pair of its panel: with
+//         256-column panels that table work, repeated by every row slice, dominated the kernel.
+constexpr int CT = 256, PW = 32, CW = CT / 32;               // threads, finder panel columns, warps per CTA
 
 constexpr int ROWP = LUT + 1;                                // a table row in shared memory, padded (banks)
 
@@ -645,12 +671,13 @@ __global__ void __launch_bounds__(CT) k_lut_finder_cols(const int64_t* __restric
                                                         int64_t* __restrict__ I, int* __restrict__ status) {
   extern __shared__ unsigned char ans[];                     // [groups of the panel][ncodes]
   __shared__ F sfx[MAXV];
-  __shared__ F sft[CT][LUT];                                 // the panel's tables as fixed points
+  __shared__ F sft[PW][LUT];                                 // the panel's tables as fixed points
   __shared__ uint32_t sbits[MAXV];                           // encode's map (value bits -> lowest code), staged
   __shared__ int16_t scode[MAXV];
   const int nc = ct.ncodes, ne = ct.nenc;
-  const int64_t jp = (int64_t)blockIdx.x * CT;
-  const int64_t gfirst = jp >> G, glast = ((jp + CT < n ? jp + CT : n) - 1) >> G;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t jp = (int64_t)blockIdx.x * PW;
+  const int64_t gfirst = jp >> G, glast = ((jp + PW < n ? jp + PW : n) - 1) >> G;
   const int ngp = (int)(glast - gfirst + 1);
   const int64_t k0 = (int64_t)blockIdx.y * rows, k1 = k0 + rows < K ? k0 + rows : K;
   for (int i = threadIdx.x; i < nc; i += CT) sfx[i] = (F)ct.fx[i];
@@ -693,28 +720,32 @@ __global__ void __launch_bounds__(CT) k_lut_finder_cols(const int64_t* __restric
     ans[i] = (unsigned char)(key & 15);
   }
   __syncthreads();
-  const int64_t j = jp + threadIdx.x;
+  const int64_t j = jp + lane;
   if (j >= n) return;
   const unsigned char* a = ans + (int)((j >> G) - gfirst) * nc;
   constexpr int BATCH = 8;                                   // loads in flight per thread
-  for (int64_t kb = k0; kb < k1; kb += BATCH) {
+  for (int64_t kb = k0 + warp; kb < k1; kb += (int64_t)CW * BATCH) {
     int64_t c[BATCH];
 #pragma unroll
-    for (int u = 0; u < BATCH; u++) c[u] = kb + u < k1 ? codes[(kb + u) * n + j] : 0;
+    for (int u = 0; u < BATCH; u++) {
+      const int64_t k = kb + (int64_t)u * CW;
+      c[u] = k < k1 ? (int64_t)__ldcs(reinterpret_cast<const long long*>(codes) + k * n + j) : 0;
+    }
 #pragma unroll
     for (int u = 0; u < BATCH; u++) {
-      if (kb + u >= k1) break;
+      const int64_t k = kb + (int64_t)u * CW;
+      if (k >= k1) break;
       int64_t r = 0;
       if (c[u] < -nc || c[u] >= nc) atomicOr(status, 1);
       else r = a[c[u] < 0 ? c[u] + nc : c[u]];
-      I[(kb + u) * n + j] = r;
+      __stcs(reinterpret_cast<long long*>(I) + k * n + j, (long long)r);
     }
   }
 }
 
-// the column kernels' grid: column panels of CT threads, and row slices so that about per_sm CTAs per SM are launched
-dim3 cols_grid(int64_t K, int64_t n, int64_t* rows, int per_sm = 16) {
-  const int64_t panels = (n + CT - 1) / CT;
+// the column kernels' grid: panels of `width` columns, and row slices so that about per_sm CTAs per SM are launched
+dim3 cols_grid(int64_t K, int64_t n, int64_t width, int per_sm, int64_t* rows) {
+  const int64_t panels = (n + width - 1) / width;
   const int64_t want = per_sm * (int64_t)sm_count();
   int64_t slices = (want + panels - 1) / panels;
   if (slices > K) slices = K;
@@ -786,19 +817,38 @@ int mxq_lut_tables(const float* P, float* T, int64_t K, int64_t n, int64_t sk, i
     tp.safe[i] = f->safe[i];
     tp.order[i] = f->order[i];
   }
-  // groups per CTA: a panel of at most 32 columns (one group when it is wider), few enough groups that the grid
-  // covers every SM about twice (each group's fit is one warp)
-  const int64_t cap = group >= 5 ? 1 : (32 >> group);
-  int64_t want = (ng + 2 * (int64_t)sm_count() - 1) / (2 * (int64_t)sm_count());
-  if (group < 2) want = (want + (4 >> group) - 1) / (4 >> group) * (4 >> group);    // panels of whole float4
-  const int gpc = (int)(want < 1 ? 1 : (want > cap ? cap : want));
+  // A cluster of cs CTAs per panel of gpc groups (32 columns, or one group when a group is wider): the CTAs split
+  // the panel's rows for the histogram and its groups for the fits; cs (1..8) makes about three CTAs per SM.
+  const int gpc = group >= 5 ? 1 : (32 >> group);
+  const int64_t panels = (ng + gpc - 1) / gpc;
+  int cs = 1;
+  while (cs < 8 && panels * cs < 3 * (int64_t)sm_count() && 2 * cs <= K) cs *= 2;
   const size_t smem = (size_t)gpc * f->nv * sizeof(int);
-  const unsigned grid = (unsigned)((ng + gpc - 1) / gpc);
   // static (~40 KB) plus the histograms can pass the 48 KB default
   if (int r = check_cuda(cudaFuncSetAttribute(k_lut_tables, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                          "lut.tables: shared memory attribute"))
     return r;
-  k_lut_tables<<<grid, NT, smem, st>>>(P, K, n, sk, sj, group, gpc, max_iters, tp, T, status);
+  // all of shared memory for the L1 / shared split, so four CTAs (with their static ~40 KB) fit on an SM
+  if (int r = check_cuda(cudaFuncSetAttribute(k_lut_tables, cudaFuncAttributePreferredSharedMemoryCarveout, 100),
+                         "lut.tables: shared memory carveout"))
+    return r;
+  MXQ_REQUIRE(panels * cs < (1ll << 31), MXQ_ERR_UNSUPPORTED, "lut.tables: %lld column groups", (long long)ng);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(panels * cs));
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (int r = check_cuda(cudaLaunchKernelEx(&cfg, k_lut_tables, P, K, n, sk, sj, (int)group, gpc, (int)max_iters, tp,
+                                            T, status),
+                         "lut.tables"))
+    return r;
   return MXQ_LAUNCH_CHECK("lut.tables");
 }
 
@@ -808,7 +858,7 @@ int mxq_lut_pick(const float* P, const float* T, int64_t* I, int64_t K, int64_t 
   if (K * n == 0) return MXQ_OK;
   if (sj == 1 && sk == n && width == LUT && (uintptr_t)T % 16 == 0 && K < (1ll << 31)) {
     int64_t rows;
-    const dim3 grid = cols_grid(K, n, &rows);
+    const dim3 grid = cols_grid(K, n, CT, 16, &rows);
     k_lut_pick_cols<<<grid, CT, 0, as_stream(stream)>>>(P, T, K, n, group, rows, I, nullptr);
     return MXQ_LAUNCH_CHECK("lut.pick");
   }
@@ -822,7 +872,7 @@ int mxq_lut_pick_lookup(const float* P, const float* T, float* out, int64_t K, i
   if (K * n == 0) return MXQ_OK;
   if (sj == 1 && sk == n && width == LUT && (uintptr_t)T % 16 == 0 && K < (1ll << 31)) {
     int64_t rows;
-    const dim3 grid = cols_grid(K, n, &rows);
+    const dim3 grid = cols_grid(K, n, CT, 16, &rows);
     k_lut_pick_cols<<<grid, CT, 0, as_stream(stream)>>>(P, T, K, n, group, rows, nullptr, out);
     return MXQ_LAUNCH_CHECK("lut.pick_lookup");
   }
@@ -864,12 +914,10 @@ int mxq_lut_finder(const int64_t* codes, const float* T, int64_t* I, int64_t K, 
   if ((uintptr_t)T % 16 == 0 && K < (1ll << 31)) {
     int64_t rows;
     const FormatTables* f = format_tables(e, m);
-    // fewer, longer CTAs than pick: each CTA first builds its panel's answer table (ncodes per column group,
-    // 16 distances each), so row slices repeat that work (measured best: 4 per SM for 64 codes, 1 for 256)
-    const dim3 grid = cols_grid(K, n, &rows, f->ncodes <= 64 ? 4 : 1);
+    const dim3 grid = cols_grid(K, n, PW, 8, &rows);
     bool narrow = true;                                       // every fixed point and difference fits in an int
     for (int i = 0; i < f->ncodes; i++) narrow = narrow && f->fx[i] > -(1ll << 30) && f->fx[i] < (1ll << 30);
-    const size_t smem = (size_t)CT * f->ncodes;               // answers: at most one group per column
+    const size_t smem = (size_t)PW * f->ncodes;               // answers: at most one group per column
     int r;
     if (narrow) {
       r = check_cuda(cudaFuncSetAttribute(k_lut_finder_cols<int>, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -511,14 +511,14 @@ def api(np, torch, T, N):
     keep = rng.integers(0, 23, bits.size)
     out["rbits/keep"] = keep
     bt = torch.tensor(bits)
+    kk = np.concatenate([(rng.standard_normal(400) * 40).astype(np.float32), np.arange(-20, 20) / 4])
+    out["rint/in"] = kk.astype(np.float32)
     for name, mod in (("rne", rounding.rne), ("ties_away", rounding.ties_away), ("truncate", rounding.truncate)):
         for k in (0, 3, 7, 10, 22):
             drop = 23 - k
             out[f"rbits/{name}/{k}"] = N(mod.bits(bt, drop, (1 << drop) - 1, 1 << (drop - 1)))
         d, m, h = rounding._drop(bt, torch.tensor(keep))
         out[f"rbits/{name}/tensor"] = N(mod.bits(bt, d, m, h))
-        kk = np.concatenate([(rng.standard_normal(400) * 40).astype(np.float32), np.arange(-20, 20) / 4])
-        out["rint/in"] = kk.astype(np.float32)
         out[f"rint/{name}/f32"] = N(mod.integer(T(kk)))
         out[f"rint/{name}/f64"] = N(mod.integer(T(kk, torch.float64) * 1.5))
 
