@@ -156,12 +156,16 @@ const FormatTables* format_tables(int e, int m) {
 }
 
 // ------------------------------------------------------------------------------------------- device side
+constexpr int KEYS = 1 << 12;                  // bit-pattern keys of a code: sign, exponent, top m <= 3 fraction bits
 struct TableParams {                           // by value: what the tables kernel needs of a format
   int nv, nsafe;
   int nmag, bias, m;                           // grid = -mag[nmag-1] .. -mag[1], 0, mag[1] .. mag[nmag-1]
+  int keyshift;                                // 23 - m: a code's float32 pattern >> keyshift is its key
+  uint32_t lowmask;                            // the fraction bits below a code's m: zero in every code
   float grid[MAXV];
   float safe[MAXV];
   uint8_t order[MAXV];
+  uint8_t bin[KEYS];                           // key -> grid rank, 0xFF for a pattern that is no code
 };
 
 constexpr int NW = NT / 32;                    // warps per CTA
@@ -223,11 +227,12 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ 
                                                    int64_t sj, int G, int gpc, int max_iters,
                                                    const __grid_constant__ TableParams tp, float* __restrict__ T,
                                                    int* __restrict__ status) {
-  extern __shared__ int counts[];                           // [gpc][nv]: this CTA's rows; then merged, own groups
+  extern __shared__ int counts[];                           // [gpc][nv + 1]: this CTA's rows; then merged, own groups
   __shared__ double pw[NW][MAXV + 1], pwx[NW][MAXV + 1];     // prefix: counts, counts x values
   __shared__ double scratch[NW][LUT], fsum[NW][LUT], fw[NW][LUT];
   __shared__ float sgrid[MAXV];
   __shared__ unsigned char member[NW][MAXV];
+  __shared__ __align__(16) uint8_t sbin[KEYS];
   __shared__ int bad;
   cg::cluster_group cluster = cg::this_cluster();
   const int cs = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
@@ -240,8 +245,11 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ 
   const int64_t kper = (K + cs - 1) / cs;                    // this CTA's rows of the panel
   const int64_t kbeg = (int64_t)rank * kper < K ? (int64_t)rank * kper : K;
   const int64_t kend = kbeg + kper < K ? kbeg + kper : K;
-  for (int i = tid; i < gpc * nv; i += NT) counts[i] = 0;
+  const int nvp = nv + 1;                                   // a group's histogram row, padded: rows start on distinct banks
+  for (int i = tid; i < gpc * nvp; i += NT) counts[i] = 0;
   for (int i = tid; i < nv; i += NT) sgrid[i] = tp.grid[i];
+  for (int i = tid; i < KEYS / 4; i += NT)
+    reinterpret_cast<uint32_t*>(sbin)[i] = reinterpret_cast<const uint32_t*>(tp.bin)[i];
   if (tid == 0) bad = 0;
   __syncthreads();
 
@@ -251,12 +259,36 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ 
   const bool kfast = sk == 1;
   bool mybad = false;
   constexpr int BATCH = 8;                                  // loads in flight per thread
+  // a code's grid rank from its bit pattern: the key (sign, exponent, top m fraction bits) through the table; any
+  // other fraction bit set, or a key that names no code (NaN, Inf, off-grid), is not a code
   auto count = [&](float v, int gc) {
-    const int b = grid_rank(v, tp);
-    if (sgrid[b] != v) mybad = true;                        // also every NaN
-    else atomicAdd(&counts[gc * nv + b], 1);
+    const uint32_t u = f2u(v), b = sbin[u >> tp.keyshift];
+    if ((u & tp.lowmask) != 0u || b == 0xFFu) mybad = true;
+    else atomicAdd(&counts[gc * nvp + (int)b], 1);
   };
-  if (sj == 1 && W % 4 == 0 && W <= 4 * NT && sk % 4 == 0 && ((uintptr_t)P + j0 * 4) % 16 == 0) {
+  if (sj == 1 && W <= 32 && W % 2 == 0 && sk % 2 == 0 && ((uintptr_t)P + j0 * 4) % 8 == 0) {
+    // a panel of at most 32 columns as float2 pairs: lane l takes the pair of columns 2 (l % 16), 2 (l % 16) + 1 of
+    // row (l / 16) of its warp's two rows, so a warp instruction's 32 lanes count into (at G = 1) 16 different
+    // groups' rows and the 16-byte-per-lane-pair row segments are read whole; the CTA steps 2 x 8 rows
+    const int c2 = lane & 15, ro = lane >> 4;
+    if (2 * c2 < W) {
+      const float2* src = reinterpret_cast<const float2*>(P + j0) + c2;
+      const int ga = (2 * c2) >> G, gb = (2 * c2 + 1) >> G;
+      const int64_t step = 2 * NW;
+      for (int64_t k0 = kbeg + 2 * warp + ro; k0 < kend; k0 += step * BATCH) {
+        float2 v[BATCH];
+#pragma unroll
+        for (int u = 0; u < BATCH; u++)
+          v[u] = k0 + (int64_t)u * step < kend ? src[(k0 + (int64_t)u * step) * (sk / 2)] : make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int u = 0; u < BATCH; u++) {
+          if (k0 + (int64_t)u * step >= kend) break;
+          count(v[u].x, ga);
+          count(v[u].y, gb);
+        }
+      }
+    }
+  } else if (sj == 1 && W % 4 == 0 && W <= 4 * NT && sk % 4 == 0 && ((uintptr_t)P + j0 * 4) % 16 == 0) {
     // rows of the panel as float4: thread (row r, quad q) of rows_per_pass rows at a time, pointers advanced by
     // whole rows (no index arithmetic per element)
     const int qpr = (int)(W / 4), rows_per_pass = NT / qpr, r = tid / qpr, q = tid - r * qpr;
@@ -314,8 +346,8 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ 
   cluster.sync();
   if (bad && tid == 0) atomicExch(status, 1);
   if (cs > 1) {
-    for (int i = tid; i < gpc * nv; i += NT) {
-      const int gl = i / nv;
+    for (int i = tid; i < gpc * nvp; i += NT) {
+      const int gl = i / nvp;
       if (gl % cs != rank) continue;
       int sum = 0;
       for (int q = 0; q < cs; q++) sum += cluster.map_shared_rank(counts, q)[i];
@@ -328,7 +360,7 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ 
   for (int gl = rank + cs * warp; gl < gpc; gl += cs * NW) {
     const int64_t g = g0 + gl;
     if (g >= ng) break;
-    const int* cnt = counts + gl * nv;
+    const int* cnt = counts + gl * nvp;
     double* PW = pw[warp];
     double* PWX = pwx[warp];
     // 2. prefix sums over the sorted codes, and the number of distinct codes present
@@ -397,14 +429,19 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ 
         if (!__any_sync(0xffffffffu, close)) {
           int end = nv;                                                  // first code past centre t's run
           if (lane < LUT - 1 && finite_d(cn)) {
-            int lo = 0, hi = nv;
-            while (lo < hi) {
-              const int mid = (lo + hi) >> 1;
-              const double x = (double)sgrid[mid];
-              if (fabs(__dsub_rn(x, cn)) < fabs(__dsub_rn(x, c))) hi = mid;
-              else lo = mid + 1;
+            // the first code strictly closer to centre t + 1 (monotone along the sorted codes, as the gap check
+            // above guarantees): start at the codes around the midpoint of the two centres and walk to it
+            auto closer = [&](int k) {
+              const double x = (double)sgrid[k];
+              return fabs(__dsub_rn(x, cn)) < fabs(__dsub_rn(x, c));
+            };
+            int i = grid_rank((float)__dmul_rn(__dadd_rn(c, cn), 0.5), tp);
+            if (closer(i)) {
+              while (i > 0 && closer(i - 1)) i--;
+            } else {
+              while (i < nv && !closer(i)) i++;
             }
-            end = lo;
+            end = i;
           }
           int begin = __shfl_up_sync(0xffffffffu, end, 1);
           if (lane == 0) begin = 0;
@@ -444,7 +481,12 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ 
           nw = ws > 0.0 ? __ddiv_rn(sm, ws) : c;
           __syncwarp();
         }
-        nw = dedupe_lanes(lane < LUT ? nw : INFINITY, scratch[warp]);
+        // _dedupe (sort, equal neighbours to +inf, sort) is the identity on centres that are already strictly
+        // increasing with any +inf at the end, which the run-based pass produces: skip it then
+        nw = lane < LUT ? nw : INFINITY;
+        const double nx = __shfl_down_sync(0xffffffffu, nw, 1);
+        const bool ordered = lane >= LUT - 1 || nw < nx || (nw == INFINITY && nx == INFINITY);
+        if (!__all_sync(0xffffffffu, ordered)) nw = dedupe_lanes(nw, scratch[warp]);
         const bool valid = finite_d(c);
         const bool ok = lane >= LUT || (finite_d(nw) == valid &&
                                         (!valid || fabs(__dsub_rn(nw, c)) <= __dadd_rn(1e-8, __dmul_rn(1e-5, fabs(c)))));
@@ -817,14 +859,20 @@ int mxq_lut_tables(const float* P, float* T, int64_t K, int64_t n, int64_t sk, i
     tp.safe[i] = f->safe[i];
     tp.order[i] = f->order[i];
   }
+  tp.keyshift = 23 - m;
+  tp.lowmask = (1u << (23 - m)) - 1u;
+  for (int i = 0; i < KEYS; i++) tp.bin[i] = 0xFF;
+  for (int b = 0; b < f->nv; b++) tp.bin[f2u(f->grid[b]) >> tp.keyshift] = (uint8_t)b;
+  for (int b = 0; b < f->nv; b++)                          // -0 counts as the zero code (the grid holds +0)
+    if (f->grid[b] == 0.0f) tp.bin[0x80000000u >> tp.keyshift] = (uint8_t)b;
   // A cluster of cs CTAs per panel of gpc groups (32 columns, or one group when a group is wider): the CTAs split
   // the panel's rows for the histogram and its groups for the fits; cs (1..8) makes about three CTAs per SM.
   const int gpc = group >= 5 ? 1 : (32 >> group);
   const int64_t panels = (ng + gpc - 1) / gpc;
   int cs = 1;
   while (cs < 8 && panels * cs < 3 * (int64_t)sm_count() && 2 * cs <= K) cs *= 2;
-  const size_t smem = (size_t)gpc * f->nv * sizeof(int);
-  // static (~40 KB) plus the histograms can pass the 48 KB default
+  const size_t smem = (size_t)gpc * (f->nv + 1) * sizeof(int);
+  // static (~44 KB) plus the histograms can pass the 48 KB default
   if (int r = check_cuda(cudaFuncSetAttribute(k_lut_tables, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                          "lut.tables: shared memory attribute"))
     return r;
