@@ -30,6 +30,21 @@ namespace {
 
 constexpr int NO_LABEL = -4096;        // the label of a zero code: no sum of two labels reaches -16 with it
 
+// Two 16-bit signed labels per 32-bit register (labels are in [-149, 127], NO_LABEL sums to -8192): the label max
+// runs on packed 16-bit integer adds and maxima, two emulated MACs per instruction.
+__device__ __forceinline__ uint32_t add_s16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("add.s16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t max_s16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.s16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ int lo_s16(uint32_t v) { return (int)(int16_t)(v & 0xffffu); }
+__device__ __forceinline__ int hi_s16(uint32_t v) { return (int)(int16_t)(v >> 16); }
+
 struct AnchorP {
   int bits[kMaxBits];                  // level widths (the generic path's view; all equal on the fast path)
   int nbits, head, drop_rne, b;
@@ -82,11 +97,11 @@ __device__ __noinline__ float tree_generic(const float* a, int sa, const float* 
 
 // The anchor label of one output when the code labels' max is below -16: the max label of the products that are
 // nonzero after truncation and flush, or NO_LABEL when there is none.
-__device__ __noinline__ int exact_top(const float* a, int sa, const float* b, int sb, const int* la, const int* lb,
-                                      ArithP A) {
+__device__ __noinline__ int exact_top(const float* a, int sa, const float* b, int sb, const uint32_t* la,
+                                      const int16_t* lb, ArithP A) {
   int top = NO_LABEL;
   for (int u = 0; u < 16; u++)
-    if (ar_product(A, a[u * sa], b[u * sb]) != 0.0f) top = max(top, la[u * sa] + lb[u * sb]);
+    if (ar_product(A, a[u * sa], b[u * sb]) != 0.0f) top = max(top, lo_s16(la[u * sa]) + (int)lb[u * sb]);
   return top;
 }
 
@@ -98,8 +113,10 @@ __global__ void __launch_bounds__(256, 2)
   using TT = Tile<RM, RN>;
   constexpr int NT = TT::NT, BM = TT::BM, BN = TT::BN, HM = TT::HM, HN = TT::HN;
   extern __shared__ __align__(16) float smem[];
-  int* La = reinterpret_cast<int*>(smem + 2 * TT::STAGE);      // [BK][BM] labels of the current block's codes
-  int* Lb = La + BK * BM;                                        // [BK][BN]
+  // labels of the current block's codes: A's as 32-bit words holding the label twice (both 16-bit halves), B's as
+  // 16-bit values, so that two adjacent columns are one word; exact_top reads the low half of A's
+  uint32_t* La = reinterpret_cast<uint32_t*>(smem + 2 * TT::STAGE);   // [BK][BM]
+  int16_t* Lb = reinterpret_cast<int16_t*>(La + BK * BM);              // [BK][BN]
   __shared__ float red[3][NT / 32];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
@@ -142,88 +159,109 @@ __global__ void __launch_bounds__(256, 2)
     };
 
     if (domain && kcount == BK) {
-      for (int q = tid; q < BK * BM; q += NT) La[q] = code_label(As[q]);
-      for (int q = tid; q < BK * BN; q += NT) Lb[q] = code_label(Bs[q]);
+      for (int q = tid; q < BK * BM; q += NT) {
+        const uint32_t l = (uint32_t)code_label(As[q]) & 0xffffu;
+        La[q] = l | (l << 16);
+      }
+      for (int q = tid; q < BK * BN; q += NT) Lb[q] = (int16_t)code_label(Bs[q]);
       __syncthreads();
 #pragma unroll 1
       for (int grp = 0; grp < 2; grp++) {
         const float* Ak = As + grp * 16 * BM;
         const float* Bk = Bs + grp * 16 * BN;
-        const int* Lak = La + grp * 16 * BM;
-        const int* Lbk = Lb + grp * 16 * BN;
-        // pass 1: the max label over codes
-        int top[RM][RN];
+        const uint32_t* Lak = La + grp * 16 * BM;
+        const int16_t* Lbk = Lb + grp * 16 * BN;
+        // pass 1: the max label over codes, pairs of columns in 16-bit halves (column 2j low, 2j + 1 high)
+        uint32_t top2[RM][RN / 2];
+        constexpr uint32_t NONE2 = ((uint32_t)(2 * NO_LABEL) & 0xffffu) * 0x00010001u;
 #pragma unroll
         for (int i = 0; i < RM; i++)
 #pragma unroll
-          for (int j = 0; j < RN; j++) top[i][j] = 2 * NO_LABEL;
+          for (int j = 0; j < RN / 2; j++) top2[i][j] = NONE2;
 #pragma unroll 4
         for (int k = 0; k < 16; k++) {
-          int la[RM], lb[RN];
+          uint32_t la[RM], lb[RN / 2];
           lds<HM>(reinterpret_cast<float*>(la), reinterpret_cast<const float*>(Lak + k * BM + ar0));
           lds<HM>(reinterpret_cast<float*>(la + HM), reinterpret_cast<const float*>(Lak + k * BM + ar1));
-          lds<HN>(reinterpret_cast<float*>(lb), reinterpret_cast<const float*>(Lbk + k * BN + bc0));
-          lds<HN>(reinterpret_cast<float*>(lb + HN), reinterpret_cast<const float*>(Lbk + k * BN + bc1));
+          lds<HN / 2>(reinterpret_cast<float*>(lb),
+                      reinterpret_cast<const float*>(reinterpret_cast<const uint32_t*>(Lbk + k * BN) + bc0 / 2));
+          lds<HN / 2>(reinterpret_cast<float*>(lb + HN / 2),
+                      reinterpret_cast<const float*>(reinterpret_cast<const uint32_t*>(Lbk + k * BN) + bc1 / 2));
 #pragma unroll
           for (int i = 0; i < RM; i++)
 #pragma unroll
-            for (int j = 0; j < RN; j++) top[i][j] = max(top[i][j], la[i] + lb[j]);
+            for (int j = 0; j < RN / 2; j++) top2[i][j] = max_s16x2(top2[i][j], add_s16x2(la[i], lb[j]));
         }
-        // the grid of each output: 2^-G as a multiplier, 2^G to scale the sum back
-        float inv[RM][RN];
+        // the grid of each output: 2^-G as a multiplier (pairs of columns), 2^G to scale the sum back
+        F2 inv2[RM][RN / 2];
         bool flush = false;
 #pragma unroll
         for (int i = 0; i < RM; i++)
 #pragma unroll
-          for (int j = 0; j < RN; j++) {
-            int t = top[i][j];
-            if (t < -16) t = exact_top(Ak + row_of(i), BM, Bk + col_of(j), BN, Lak + row_of(i), Lbk + col_of(j), A);
-            const int G = (t == NO_LABEL ? 0 : t) + gshift;
-            inv[i][j] = u2f((uint32_t)(127 - G) << 23);
-            flush |= G < -16;
+          for (int j = 0; j < RN / 2; j++) {
+            float v[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+              int t = h ? hi_s16(top2[i][j]) : lo_s16(top2[i][j]);
+              if (t < -16)
+                t = exact_top(Ak + row_of(i), BM, Bk + col_of(2 * j + h), BN, Lak + row_of(i), Lbk + col_of(2 * j + h),
+                              A);
+              const int G = (t == NO_LABEL ? 0 : t) + gshift;
+              v[h] = u2f((uint32_t)(127 - G) << 23);
+              flush |= G < -16;
+            }
+            inv2[i][j] = pk2(v[0], v[1]);
           }
         flush = __any_sync(0xffffffffu, flush);
-        // pass 2: the terms, summed exactly in float32
-        float acc[RM][RN];
+        // pass 2: the terms, summed exactly in float32. Pairs of columns stay in 64-bit register pairs for sm_100's
+        // packed FP32 instructions (the same IEEE operations, half the issue slots); the masks act on both halves
+        // at once
+        F2 acc2[RM][RN / 2];
 #pragma unroll
         for (int i = 0; i < RM; i++)
 #pragma unroll
-          for (int j = 0; j < RN; j++) acc[i][j] = 0.0f;
+          for (int j = 0; j < RN / 2; j++) acc2[i][j] = 0ull;
 #pragma unroll 1
         for (int k = 0; k < 16; k++) {
-          float a[RM], b[RN];
+          float a[RM];
+          F2 b2[RN / 2];
           lds<HM>(a, Ak + k * BM + ar0);
           lds<HM>(a + HM, Ak + k * BM + ar1);
-          lds<HN>(b, Bk + k * BN + bc0);
-          lds<HN>(b + HN, Bk + k * BN + bc1);
+          lds<HN>(reinterpret_cast<float*>(b2), Bk + k * BN + bc0);
+          lds<HN>(reinterpret_cast<float*>(b2 + HN / 2), Bk + k * BN + bc1);
           if (flush) {
 #pragma unroll
             for (int i = 0; i < RM; i++)
 #pragma unroll
-              for (int j = 0; j < RN; j++) {
-                const float p = __fmul_rn(a[i], b[j]);
-                const float y = __fmul_rn(u2f(f2u(p) & 0xfff00000u), inv[i][j]);
-                const float c = P.drop_rne ? keep_magic : u2f((f2u(y) & 0x80000000u) | 0x4b000000u);
-                const float term = P.drop_rne ? __fsub_rn(__fadd_rn(y, c), c) : __fsub_rn(__fadd_rz(y, c), c);
-                acc[i][j] = __fadd_rn(acc[i][j], fabsf(p) >= 1.52587890625e-05f ? term : 0.0f);
+              for (int j = 0; j < RN / 2; j++) {
+                float r[2];
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                  const float bj = h ? hi2(b2[j]) : lo2(b2[j]);
+                  const float p = __fmul_rn(a[i], bj);
+                  const float y = __fmul_rn(u2f(f2u(p) & 0xfff00000u), h ? hi2(inv2[i][j]) : lo2(inv2[i][j]));
+                  const float c = P.drop_rne ? keep_magic : u2f((f2u(y) & 0x80000000u) | 0x4b000000u);
+                  const float term = P.drop_rne ? __fsub_rn(__fadd_rn(y, c), c) : __fsub_rn(__fadd_rz(y, c), c);
+                  r[h] = __fadd_rn(h ? hi2(acc2[i][j]) : lo2(acc2[i][j]),
+                                   fabsf(p) >= 1.52587890625e-05f ? term : 0.0f);
+                }
+                acc2[i][j] = pk2(r[0], r[1]);
               }
           } else {
-            // pairs of columns on the packed FP32 instructions (the same IEEE operations, fewer issue slots)
+            const F2 rne_magic = pk2(keep_magic, keep_magic);
 #pragma unroll
             for (int i = 0; i < RM; i++) {
               const F2 ai = pk2(a[i], a[i]);
 #pragma unroll
-              for (int j = 0; j < RN; j += 2) {
-                const F2 p = mul2(ai, pk2(b[j], b[j + 1]));
-                const F2 y = mul2(pk2(u2f(f2u(lo2(p)) & 0xfff00000u), u2f(f2u(hi2(p)) & 0xfff00000u)),
-                                  pk2(inv[i][j], inv[i][j + 1]));
-                const float c0 = P.drop_rne ? keep_magic : u2f((f2u(lo2(y)) & 0x80000000u) | 0x4b000000u);
-                const float c1 = P.drop_rne ? keep_magic : u2f((f2u(hi2(y)) & 0x80000000u) | 0x4b000000u);
-                const F2 c = pk2(c0, c1);
-                const F2 t = P.drop_rne ? sub2(add2(y, c), c) : sub2(addrz2(y, c), c);
-                const F2 acc2 = add2(pk2(acc[i][j], acc[i][j + 1]), t);
-                acc[i][j] = lo2(acc2);
-                acc[i][j + 1] = hi2(acc2);
+              for (int j = 0; j < RN / 2; j++) {
+                const F2 p = mul2(ai, b2[j]) & 0xfff00000fff00000ull;          // products truncated to 3 bits
+                const F2 y = mul2(p, inv2[i][j]);
+                if (P.drop_rne) {
+                  acc2[i][j] = add2(acc2[i][j], sub2(add2(y, rne_magic), rne_magic));
+                } else {
+                  const F2 c = (y & 0x8000000080000000ull) | 0x4b0000004b000000ull;   // copysign(2^23, y)
+                  acc2[i][j] = add2(acc2[i][j], sub2(addrz2(y, c), c));
+                }
               }
             }
           }
@@ -234,8 +272,8 @@ __global__ void __launch_bounds__(256, 2)
 #pragma unroll
           for (int j = 0; j < RN / 2; j++) {
             // 2^G from 2^-G: the biased exponents add up to 254
-            const float s0 = __fmul_rn(acc[i][2 * j], u2f(0x7f000000u - f2u(inv[i][2 * j])));
-            const float s1 = __fmul_rn(acc[i][2 * j + 1], u2f(0x7f000000u - f2u(inv[i][2 * j + 1])));
+            const float s0 = __fmul_rn(lo2(acc2[i][j]), u2f(0x7f000000u - f2u(lo2(inv2[i][j]))));
+            const float s1 = __fmul_rn(hi2(acc2[i][j]), u2f(0x7f000000u - f2u(hi2(inv2[i][j]))));
             const uint32_t c = bf16x2_rne(s0, s1);                 // S4: the tree's bf16 lane
             const uint32_t t = bf16x2_rne(__fmul_rn(unpack_hi(c), __fmul_rn(xa(i), xb(2 * j))),
                                           __fmul_rn(unpack_lo(c), __fmul_rn(xa(i), xb(2 * j + 1))));
