@@ -579,6 +579,35 @@ def leg_sharded(R, args, quant, runs):
         "GB/s": round(BYTES_PER_ELEM * ROWS * COLS * len(runs) / (t_all * 1e-3) / 1e9, 1),
         "ms_per_step": round(t_all, 3), "compute_ms": round(t_cmp, 3), "gather_ms": round(t_all - t_cmp, 3),
         "gather_bytes_received_per_rank": int(gbytes), "parity_vs_one_gpu": ok}
+    # the same sweep with the gather fused into the quantizer: each rank's kernel writes its slice of P and X into
+    # every rank's symmetric buffers over NVLink (no NCCL); one group barrier per step
+    if R.world > 1:
+        targets = {}
+        for ax in (0, 1):
+            xshape = [ROWS, COLS]
+            xshape[ax] //= 32
+            targets[ax] = shard.GatherTarget((ROWS, COLS), xshape, R.dev)
+
+        def fused_sweep():
+            for f, fmt, ax in runs:
+                shard.quantize_gathered(quant[f], V, fmt, axis=ax, target=targets[ax], sync=False)
+            targets[0].barrier()
+
+        t_fused = R.timed(fused_sweep, steps)
+        ok = True
+        for f, fmt, ax in runs:                               # parity: every rank writes, rank 0 checks
+            P, X = shard.quantize_gathered(quant[f], V, fmt, axis=ax, target=targets[ax])
+            if R.rank == 0:
+                Pw, Xw = quant[f](V, fmt, axis=ax)
+                ok &= same_bits(P, Pw) and same_bits(X, Xw)
+            targets[ax].barrier()                             # no rank writes the next run before rank 0 has read
+        ok = R.all(ok)
+        out["config 2: sweep, rows split, gather fused into the quantizer (NVLink stores)"] = {
+            "GB/s": round(BYTES_PER_ELEM * ROWS * COLS * len(runs) / (t_fused * 1e-3) / 1e9, 1),
+            "ms_per_step": round(t_fused, 3), "compute_ms (NCCL leg, gather=False)": round(t_cmp, 3),
+            "nvlink_bytes_sent_per_rank": int(gbytes), "parity_vs_one_gpu": ok,
+            "nvlink_roofline_ms": round(gbytes / 770e9 * 1e3, 3)}
+        del targets
     del V
 
     # config 3: the 4096^3 systolic GEMM (MXGEMMINI / HW_FINAL), column panels of B

@@ -131,6 +131,14 @@ int mxq_block_quantize(const float* V, float* P, float* X, int64_t outer, int64_
 int mxq_block_quantize_packed(const float* V, uint8_t* codes, uint8_t* scales, int64_t outer, int64_t len,
                               int64_t inner, int64_t block, const mxq_quant_spec* spec, int32_t* status,
                               void* stream);
+/* No reference counterpart: mxq_block_quantize writing its codes and scales to ndst (1..8) destinations at once,
+ * P[i] / X[i] each a DEVICE pointer to a [outer, len, inner] / [outer, ceil(len/block), inner] buffer (a HOST array
+ * of ndst pointers). With peer mappings of the other ranks' buffers (CUDA IPC or symmetric memory over NVLink) the
+ * quantizer of a rank's slice of rows is also the all-gather of its outputs: mxq/shard.py quantize_gathered. The
+ * caller orders the ranks' writes before anyone reads (a barrier after the call). Blocks of 32; the TMA kernel's
+ * layouts (rows a multiple of 4 elements, 16-byte aligned V and destinations); MXQ_ERR_UNSUPPORTED otherwise. */
+int mxq_block_quantize_multi(const float* V, float* const* P, float* const* X, int32_t ndst, int64_t outer,
+                             int64_t len, int64_t inner, int64_t block, const mxq_quant_spec* spec, void* stream);
 /* No reference counterpart: float32 codes and scales from the compact form (n_codes elements, n_scales scales) */
 int mxq_unpack(const uint8_t* codes, const uint8_t* scales, float* P, float* X, int64_t n_codes, int64_t n_scales,
                int32_t e, int32_t m, void* stream);

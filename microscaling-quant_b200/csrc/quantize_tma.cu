@@ -140,6 +140,30 @@ struct OutF {
   __device__ __forceinline__ void lost() {}                // the tile's NaN codes and scales say it
 };
 
+// The float32 outputs written to up to kMaxDst destinations at once: this GPU's buffers and, through peer (NVLink)
+// mappings, the same slice of every other rank's buffers, so the quantizer is also the all-gather of its outputs.
+// Destination 0 takes streaming stores; the others plain stores (remote writes over NVLink).
+constexpr int kMaxDst = 8;
+struct OutMulti {
+  float* P[kMaxDst];
+  float* X[kMaxDst];
+  int n;
+  template <bool FINITE = false>
+  __device__ __forceinline__ void codes(int64_t idx, float4 v) {
+    __stcs(reinterpret_cast<float4*>(P[0] + idx), v);
+#pragma unroll
+    for (int d = 1; d < kMaxDst; d++)
+      if (d < n) *reinterpret_cast<float4*>(P[d] + idx) = v;
+  }
+  __device__ __forceinline__ void scale(int64_t idx, float x) {
+#pragma unroll
+    for (int d = 0; d < kMaxDst; d++)
+      if (d < n) X[d][idx] = x;
+  }
+  __device__ __forceinline__ void finish() {}
+  __device__ __forceinline__ void lost() {}                // the tile's NaN codes and scales say it
+};
+
 // an OCP element code's bit pattern (sign at bit E + M); `bad` set for what the format lacks (Inf, and NaN in FP6 /
 // FP4; E4M3 keeps NaN as S.1111.111, E5M2 Inf as S.11111.00 and NaN as S.11111.11)
 template <int E, int M>
@@ -483,19 +507,22 @@ int launch(const CUtensorMap& map, bool cols, Out out, int64_t outer, int64_t le
   return MXQ_LAUNCH_CHECK("block_quantize");
 }
 
-// the float32 outputs (packed == nullptr) or the compact ones
+// the float32 outputs (packed == nullptr) or the compact ones, or (multi != nullptr) float32 outputs to several
+// destinations
 struct Dest {
   float* P;
   float* X;
   uint8_t* Pc;
   uint8_t* Xc;
   int* status;
+  const OutMulti* multi = nullptr;
 };
 
 // block: 32 for every layout and output; 16 or 64 for ROWS with float outputs (the launcher checks)
 template <int FAM, int E, int M>
 int launch_dest(const CUtensorMap& map, bool cols, const Dest& d, int64_t outer, int64_t len, int64_t inner,
                 int64_t block, const TParams& prm, cudaStream_t st) {
+  if (d.multi != nullptr) return launch<FAM, E, M, 32>(map, cols, *d.multi, outer, len, inner, prm, st);
   if (d.Pc == nullptr) {
     const OutF o{d.P, d.X};
     if (block == 16) return launch<FAM, E, M, 16>(map, cols, o, outer, len, inner, prm, st);
@@ -532,7 +559,12 @@ int quantize_tma_dest(const float* V, const Dest& d, int64_t outer, int64_t len,
   const bool other = d.Pc == nullptr && (block == 16 || (block == 64 && !cols));
   if ((block != 32 && !other) || s.family == MXQ_FAMILY_FP32) return MXQ_ERR_UNSUPPORTED;
   const int64_t rowlen = cols ? inner : len;
-  const uintptr_t out_base = d.Pc ? (uintptr_t)d.Pc : (uintptr_t)d.P;
+  uintptr_t out_base = d.Pc ? (uintptr_t)d.Pc : (uintptr_t)d.P;
+  if (d.multi != nullptr) {
+    if (block != 32) return MXQ_ERR_UNSUPPORTED;
+    out_base = 0;
+    for (int i = 0; i < d.multi->n; i++) out_base |= (uintptr_t)d.multi->P[i];   // every destination 16-byte aligned
+  }
   if ((uintptr_t)V % 16 || out_base % 16 || rowlen % 4 || outer >= (1ll << 31) || len >= (1ll << 31) ||
       inner >= (1ll << 31))
     return MXQ_ERR_UNSUPPORTED;
@@ -571,6 +603,29 @@ int quantize_tma_packed(const float* V, uint8_t* Pc, uint8_t* Xc, int* status, i
 }
 
 }  // namespace mxq
+
+extern "C" int mxq_block_quantize_multi(const float* V, float* const* P, float* const* X, int32_t ndst,
+                                        int64_t outer, int64_t len, int64_t inner, int64_t block,
+                                        const mxq_quant_spec* spec, void* stream) {
+  MXQ_REQUIRE(spec != nullptr && P != nullptr && X != nullptr, MXQ_ERR_VALUE, "block_quantize_multi: null argument");
+  MXQ_REQUIRE(ndst >= 1 && ndst <= kMaxDst, MXQ_ERR_VALUE, "block_quantize_multi: %d destinations (1..%d)", ndst,
+              kMaxDst);
+  MXQ_REQUIRE(outer >= 0 && len >= 0 && inner >= 0, MXQ_ERR_VALUE, "block_quantize_multi: bad layout");
+  MXQ_REQUIRE(spec->family != MXQ_FAMILY_FP32, MXQ_ERR_VALUE, "block_quantize_multi: format FP32 has no kernel");
+  if (outer * len * inner == 0) return MXQ_OK;
+  OutMulti o{};
+  o.n = ndst;
+  for (int i = 0; i < ndst; i++) {
+    MXQ_REQUIRE(P[i] != nullptr && X[i] != nullptr, MXQ_ERR_VALUE, "block_quantize_multi: destination %d is null", i);
+    o.P[i] = P[i];
+    o.X[i] = X[i];
+  }
+  Dest d{nullptr, nullptr, nullptr, nullptr, nullptr, &o};
+  const int r = mxq::quantize_tma_dest(V, d, outer, len, inner, block, *spec, mxq::as_stream(stream));
+  MXQ_REQUIRE(r != MXQ_ERR_UNSUPPORTED, MXQ_ERR_UNSUPPORTED,
+              "block_quantize_multi: blocks of 32, rows (the innermost extent) a multiple of 4, 16-byte aligned buffers");
+  return r;
+}
 
 // Test-only: block.mxgemmini MXFP8_E4M3 along the rows of a rows x cols V through the TMA kernel with its loads never
 // issued and waits of `wait_rounds` rounds, so every tile's wait runs out (nothing is in flight when the CTAs

@@ -65,6 +65,7 @@ _SIGS = {
     "mxq_arith_tile_add": [P, P, P, I64, ctypes.POINTER(MxqArith), P],
     "mxq_block_quantize": [P, P, P, I64, I64, I64, I64, ctypes.POINTER(MxqQuantSpec), P],
     "mxq_block_quantize_packed": [P, P, P, I64, I64, I64, I64, ctypes.POINTER(MxqQuantSpec), P, P],
+    "mxq_block_quantize_multi": [P, P, P, I32, I64, I64, I64, I64, ctypes.POINTER(MxqQuantSpec), P],
     "mxq_unpack": [P, P, P, P, I64, I64, I32, I32, P],
     "mxq_dequantize_packed": [P, P, P, I64, I64, I64, I64, I32, I32, P],
     "mxq_block_amax": [P, P, I64, I64, I64, I64, P],

@@ -22,7 +22,7 @@ import torch.distributed as dist
 
 from .block._driver import _layout
 
-__all__ = ["world", "split", "quantize", "reduce", "lut_tables", "rows"]
+__all__ = ["world", "split", "quantize", "reduce", "lut_tables", "rows", "GatherTarget", "quantize_gathered"]
 
 
 def world(process_group=None) -> Tuple[int, int]:
@@ -83,6 +83,75 @@ def quantize(quantizer: Callable, V: torch.Tensor, fmt, axis: int = 0, block_siz
     xshape = list(V.shape)
     xshape[axis_] = nb
     return P.reshape(V.shape), X.reshape(xshape)
+
+
+class GatherTarget:
+    """Output buffers for quantize_gathered: P and X of the whole problem on every rank, in symmetric memory (each
+    rank's buffers mapped into every other rank's address space over NVLink). Built collectively (every rank of the
+    group, the same shapes); reused by every call with those shapes. A call overwrites them."""
+
+    def __init__(self, shape, xshape, device, process_group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        group = process_group or dist.group.WORLD
+        self.shape, self.xshape, self.device = tuple(shape), tuple(xshape), torch.device(device)
+        self.P = symm_mem.empty(self.shape, dtype=torch.float32, device=self.device)
+        self.X = symm_mem.empty(self.xshape, dtype=torch.float32, device=self.device)
+        self._hp = symm_mem.rendezvous(self.P, group)
+        self._hx = symm_mem.rendezvous(self.X, group)
+        self.group = group
+        self.rank, self.size = dist.get_rank(group), dist.get_world_size(group)
+        # every rank's buffers as this process sees them (this rank's first), byte addresses
+        order = [self.rank] + [r for r in range(self.size) if r != self.rank]
+        self.p_ptrs = [int(self._hp.buffer_ptrs[r]) for r in order]
+        self.x_ptrs = [int(self._hx.buffer_ptrs[r]) for r in order]
+
+    def barrier(self):
+        """Every rank's writes into every rank's buffers are complete and visible: a barrier of the group, which
+        (NCCL) waits on each rank's earlier work on its current stream; bounded by the group's timeout."""
+        dist.barrier(group=self.group)
+
+
+def quantize_gathered(quantizer: Callable, V: torch.Tensor, fmt, axis: int = 0, block_size: int = 32, *,
+                      target: GatherTarget, sync: bool = True, **kw):
+    """quantize with V's rows split across the ranks, each rank's kernel writing its slice of P and X straight into
+    every rank's `target` buffers over NVLink: the quantizer is the all-gather, no separate collective (no reference
+    counterpart; quantize() does the same with an NCCL all-gather). `quantizer` is block.mxquant / mxgemmini / ocp's
+    quantize and `kw` its options; blocks of 32 and the TMA kernel's layouts. Returns (target.P, target.X) after a
+    barrier of the group; with sync=False the caller calls target.barrier() before any rank reads them (several
+    calls can then share one barrier)."""
+    import ctypes
+    from . import _lib
+    from .block import mxgemmini, mxquant, ocp
+    module = {mxquant.quantize: mxquant, mxgemmini.quantize: mxgemmini, ocp.quantize: ocp}.get(quantizer)
+    if module is None:
+        raise ValueError("quantize_gathered: the quantizer must be block.mxquant, block.mxgemmini or block.ocp's "
+                         "quantize")
+    axis_, outer, L, inner, nb = _layout(V, axis, block_size)
+    xshape = list(V.shape)
+    xshape[axis_] = nb
+    if target.shape != tuple(V.shape) or target.xshape != tuple(xshape):
+        raise ValueError(f"quantize_gathered: target holds {target.shape} / {target.xshape}, the call needs "
+                         f"{tuple(V.shape)} / {tuple(xshape)}")
+    rank, size = target.rank, target.size
+    spec = module.spec(fmt, **kw)
+    v = V.contiguous()
+    if outer > 1:                                   # whole outer slices
+        o0, o1, _ = split(outer, size, rank)
+        lay = (o1 - o0, L, inner)
+        v_off, p_off, x_off = o0 * L * inner, o0 * L * inner, o0 * nb * inner
+    else:                                           # whole blocks along len
+        r0, r1, _ = split(L, size, rank, block_size)
+        lay = (1, r1 - r0, inner)
+        v_off, p_off, x_off = r0 * inner, r0 * inner, (r0 // block_size) * inner
+    if lay[0] * lay[1] * lay[2] > 0:
+        n = len(target.p_ptrs)
+        ps = (ctypes.c_void_p * n)(*[p + 4 * p_off for p in target.p_ptrs])
+        xs = (ctypes.c_void_p * n)(*[x + 4 * x_off for x in target.x_ptrs])
+        _lib.run("mxq_block_quantize_multi", v.device, ctypes.c_void_p(v.data_ptr() + 4 * v_off), ps, xs, n,
+                 *lay, block_size, ctypes.byref(spec))
+    if sync:
+        target.barrier()
+    return target.P, target.X
 
 
 def _run_quant(quantizer, Vl, fmt, axis, block_size, pshape, xshape, V, kw):

@@ -1,7 +1,8 @@
 """mxq.shard on real GPUs with NCCL (skipped with fewer than two devices): one process per GPU, each computing its
 slice of config-2, config-3 and config-4 style problems on its own device, the slices reassembled by NCCL
-all_gather_into_tensor; every rank checks the gathered result bit for bit against the same problem computed whole
-on its own GPU. Run on 2 GPUs (and on more when they are there, up to 4)."""
+all_gather_into_tensor -- and, for the quantizers, by the fused form, whose kernel writes each rank's slice into every
+rank's symmetric buffers over NVLink; every rank checks the gathered result bit for bit against the same problem
+computed whole on its own GPU. Run on 2 GPUs (and on more when they are there, up to 4)."""
 import os
 import socket
 
@@ -60,6 +61,19 @@ def _rank_main(rank, size, port, errors):
             T = shard.lut_tables(lut.tables, PL, "MXFP6_E3M2", group=G, max_iters=20)
             if not _same(T, lut.tables(PL, "MXFP6_E3M2", group=G, max_iters=20)):
                 bad.append(f"lut.tables G={G}")
+        # the fused form: each rank's quantizer writes its slice into every rank's symmetric buffers over NVLink
+        for f, q in (("mxgemmini", block.mxgemmini.quantize), ("mxquant", block.mxquant.quantize),
+                     ("ocp", block.ocp.quantize)):
+            for ax in (0, 1):
+                xshape = list(V.shape)
+                xshape[ax] = -(-V.shape[ax] // 32)
+                target = shard.GatherTarget(V.shape, xshape, dev)
+                for call in range(2):                        # the target is reused
+                    P, X = shard.quantize_gathered(q, V, "MXFP8_E4M3", axis=ax, target=target)
+                    Pw, Xw = q(V, "MXFP8_E4M3", axis=ax)
+                    if not (_same(P, Pw) and _same(X, Xw)):
+                        bad.append(f"quantize_gathered {f} axis {ax} call {call}")
+                del target
         R = shard.rows(lambda x: x * 3.0 - 1.0, torch.arange(45, dtype=torch.float32, device=dev).reshape(9, 5))
         if not _same(R, torch.arange(45, dtype=torch.float32, device=dev).reshape(9, 5) * 3.0 - 1.0):
             bad.append("rows")
