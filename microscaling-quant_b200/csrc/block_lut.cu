@@ -22,6 +22,20 @@ int64_t round_up(int64_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 bool lut_format(int e, int m) { return (e == 3 && m == 2) || (e == 2 && m == 3) || (e == 5 && m == 2) || (e == 4 && m == 3); }
 
 constexpr int kMaxDevices = 64;
+
+}  // namespace
+
+namespace mxq {
+int quantize_tma_codes(const float* V, uint8_t* codes, float* X, int* status, int64_t outer, int64_t len,
+                       int64_t inner, const mxq_quant_spec& s, cudaStream_t st);
+int lut_tables_codes_map(const uint8_t* codes, float* T, float* cmap, int64_t K, int64_t n, int32_t group,
+                         int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream);
+size_t lut_code_lookup_smem(int64_t n, int32_t group, int32_t e, int32_t m);
+int lut_code_lookup(const uint8_t* codes, const float* cmap, float* out, int64_t K, int64_t n, int32_t group,
+                    int32_t e, int32_t m, void* stream);
+}  // namespace mxq
+
+namespace {
 std::mutex g_scratch_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
 
@@ -69,6 +83,31 @@ int mxq_block_lut_quantize(const float* V, float* P_lut, float* X, int64_t rows,
               "block.lut: the workspace needs %lld bytes, 256-byte aligned (got %lld)", (long long)need,
               (long long)workspace_bytes);
   const bool ax0 = axis % 2 == 0;
+  // Axis 0 (the K x n operand is V's own row-major layout): the codes as bytes (their OCP bit patterns) from the fused
+  // quantizer, the tables and each group's code -> entry map from the bytes, then one map read per element. The
+  // workspace holds the bytes, the tables and the maps (less than the float codes of the general path below).
+  if (ax0 && rows * cols > 0 && mxq::lut_code_lookup_smem(cols, group, spec->e, spec->m) > 0 &&
+      (uintptr_t)V % 16 == 0 && (uintptr_t)P_lut % 16 == 0) {
+    const int64_t ng = (cols + ((int64_t)1 << group) - 1) >> group;
+    const int64_t nc = (int64_t)1 << (1 + spec->e + spec->m);
+    uint8_t* codes = static_cast<uint8_t*>(workspace);
+    float* Tb = reinterpret_cast<float*>(codes + round_up(rows * cols));
+    float* cmap = Tb + round_up(ng * kTableWidth * (int64_t)sizeof(float)) / (int64_t)sizeof(float);
+    const int64_t used = round_up(rows * cols) + round_up(ng * kTableWidth * (int64_t)sizeof(float)) +
+                         ng * nc * (int64_t)sizeof(float);
+    cudaStream_t st = as_stream(stream);
+    if (used <= workspace_bytes) {
+      if (int r = check_cuda(cudaMemsetAsync(status, 0, sizeof(int32_t), st), "block.lut")) return r;
+      const int q = mxq::quantize_tma_codes(V, codes, X, status, 1, rows, cols, *spec, st);
+      if (q != MXQ_ERR_UNSUPPORTED) {
+        if (q) return q;
+        if (int r = mxq::lut_tables_codes_map(codes, Tb, cmap, rows, cols, group, max_iters, spec->e, spec->m, status,
+                                              stream))
+          return r;
+        return mxq::lut_code_lookup(codes, cmap, P_lut, rows, cols, group, spec->e, spec->m, stream);
+      }
+    }
+  }
   float* P = static_cast<float*>(workspace);
   float* T = reinterpret_cast<float*>(static_cast<char*>(workspace) + round_up(rows * cols * (int64_t)sizeof(float)));
   // the codes: V viewed as [outer, len, inner] with blocks along `axis`

@@ -12,6 +12,8 @@
 // lanes (k_lut_tables). Every sum is exact (integer counts, codes times counts), so no summation order changes a
 // bit.
 #include <cooperative_groups.h>
+#include <type_traits>
+#include <cmath>
 #include <algorithm>
 #include <mutex>
 #include <vector>
@@ -166,6 +168,9 @@ struct TableParams {                           // by value: what the tables kern
   float safe[MAXV];
   uint8_t order[MAXV];
   uint8_t bin[KEYS];                           // key -> grid rank, 0xFF for a pattern that is no code
+  uint8_t cbin[MAXV];                          // code (its OCP bit pattern) -> grid rank, 0xFF for NaN / Inf
+  int ncodes;
+  float vals[MAXV];                            // every code's value (for the code -> entry map of block.lut)
 };
 
 constexpr int NW = NT / 32;                    // warps per CTA
@@ -223,12 +228,14 @@ __device__ __forceinline__ double dedupe_lanes(double v, double* scratch) {
 // are differences of the prefix sums. That equals the reference's argmin over all 16 centres whenever consecutive
 // centres are at least 2^-33 apart (distances below 2^17 then never round to a tie across a centre); a pass that
 // finds two closer centres assigns code by code instead.
-__global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ P, int64_t K, int64_t n, int64_t sk,
+template <typename TIn>                                     // float codes, or uint8_t OCP bit patterns (block.lut)
+__global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P, int64_t K, int64_t n, int64_t sk,
                                                    int64_t sj, int G, int gpc, int max_iters,
                                                    const __grid_constant__ TableParams tp, float* __restrict__ T,
-                                                   int* __restrict__ status) {
-  extern __shared__ int counts[];                           // [gpc][nv + 1]: this CTA's rows; then merged, own groups
-  __shared__ double pw[NW][MAXV + 1], pwx[NW][MAXV + 1];     // prefix: counts, counts x values
+                                                   int* __restrict__ status, float* __restrict__ cmap) {
+  // dynamic shared memory: counts [gpc][nv | 1] (this CTA's rows; then merged, its own groups), then the fits'
+  // prefix sums [2][NW][MAXV + 1] doubles
+  extern __shared__ int counts[];
   __shared__ double scratch[NW][LUT], fsum[NW][LUT], fw[NW][LUT];
   __shared__ float sgrid[MAXV];
   __shared__ unsigned char member[NW][MAXV];
@@ -245,11 +252,19 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ 
   const int64_t kper = (K + cs - 1) / cs;                    // this CTA's rows of the panel
   const int64_t kbeg = (int64_t)rank * kper < K ? (int64_t)rank * kper : K;
   const int64_t kend = kbeg + kper < K ? kbeg + kper : K;
-  const int nvp = nv + 1;                                   // a group's histogram row, padded: rows start on distinct banks
+  const int nvp = nv | 1;                                   // a group's histogram row, odd: a bin of 32 groups hits 32 banks
+  double* const pw = reinterpret_cast<double*>(counts + ((gpc * nvp + 1) & ~1));   // [NW][MAXV + 1]
+  double* const pwx = pw + NW * (MAXV + 1);
   for (int i = tid; i < gpc * nvp; i += NT) counts[i] = 0;
   for (int i = tid; i < nv; i += NT) sgrid[i] = tp.grid[i];
-  for (int i = tid; i < KEYS / 4; i += NT)
-    reinterpret_cast<uint32_t*>(sbin)[i] = reinterpret_cast<const uint32_t*>(tp.bin)[i];
+  constexpr bool BYTES = sizeof(TIn) == 1;
+  if (BYTES) {                                              // a code byte's grid rank (0xFF: NaN / Inf)
+    for (int i = tid; i < MAXV / 4; i += NT)
+      reinterpret_cast<uint32_t*>(sbin)[i] = reinterpret_cast<const uint32_t*>(tp.cbin)[i];
+  } else {
+    for (int i = tid; i < KEYS / 4; i += NT)
+      reinterpret_cast<uint32_t*>(sbin)[i] = reinterpret_cast<const uint32_t*>(tp.bin)[i];
+  }
   if (tid == 0) bad = 0;
   __syncthreads();
 
@@ -259,41 +274,53 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ 
   const bool kfast = sk == 1;
   bool mybad = false;
   constexpr int BATCH = 8;                                  // loads in flight per thread
+  constexpr int PBATCH = 8;                                 // the pair path's
   // a code's grid rank from its bit pattern: the key (sign, exponent, top m fraction bits) through the table; any
   // other fraction bit set, or a key that names no code (NaN, Inf, off-grid), is not a code
-  auto count = [&](float v, int gc) {
-    const uint32_t u = f2u(v), b = sbin[u >> tp.keyshift];
-    if ((u & tp.lowmask) != 0u || b == 0xFFu) mybad = true;
+  // (code bytes: the byte's rank through its own table)
+  auto count = [&](TIn v, int gc) {
+    uint32_t b;
+    bool ok;
+    if constexpr (BYTES) {
+      b = sbin[(uint32_t)v];
+      ok = b != 0xFFu;
+    } else {
+      const uint32_t u = f2u(v);
+      b = sbin[u >> tp.keyshift];
+      ok = (u & tp.lowmask) == 0u && b != 0xFFu;
+    }
+    if (!ok) mybad = true;
     else atomicAdd(&counts[gc * nvp + (int)b], 1);
   };
-  if (sj == 1 && W <= 32 && W % 2 == 0 && sk % 2 == 0 && ((uintptr_t)P + j0 * 4) % 8 == 0) {
+  using V2 = typename std::conditional<BYTES, uchar2, float2>::type;
+  if (sj == 1 && W <= 32 && W % 2 == 0 && sk % 2 == 0 && ((uintptr_t)(P + j0)) % (2 * sizeof(TIn)) == 0) {
     // a panel of at most 32 columns as float2 pairs: lane l takes the pair of columns 2 (l % 16), 2 (l % 16) + 1 of
     // row (l / 16) of its warp's two rows, so a warp instruction's 32 lanes count into (at G = 1) 16 different
     // groups' rows and the 16-byte-per-lane-pair row segments are read whole; the CTA steps 2 x 8 rows
     const int c2 = lane & 15, ro = lane >> 4;
     if (2 * c2 < W) {
-      const float2* src = reinterpret_cast<const float2*>(P + j0) + c2;
+      const V2* src = reinterpret_cast<const V2*>(P + j0) + c2;
       const int ga = (2 * c2) >> G, gb = (2 * c2 + 1) >> G;
       const int64_t step = 2 * NW;
-      for (int64_t k0 = kbeg + 2 * warp + ro; k0 < kend; k0 += step * BATCH) {
-        float2 v[BATCH];
+      for (int64_t k0 = kbeg + 2 * warp + ro; k0 < kend; k0 += step * PBATCH) {
+        V2 v[PBATCH];
 #pragma unroll
-        for (int u = 0; u < BATCH; u++)
-          v[u] = k0 + (int64_t)u * step < kend ? src[(k0 + (int64_t)u * step) * (sk / 2)] : make_float2(0.0f, 0.0f);
+        for (int u = 0; u < PBATCH; u++)
+          v[u] = k0 + (int64_t)u * step < kend ? src[(k0 + (int64_t)u * step) * (sk / 2)] : V2{};
 #pragma unroll
-        for (int u = 0; u < BATCH; u++) {
+        for (int u = 0; u < PBATCH; u++) {
           if (k0 + (int64_t)u * step >= kend) break;
           count(v[u].x, ga);
           count(v[u].y, gb);
         }
       }
     }
-  } else if (sj == 1 && W % 4 == 0 && W <= 4 * NT && sk % 4 == 0 && ((uintptr_t)P + j0 * 4) % 16 == 0) {
+  } else if (!BYTES && sj == 1 && W % 4 == 0 && W <= 4 * NT && sk % 4 == 0 && ((uintptr_t)(P + j0)) % 16 == 0) {
     // rows of the panel as float4: thread (row r, quad q) of rows_per_pass rows at a time, pointers advanced by
     // whole rows (no index arithmetic per element)
     const int qpr = (int)(W / 4), rows_per_pass = NT / qpr, r = tid / qpr, q = tid - r * qpr;
     if (r < rows_per_pass) {
-      const float4* src = reinterpret_cast<const float4*>(P + j0) + q;
+      const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(P) + j0) + q;
       int gc[4];
 #pragma unroll
       for (int i = 0; i < 4; i++) gc[i] = (4 * q + i) >> G;
@@ -319,14 +346,14 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ 
   const int64_t R = kfast ? Kc : W, dmaj = NT / R, dmin = NT % R;
   int64_t maj = tid / R, mnr = tid % R;
   for (int64_t e0 = tid; e0 < total; e0 += (int64_t)NT * BATCH) {
-    float v[BATCH];
+    TIn v[BATCH];
     int gcol[BATCH];
 #pragma unroll
     for (int u = 0; u < BATCH; u++) {
       const int64_t e = e0 + (int64_t)u * NT;
       const int64_t k = kfast ? mnr : maj, jj = kfast ? maj : mnr;
       gcol[u] = e < total ? (int)(jj >> G) : -1;
-      v[u] = e < total ? P[(kbeg + k) * sk + (j0 + jj) * sj] : 0.0f;
+      v[u] = e < total ? P[(kbeg + k) * sk + (j0 + jj) * sj] : TIn{};
       maj += dmaj;
       mnr += dmin;
       if (mnr >= R) {
@@ -361,8 +388,8 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ 
     const int64_t g = g0 + gl;
     if (g >= ng) break;
     const int* cnt = counts + gl * nvp;
-    double* PW = pw[warp];
-    double* PWX = pwx[warp];
+    double* PW = pw + warp * (MAXV + 1);
+    double* PWX = pwx + warp * (MAXV + 1);
     // 2. prefix sums over the sorted codes, and the number of distinct codes present
     double runw = 0.0, runx = 0.0;
     int npres = 0;
@@ -540,6 +567,23 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const float* __restrict__ 
     }
     if (lane >= base && lane < LUT) T[g * LUT + lane] = INFINITY;
     __syncwarp();
+    if (cmap != nullptr) {
+      // block.lut: the entry pick(P, T) chooses for each code's value (nearest of the two sorted entries around it,
+      // ties to the lower index), so that the lookup of an element is one read
+      const float* t = T + g * LUT;
+      for (int c = lane; c < tp.ncodes; c += 32) {
+        const float v = tp.vals[c];
+        int b = 0;
+        b += t[b + 7] < v ? 8 : 0;
+        b += t[b + 3] < v ? 4 : 0;
+        b += t[b + 1] < v ? 2 : 0;
+        b += t[b] < v ? 1 : 0;
+        const int lb = b + (b == LUT - 1 && t[LUT - 1] < v ? 1 : 0);
+        const int lo = lb < 1 ? 0 : (lb > LUT - 1 ? LUT - 2 : lb - 1);
+        const float rl = t[lo], rh = t[lo + 1];
+        cmap[g * tp.ncodes + c] = abs_f(__fsub_rn(v, rl)) <= abs_f(__fsub_rn(rh, v)) ? rl : rh;
+      }
+    }
   }
 }
 
@@ -785,6 +829,46 @@ __global__ void __launch_bounds__(CT) k_lut_finder_cols(const int64_t* __restric
   }
 }
 
+// block.lut's last step from code bytes: lookup(pick(P, T), T) of each element through the code -> entry map that
+// the tables kernel wrote per group (cmap, groups x ncodes), so an element is one shared-memory read. A CTA owns a
+// panel of PWL = 128 columns (lane l of every warp takes columns 4l .. 4l + 3 as one 4-byte load and one float4
+// store), stages its groups' maps, and takes a slice of rows, its 8 warps taking the rows in turn.
+constexpr int PWL = 128;
+__global__ void __launch_bounds__(CT) k_lut_code_lookup(const uint8_t* __restrict__ codes, const float* __restrict__ cmap,
+                                                        float* __restrict__ out, int64_t K, int64_t n, int G, int nc,
+                                                        int64_t rows) {
+  extern __shared__ float smap[];                            // [groups of the panel][ncodes]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t jp = (int64_t)blockIdx.x * PWL;
+  const int64_t gfirst = jp >> G, glast = ((jp + PWL < n ? jp + PWL : n) - 1) >> G;
+  const int ngp = (int)(glast - gfirst + 1);
+  for (int i = threadIdx.x; i < ngp * nc; i += CT) smap[i] = __ldg(cmap + gfirst * nc + i);
+  __syncthreads();
+  const int64_t j = jp + 4 * lane;
+  if (j >= n) return;
+  int gofs[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) gofs[i] = (int)(((j + i) >> G) - gfirst) * nc;
+  const int64_t k0 = (int64_t)blockIdx.y * rows, k1 = k0 + rows < K ? k0 + rows : K;
+  constexpr int BATCH = 8;
+  for (int64_t kb = k0 + warp; kb < k1; kb += (int64_t)CW * BATCH) {
+    uint32_t c[BATCH];
+#pragma unroll
+    for (int u = 0; u < BATCH; u++) {
+      const int64_t k = kb + (int64_t)u * CW;
+      c[u] = k < k1 ? __ldcs(reinterpret_cast<const unsigned int*>(codes + k * n + j)) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < BATCH; u++) {
+      const int64_t k = kb + (int64_t)u * CW;
+      if (k >= k1) break;
+      const float4 r = make_float4(smap[gofs[0] + (int)(c[u] & 0xffu)], smap[gofs[1] + (int)((c[u] >> 8) & 0xffu)],
+                                   smap[gofs[2] + (int)((c[u] >> 16) & 0xffu)], smap[gofs[3] + (int)(c[u] >> 24)]);
+      __stcs(reinterpret_cast<float4*>(out + k * n + j), r);
+    }
+  }
+}
+
 // the column kernels' grid: panels of `width` columns, and row slices so that about per_sm CTAs per SM are launched
 dim3 cols_grid(int64_t K, int64_t n, int64_t width, int per_sm, int64_t* rows) {
   const int64_t panels = (n + width - 1) / width;
@@ -804,40 +888,10 @@ int fmt_slot_check(int e, int m, const char* what) {
   return MXQ_OK;
 }
 
-CodeTables code_tables(const FormatTables* f) {
-  CodeTables ct;
-  ct.ncodes = f->ncodes;
-  ct.nenc = f->nenc;
-  for (int i = 0; i < f->ncodes; i++) {
-    ct.vals[i] = f->vals[i];
-    ct.fx[i] = f->fx[i];
-  }
-  for (int i = 0; i < f->nenc; i++) {
-    ct.enc_bits[i] = f->enc_bits[i];
-    ct.enc_code[i] = f->enc_code[i];
-  }
-  return ct;
-}
-
-}  // namespace
-
-extern "C" {
-
-int mxq_lut_format_tables(int32_t e, int32_t m, float* vals, int64_t* fx, float* safe, int32_t* nsafe) {
-  if (int r = fmt_slot_check(e, m, "format_tables")) return r;
-  const FormatTables* f = format_tables(e, m);
-  if (vals)
-    for (int i = 0; i < f->ncodes; i++) vals[i] = f->vals[i];
-  if (fx)
-    for (int i = 0; i < f->ncodes; i++) fx[i] = f->fx[i];
-  if (safe)
-    for (int i = 0; i < f->nsafe; i++) safe[i] = f->safe[i];
-  if (nsafe) *nsafe = f->nsafe;
-  return MXQ_OK;
-}
-
-int mxq_lut_tables(const float* P, float* T, int64_t K, int64_t n, int64_t sk, int64_t sj, int32_t group,
-                   int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream) {
+template <typename TIn>
+int launch_tables(const TIn* P, float* T, int64_t K, int64_t n, int64_t sk, int64_t sj, int32_t group,
+                   int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream, bool zero_status = true,
+                   float* cmap = nullptr) {
   if (int r = fmt_slot_check(e, m, "tables")) return r;
   MXQ_REQUIRE(group >= 0 && group < 31, MXQ_ERR_VALUE, "mxq.lut: group %d must be a non-negative integer", group);
   MXQ_REQUIRE(max_iters >= 0, MXQ_ERR_VALUE, "mxq.lut: max_iters %d must be a non-negative integer", max_iters);
@@ -845,7 +899,8 @@ int mxq_lut_tables(const float* P, float* T, int64_t K, int64_t n, int64_t sk, i
   const FormatTables* f = format_tables(e, m);
   MXQ_REQUIRE(f->nmag > 0, MXQ_ERR_UNSUPPORTED, "lut.tables: (e=%d, m=%d) has no sign-magnitude grid", e, m);
   cudaStream_t st = as_stream(stream);
-  if (int r = check_cuda(cudaMemsetAsync(status, 0, sizeof(int32_t), st), "lut.tables")) return r;
+  if (zero_status)
+    if (int r = check_cuda(cudaMemsetAsync(status, 0, sizeof(int32_t), st), "lut.tables")) return r;
   const int64_t ng = (n + ((int64_t)1 << group) - 1) >> group;
   if (ng == 0) return MXQ_OK;
   TableParams tp;
@@ -865,19 +920,28 @@ int mxq_lut_tables(const float* P, float* T, int64_t K, int64_t n, int64_t sk, i
   for (int b = 0; b < f->nv; b++) tp.bin[f2u(f->grid[b]) >> tp.keyshift] = (uint8_t)b;
   for (int b = 0; b < f->nv; b++)                          // -0 counts as the zero code (the grid holds +0)
     if (f->grid[b] == 0.0f) tp.bin[0x80000000u >> tp.keyshift] = (uint8_t)b;
+  tp.ncodes = f->ncodes;
+  for (int c = 0; c < f->ncodes; c++) tp.vals[c] = f->vals[c];
+  for (int c = 0; c < MAXV; c++) {                         // a code byte's rank: its value's place in the grid
+    tp.cbin[c] = 0xFF;
+    if (c < f->ncodes && !std::isnan(f->vals[c]) && !std::isinf(f->vals[c]))
+      for (int b = 0; b < f->nv; b++)
+        if (f->grid[b] == f->vals[c]) tp.cbin[c] = (uint8_t)b;
+  }
   // A cluster of cs CTAs per panel of gpc groups (32 columns, or one group when a group is wider): the CTAs split
   // the panel's rows for the histogram and its groups for the fits; cs (1..8) makes about three CTAs per SM.
   const int gpc = group >= 5 ? 1 : (32 >> group);
   const int64_t panels = (ng + gpc - 1) / gpc;
   int cs = 1;
   while (cs < 8 && panels * cs < 3 * (int64_t)sm_count() && 2 * cs <= K) cs *= 2;
-  const size_t smem = (size_t)gpc * (f->nv + 1) * sizeof(int);
-  // static (~44 KB) plus the histograms can pass the 48 KB default
-  if (int r = check_cuda(cudaFuncSetAttribute(k_lut_tables, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+  const size_t smem = (((size_t)gpc * (f->nv | 1) + 1) & ~(size_t)1) * sizeof(int) +
+                      2 * (size_t)NW * (MAXV + 1) * sizeof(double);
+  // static (~10 KB) plus the histograms and the prefix sums (33 KB) pass the 48 KB default
+  if (int r = check_cuda(cudaFuncSetAttribute(k_lut_tables<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                          "lut.tables: shared memory attribute"))
     return r;
   // all of shared memory for the L1 / shared split, so four CTAs (with their static ~40 KB) fit on an SM
-  if (int r = check_cuda(cudaFuncSetAttribute(k_lut_tables, cudaFuncAttributePreferredSharedMemoryCarveout, 100),
+  if (int r = check_cuda(cudaFuncSetAttribute(k_lut_tables<TIn>, cudaFuncAttributePreferredSharedMemoryCarveout, 100),
                          "lut.tables: shared memory carveout"))
     return r;
   MXQ_REQUIRE(panels * cs < (1ll << 31), MXQ_ERR_UNSUPPORTED, "lut.tables: %lld column groups", (long long)ng);
@@ -893,11 +957,83 @@ int mxq_lut_tables(const float* P, float* T, int64_t K, int64_t n, int64_t sk, i
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (int r = check_cuda(cudaLaunchKernelEx(&cfg, k_lut_tables, P, K, n, sk, sj, (int)group, gpc, (int)max_iters, tp,
-                                            T, status),
+  if (int r = check_cuda(cudaLaunchKernelEx(&cfg, k_lut_tables<TIn>, P, K, n, sk, sj, (int)group, gpc, (int)max_iters,
+                                            tp, T, status, cmap),
                          "lut.tables"))
     return r;
   return MXQ_LAUNCH_CHECK("lut.tables");
+}
+
+CodeTables code_tables(const FormatTables* f) {
+  CodeTables ct;
+  ct.ncodes = f->ncodes;
+  ct.nenc = f->nenc;
+  for (int i = 0; i < f->ncodes; i++) {
+    ct.vals[i] = f->vals[i];
+    ct.fx[i] = f->fx[i];
+  }
+  for (int i = 0; i < f->nenc; i++) {
+    ct.enc_bits[i] = f->enc_bits[i];
+    ct.enc_code[i] = f->enc_code[i];
+  }
+  return ct;
+}
+
+}  // namespace
+
+namespace mxq {
+// block.lut from code bytes (row-major K x n, n a multiple of 4, 16-byte aligned): the tables of the codes with every
+// group's code -> entry map (status not zeroed: the quantizer's bits stay), then every code replaced by its entry.
+// MXQ_ERR_UNSUPPORTED when a panel's maps do not fit in shared memory (8-bit formats at group 0).
+int lut_tables_codes_map(const uint8_t* codes, float* T, float* cmap, int64_t K, int64_t n, int32_t group,
+                         int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream) {
+  return launch_tables(codes, T, K, n, n, 1, group, max_iters, e, m, status, stream, false, cmap);
+}
+// the shared memory a panel's maps need (0 when the lookup cannot take these sizes)
+size_t lut_code_lookup_smem(int64_t n, int32_t group, int32_t e, int32_t m) {
+  const FormatTables* f = format_tables(e, m);
+  if (f == nullptr || n % 4) return 0;
+  const int64_t groups = group >= 7 ? 1 : (PWL >> group);
+  const size_t smem = (size_t)groups * f->ncodes * sizeof(float);
+  return smem <= (96u << 10) ? smem : 0;
+}
+int lut_code_lookup(const uint8_t* codes, const float* cmap, float* out, int64_t K, int64_t n, int32_t group,
+                    int32_t e, int32_t m, void* stream) {
+  if (int r = fmt_slot_check(e, m, "lookup")) return r;
+  if (K * n == 0) return MXQ_OK;
+  const size_t smem = lut_code_lookup_smem(n, group, e, m);
+  if (smem == 0 || (uintptr_t)codes % 4 || (uintptr_t)out % 16 || K >= (1ll << 31)) return MXQ_ERR_UNSUPPORTED;
+  if (int r = check_cuda(cudaFuncSetAttribute(k_lut_code_lookup, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)smem), "lut lookup: shared memory attribute"))
+    return r;
+  // CTAs per SM: each stages its panel's maps (from L2), so fewer, longer CTAs when the maps are large
+  const int per_sm = 8;
+  int64_t rows;
+  const dim3 grid = cols_grid(K, n, PWL, per_sm, &rows);
+  k_lut_code_lookup<<<grid, CT, smem, as_stream(stream)>>>(codes, cmap, out, K, n, group, format_tables(e, m)->ncodes,
+                                                          rows);
+  return MXQ_LAUNCH_CHECK("block.lut lookup");
+}
+}  // namespace mxq
+
+extern "C" {
+
+int mxq_lut_format_tables(int32_t e, int32_t m, float* vals, int64_t* fx, float* safe, int32_t* nsafe) {
+  if (int r = fmt_slot_check(e, m, "format_tables")) return r;
+  const FormatTables* f = format_tables(e, m);
+  if (vals)
+    for (int i = 0; i < f->ncodes; i++) vals[i] = f->vals[i];
+  if (fx)
+    for (int i = 0; i < f->ncodes; i++) fx[i] = f->fx[i];
+  if (safe)
+    for (int i = 0; i < f->nsafe; i++) safe[i] = f->safe[i];
+  if (nsafe) *nsafe = f->nsafe;
+  return MXQ_OK;
+}
+
+int mxq_lut_tables(const float* P, float* T, int64_t K, int64_t n, int64_t sk, int64_t sj, int32_t group,
+                   int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream) {
+  return launch_tables(P, T, K, n, sk, sj, group, max_iters, e, m, status, stream);
 }
 
 int mxq_lut_pick(const float* P, const float* T, int64_t* I, int64_t K, int64_t n, int64_t sk, int64_t sj,

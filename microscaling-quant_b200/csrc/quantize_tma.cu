@@ -244,6 +244,39 @@ struct OutPack {
   }
 };
 
+// block.lut's codes: each code as its OCP bit pattern in a byte (the 6- and 8-bit LUT formats) and each scale as
+// float32; status bit 1 for a code the format cannot hold (as OutPack), 4 for a lost tile
+template <int E, int M>
+struct OutCodes {
+  uint8_t* P;
+  float* X;
+  int* status;
+  bool bad_code = false;
+  template <bool FINITE = false>
+  __device__ __forceinline__ void codes(int64_t idx, float4 v) {
+    uint32_t c0, c1, c2, c3;
+    if (FINITE) {
+      c0 = ocp_code_finite<E, M>(v.x);
+      c1 = ocp_code_finite<E, M>(v.y);
+      c2 = ocp_code_finite<E, M>(v.z);
+      c3 = ocp_code_finite<E, M>(v.w);
+    } else {
+      c0 = ocp_code<E, M>(v.x, bad_code);
+      c1 = ocp_code<E, M>(v.y, bad_code);
+      c2 = ocp_code<E, M>(v.z, bad_code);
+      c3 = ocp_code<E, M>(v.w, bad_code);
+    }
+    __stcs(reinterpret_cast<unsigned int*>(P + idx), c0 | (c1 << 8) | (c2 << 16) | (c3 << 24));
+  }
+  __device__ __forceinline__ void scale(int64_t idx, float x) { X[idx] = x; }
+  __device__ __forceinline__ void finish() {
+    if (bad_code) atomicOr(status, 1);
+  }
+  __device__ __forceinline__ void lost() {
+    if (threadIdx.x == 0) atomicOr(status, 4);
+  }
+};
+
 // A tile's coordinates, from its index by 32-bit division once per tile: column tile ct, and rest = the row tile
 // (ROWS) or (o, b) = the outer slice and block (COLS). Tile counts stay below 2^31 (the launch checks).
 struct TileAt {
@@ -516,6 +549,7 @@ struct Dest {
   uint8_t* Xc;
   int* status;
   const OutMulti* multi = nullptr;
+  bool codes8 = false;     // Pc: byte codes, X: float32 scales (block.lut's codes)
 };
 
 // block: 32 for every layout and output; 16 or 64 for ROWS with float outputs (the launcher checks)
@@ -523,6 +557,12 @@ template <int FAM, int E, int M>
 int launch_dest(const CUtensorMap& map, bool cols, const Dest& d, int64_t outer, int64_t len, int64_t inner,
                 int64_t block, const TParams& prm, cudaStream_t st) {
   if (d.multi != nullptr) return launch<FAM, E, M, 32>(map, cols, *d.multi, outer, len, inner, prm, st);
+  if (d.codes8) {
+    if constexpr (FAM == MXQ_FAMILY_MXGEMMINI && E + M >= 5)
+      return launch<FAM, E, M, 32>(map, cols, OutCodes<E, M>{d.Pc, d.X, d.status}, outer, len, inner, prm, st);
+    else
+      return MXQ_ERR_UNSUPPORTED;
+  }
   if (d.Pc == nullptr) {
     const OutF o{d.P, d.X};
     if (block == 16) return launch<FAM, E, M, 16>(map, cols, o, outer, len, inner, prm, st);
@@ -560,6 +600,7 @@ int quantize_tma_dest(const float* V, const Dest& d, int64_t outer, int64_t len,
   if ((block != 32 && !other) || s.family == MXQ_FAMILY_FP32) return MXQ_ERR_UNSUPPORTED;
   const int64_t rowlen = cols ? inner : len;
   uintptr_t out_base = d.Pc ? (uintptr_t)d.Pc : (uintptr_t)d.P;
+  if (d.codes8 && (block != 32 || (uintptr_t)d.X % 4)) return MXQ_ERR_UNSUPPORTED;
   if (d.multi != nullptr) {
     if (block != 32) return MXQ_ERR_UNSUPPORTED;
     out_base = 0;
@@ -602,6 +643,18 @@ int quantize_tma_packed(const float* V, uint8_t* Pc, uint8_t* Xc, int* status, i
   return quantize_tma_dest(V, Dest{nullptr, nullptr, Pc, Xc, status}, outer, len, inner, block, s, st);
 }
 
+}  // namespace mxq
+
+namespace mxq {
+// block.lut's codes: block.mxgemmini (no via) of V as byte codes (OCP bit patterns) and float32 scales; status bit 1
+// for a code the format cannot hold. MXQ_ERR_UNSUPPORTED for layouts the TMA kernel does not take.
+int quantize_tma_codes(const float* V, uint8_t* codes, float* X, int* status, int64_t outer, int64_t len,
+                       int64_t inner, const mxq_quant_spec& s, cudaStream_t st) {
+  if (s.family != MXQ_FAMILY_MXGEMMINI || s.via_e != 0) return MXQ_ERR_UNSUPPORTED;
+  Dest d{nullptr, X, codes, nullptr, status};
+  d.codes8 = true;
+  return quantize_tma_dest(V, d, outer, len, inner, 32, s, st);
+}
 }  // namespace mxq
 
 extern "C" int mxq_block_quantize_multi(const float* V, float* const* P, float* const* X, int32_t ndst,

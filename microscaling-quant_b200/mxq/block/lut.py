@@ -5,8 +5,10 @@ keyword-required, as in the reference.
     P, X = quantize(V, "MXFP6_E3M2", axis=0, block_size=32, rounding_mode="rne", scale_floor=2**-23,
                     group=1, max_iters=50)                                V_hat = P * expand(X)
 
-One C call (mxq_block_lut_quantize): the fused block quantizer, the table fit and pick with lookup fused, the
-codes and tables in a workspace; an axis-1 operand is read transposed in place, never copied.
+One C call (mxq_block_lut_quantize). Along axis 0 the fused quantizer writes each code as a byte (its OCP bit
+pattern), the table fit histograms the bytes and leaves each group's code -> entry map, and the last kernel reads
+one map entry per element; along axis 1 (the operand read transposed in place, never copied) the quantizer writes
+float codes, and the fit and a fused pick + lookup read them. Codes, tables and maps live in a workspace.
 """
 import ctypes
 
@@ -44,7 +46,10 @@ def quantize(V: torch.Tensor, fmt, axis: int, block_size: int, *, rounding_mode:
     st = torch.empty(1, dtype=torch.int32, device=dev)
     _lib.run("mxq_block_lut_quantize", dev, _lib.ptr(v), _lib.ptr(P), _lib.ptr(X), rows, cols, ax, block_size,
              ctypes.byref(spec), group, max_iters, _lib.ptr(ws), ws.numel(), _lib.ptr(st))
-    if int(st.item()):
+    bits = int(st.item())
+    if bits & 4:
+        raise RuntimeError("block.lut: a tile's load did not arrive within the quantizer's bounded wait")
+    if bits:
         raise ValueError(f"mxq.lut: P holds a value that is not a {f.name} code; quantize it first")
     return _lib.back(P, home), _lib.back(X, home)
 
