@@ -28,11 +28,8 @@ constexpr int kMaxDevices = 64;
 namespace mxq {
 int quantize_tma_codes(const float* V, uint8_t* codes, float* X, int* status, int64_t outer, int64_t len,
                        int64_t inner, const mxq_quant_spec& s, cudaStream_t st);
-int lut_tables_codes_map(const uint8_t* codes, float* T, float* cmap, int64_t K, int64_t n, int32_t group,
-                         int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream);
-size_t lut_code_lookup_smem(int64_t n, int32_t group, int32_t e, int32_t m);
-int lut_code_lookup(const uint8_t* codes, const float* cmap, float* out, int64_t K, int64_t n, int32_t group,
-                    int32_t e, int32_t m, void* stream);
+int lut_tables_codes_lookup(const uint8_t* codes, float* T, float* cmap, float* out, int64_t K, int64_t n,
+                            int32_t group, int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream);
 }  // namespace mxq
 
 namespace {
@@ -84,16 +81,17 @@ int mxq_block_lut_quantize(const float* V, float* P_lut, float* X, int64_t rows,
               (long long)workspace_bytes);
   const bool ax0 = axis % 2 == 0;
   // Axis 0 (the K x n operand is V's own row-major layout): the codes as bytes (their OCP bit patterns) from the fused
-  // quantizer, the tables and each group's code -> entry map from the bytes, then one map read per element. The
-  // workspace holds the bytes, the tables and the maps (less than the float codes of the general path below).
-  if (ax0 && rows * cols > 0 && mxq::lut_code_lookup_smem(cols, group, spec->e, spec->m) > 0 &&
-      (uintptr_t)V % 16 == 0 && (uintptr_t)P_lut % 16 == 0) {
+  // quantizer, then one launch that fits the tables from the bytes, leaves each group's code -> entry map and reads
+  // one map entry per element. The workspace holds the bytes, the tables and the maps (less than the float codes of
+  // the general path below).
+  if (ax0 && rows * cols > 0 && cols % 4 == 0 && (uintptr_t)V % 16 == 0 && (uintptr_t)P_lut % 16 == 0) {
     const int64_t ng = (cols + ((int64_t)1 << group) - 1) >> group;
     const int64_t nc = (int64_t)1 << (1 + spec->e + spec->m);
-    uint8_t* codes = static_cast<uint8_t*>(workspace);
-    float* Tb = reinterpret_cast<float*>(codes + round_up(rows * cols));
+    uint8_t* codes = static_cast<uint8_t*>(workspace);         // by 32-column panels: rows x (cols rounded up to 32)
+    const int64_t code_bytes = round_up(rows * ((cols + 31) / 32 * 32));
+    float* Tb = reinterpret_cast<float*>(codes + code_bytes);
     float* cmap = Tb + round_up(ng * kTableWidth * (int64_t)sizeof(float)) / (int64_t)sizeof(float);
-    const int64_t used = round_up(rows * cols) + round_up(ng * kTableWidth * (int64_t)sizeof(float)) +
+    const int64_t used = code_bytes + round_up(ng * kTableWidth * (int64_t)sizeof(float)) +
                          ng * nc * (int64_t)sizeof(float);
     cudaStream_t st = as_stream(stream);
     if (used <= workspace_bytes) {
@@ -101,10 +99,8 @@ int mxq_block_lut_quantize(const float* V, float* P_lut, float* X, int64_t rows,
       const int q = mxq::quantize_tma_codes(V, codes, X, status, 1, rows, cols, *spec, st);
       if (q != MXQ_ERR_UNSUPPORTED) {
         if (q) return q;
-        if (int r = mxq::lut_tables_codes_map(codes, Tb, cmap, rows, cols, group, max_iters, spec->e, spec->m, status,
-                                              stream))
-          return r;
-        return mxq::lut_code_lookup(codes, cmap, P_lut, rows, cols, group, spec->e, spec->m, stream);
+        return mxq::lut_tables_codes_lookup(codes, Tb, cmap, P_lut, rows, cols, group, max_iters, spec->e, spec->m,
+                                            status, stream);
       }
     }
   }

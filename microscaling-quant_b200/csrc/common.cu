@@ -40,6 +40,30 @@ int sm_count() {
   return cache[dev];
 }
 
+unsigned long long context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static std::once_flag once;
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static std::once_flag once;
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;

@@ -16,6 +16,10 @@ int set_error(int code, const char* fmt, ...);
 int check_cuda(cudaError_t e, const char* what);
 // Number of SMs of the current device (cached per device).
 int sm_count();
+// A number naming the calling thread's current CUDA context, unique for the life of the process (a context made
+// after cudaDeviceReset gets a new one), so per-device state uploaded once can tell that it must be uploaded again;
+// 0 when the driver cannot say.
+unsigned long long context_id();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

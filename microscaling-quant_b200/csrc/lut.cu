@@ -15,6 +15,7 @@
 #include <type_traits>
 #include <cmath>
 #include <algorithm>
+#include <memory>
 #include <mutex>
 #include <vector>
 
@@ -159,18 +160,24 @@ const FormatTables* format_tables(int e, int m) {
 
 // ------------------------------------------------------------------------------------------- device side
 constexpr int KEYS = 1 << 12;                  // bit-pattern keys of a code: sign, exponent, top m <= 3 fraction bits
+// A format's tables for the tables kernel, in global memory (read with coalesced loads at each CTA's start; kernel
+// parameters indexed per lane would be serialised by the constant cache)
+struct DevTables {
+  float grid[MAXV];                            // sorted distinct finite values
+  float safe[MAXV];                            // finder-safe values, sorted
+  float vals[MAXV];                            // every code's value (for the code -> entry map of block.lut)
+  uint8_t order[MAXV];                         // safe indices by |value|: the padding order
+  uint8_t cbin[MAXV];                          // code (its OCP bit pattern) -> grid rank, 0xFF for NaN / Inf
+  uint8_t bin[KEYS];                           // key -> grid rank, 0xFF for a pattern that is no code
+};
+__device__ DevTables g_dev_tables[4];          // one per format slot, per device (module globals are per device)
+
 struct TableParams {                           // by value: what the tables kernel needs of a format
-  int nv, nsafe;
+  int nv, nsafe, ncodes;
   int nmag, bias, m;                           // grid = -mag[nmag-1] .. -mag[1], 0, mag[1] .. mag[nmag-1]
   int keyshift;                                // 23 - m: a code's float32 pattern >> keyshift is its key
   uint32_t lowmask;                            // the fraction bits below a code's m: zero in every code
-  float grid[MAXV];
-  float safe[MAXV];
-  uint8_t order[MAXV];
-  uint8_t bin[KEYS];                           // key -> grid rank, 0xFF for a pattern that is no code
-  uint8_t cbin[MAXV];                          // code (its OCP bit pattern) -> grid rank, 0xFF for NaN / Inf
-  int ncodes;
-  float vals[MAXV];                            // every code's value (for the code -> entry map of block.lut)
+  const DevTables* dt;
 };
 
 constexpr int NW = NT / 32;                    // warps per CTA
@@ -215,6 +222,12 @@ __device__ __forceinline__ double dedupe_lanes(double v, double* scratch) {
   return v;
 }
 
+// The warps of a CTA that fit a group: group gl of a cs-CTA cluster's gpc is fitted by CTA gl % cs, warp gl / cs
+__host__ __device__ __forceinline__ int fit_warps(int gpc, int cs) {
+  const int w = (gpc + cs - 1) / cs;
+  return w < NW ? w : NW;
+}
+
 // The tables (kmeans.py:46-122). A cluster of cs CTAs per panel of gpc column groups: (1) the panel's codes
 // histogrammed by grid rank, each CTA its rows into its own shared memory, then group gl merged across the cluster by
 // CTA gl % cs; then one warp per group: (2) prefix sums of counts and of counts x values over the sorted
@@ -228,22 +241,32 @@ __device__ __forceinline__ double dedupe_lanes(double v, double* scratch) {
 // are differences of the prefix sums. That equals the reference's argmin over all 16 centres whenever consecutive
 // centres are at least 2^-33 apart (distances below 2^17 then never round to a tie across a centre); a pass that
 // finds two closer centres assigns code by code instead.
-template <typename TIn>                                     // float codes, or uint8_t OCP bit patterns (block.lut)
+// TIn: float codes at P[k sk + j sj], or (block.lut) code bytes stored by 32-column panels, byte (k, j) at
+// ((j / 32) K + k) 32 + j % 32 (sk, sj unused)
+template <typename TIn>
 __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P, int64_t K, int64_t n, int64_t sk,
-                                                   int64_t sj, int G, int gpc, int max_iters,
+                                                   int64_t sj, int G, int gpc, int max_iters, int priv_ok,
                                                    const __grid_constant__ TableParams tp, float* __restrict__ T,
-                                                   int* __restrict__ status, float* __restrict__ cmap) {
+                                                   int* __restrict__ status, float* __restrict__ cmap,
+                                                   float* __restrict__ out) {
   // dynamic shared memory: counts [gpc][nv | 1] (this CTA's rows; then merged, its own groups), then the fits'
-  // prefix sums [2][NW][MAXV + 1] doubles
+  // prefix sums [2][nfw][nv + 1] doubles for the nfw warps that fit a group; with `out`, the panel's code -> entry
+  // maps [gpc][ncodes + 1] over the same bytes once the fits are done
+  constexpr bool BYTES = sizeof(TIn) == 1;
   extern __shared__ int counts[];
   __shared__ double scratch[NW][LUT], fsum[NW][LUT], fw[NW][LUT];
-  __shared__ float sgrid[MAXV];
+  __shared__ __align__(16) float sgrid[MAXV];                // the format's tables, read with per-lane indices
+  __shared__ __align__(16) float ssafe[MAXV];
+  __shared__ __align__(16) float svals[MAXV];
+  __shared__ __align__(16) uint8_t sorder[MAXV];
+  __shared__ float stab[NW][LUT];                            // each fitting warp's finished table
   __shared__ unsigned char member[NW][MAXV];
-  __shared__ __align__(16) uint8_t sbin[KEYS];
+  __shared__ __align__(16) uint8_t sbin[BYTES ? MAXV : KEYS];
   __shared__ int bad;
   cg::cluster_group cluster = cg::this_cluster();
   const int cs = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nv = tp.nv;
+  const int nfw = fit_warps(gpc, cs);
   const unsigned lt = (1u << lane) - 1u;
   const int64_t ng = (n + ((int64_t)1 << G) - 1) >> G;
   const int64_t g0 = (int64_t)(blockIdx.x / cs) * gpc;       // the cluster's panel of groups
@@ -253,17 +276,21 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
   const int64_t kbeg = (int64_t)rank * kper < K ? (int64_t)rank * kper : K;
   const int64_t kend = kbeg + kper < K ? kbeg + kper : K;
   const int nvp = nv | 1;                                   // a group's histogram row, odd: a bin of 32 groups hits 32 banks
-  double* const pw = reinterpret_cast<double*>(counts + ((gpc * nvp + 1) & ~1));   // [NW][MAXV + 1]
-  double* const pwx = pw + NW * (MAXV + 1);
+  double* const pw = reinterpret_cast<double*>(counts + ((gpc * nvp + 3) & ~3));   // [nfw][nv + 1]
+  double* const pwx = pw + nfw * (nv + 1);
   for (int i = tid; i < gpc * nvp; i += NT) counts[i] = 0;
-  for (int i = tid; i < nv; i += NT) sgrid[i] = tp.grid[i];
-  constexpr bool BYTES = sizeof(TIn) == 1;
-  if (BYTES) {                                              // a code byte's grid rank (0xFF: NaN / Inf)
-    for (int i = tid; i < MAXV / 4; i += NT)
-      reinterpret_cast<uint32_t*>(sbin)[i] = reinterpret_cast<const uint32_t*>(tp.cbin)[i];
-  } else {
-    for (int i = tid; i < KEYS / 4; i += NT)
-      reinterpret_cast<uint32_t*>(sbin)[i] = reinterpret_cast<const uint32_t*>(tp.bin)[i];
+  // the tables the fits index per lane, into shared memory once
+  {
+    const DevTables* dt = tp.dt;
+    for (int i = tid; i < MAXV / 4; i += NT) {
+      reinterpret_cast<float4*>(sgrid)[i] = __ldg(reinterpret_cast<const float4*>(dt->grid) + i);
+      reinterpret_cast<float4*>(ssafe)[i] = __ldg(reinterpret_cast<const float4*>(dt->safe) + i);
+      if (cmap != nullptr) reinterpret_cast<float4*>(svals)[i] = __ldg(reinterpret_cast<const float4*>(dt->vals) + i);
+    }
+    for (int i = tid; i < MAXV / 16; i += NT)
+      reinterpret_cast<uint4*>(sorder)[i] = __ldg(reinterpret_cast<const uint4*>(dt->order) + i);
+    const uint4* bsrc = reinterpret_cast<const uint4*>(BYTES ? dt->cbin : dt->bin);   // a code's grid rank
+    for (int i = tid; i < (BYTES ? MAXV : KEYS) / 16; i += NT) reinterpret_cast<uint4*>(sbin)[i] = __ldg(bsrc + i);
   }
   if (tid == 0) bad = 0;
   __syncthreads();
@@ -271,7 +298,7 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
   // 1. counts of each distinct code per group (kmeans.py:58-64); consecutive threads read consecutive memory
   const int64_t Kc = kend - kbeg;                           // rows of this CTA
   const int64_t total = Kc * W;
-  const bool kfast = sk == 1;
+  const bool kfast = !BYTES && sk == 1;
   bool mybad = false;
   constexpr int BATCH = 8;                                  // loads in flight per thread
   constexpr int PBATCH = 8;                                 // the pair path's
@@ -293,20 +320,121 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
     else atomicAdd(&counts[gc * nvp + (int)b], 1);
   };
   using V2 = typename std::conditional<BYTES, uchar2, float2>::type;
-  if (sj == 1 && W <= 32 && W % 2 == 0 && sk % 2 == 0 && ((uintptr_t)(P + j0)) % (2 * sizeof(TIn)) == 0) {
+  // the panel's first element and row stride (a panel never spans two 32-column runs of code bytes), and any
+  // element's place
+  const TIn* const pb = BYTES ? P + j0 * K : P + j0 * sj;
+  const int64_t rs = BYTES ? 32 : sk, cst = BYTES ? 1 : sj;
+  auto at = [&](int64_t k, int64_t j) -> int64_t { return BYTES ? ((j >> 5) * K + k) * 32 + (j & 31) : k * sk + j * sj; };
+  const bool pairs = cst == 1 && W <= 32 && W % 2 == 0 && rs % 2 == 0 && ((uintptr_t)pb) % (2 * sizeof(TIn)) == 0;
+  bool counted = false;
+  if constexpr (BYTES) {
+    if (pairs && priv_ok && G >= 1 && tp.ncodes <= 64 && Kc <= 16 * 32767) {
+      // 6-bit codes: every thread counts its bytes in its own column of [64][NT] 16-bit counters (a thread's column
+      // pair lies in one group at G >= 1, and it sees at most 2 ceil(Kc / 16) codes) with plain shared loads and
+      // stores: no atomics, and the 32 counters of one code of a warp are 64 consecutive bytes, so lanes never meet
+      // in a bank whatever their codes. A code past the format's (a byte >= ncodes) is remembered by the largest
+      // byte seen and counted, masked, where it cannot hurt: the whole panel is refused.
+      uint16_t* const priv = reinterpret_cast<uint16_t*>(pw);
+      for (int i = tid; i < 64 * NT / 8; i += NT) reinterpret_cast<uint4*>(priv)[i] = make_uint4(0u, 0u, 0u, 0u);
+      __syncthreads();
+      const int c2 = lane & 15, ro = lane >> 4;
+      uint32_t mx = 0;
+      if (2 * c2 < W) {
+        const int64_t r0 = 2 * warp + ro;                    // rows r0, r0 + 16, ... of the CTA's
+        const int64_t nr = r0 < Kc ? (Kc - 1 - r0) / 16 + 1 : 0;
+        const uint16_t* src = reinterpret_cast<const uint16_t*>(pb + (kbeg + r0) * rs) + c2;
+        const int64_t rstep = 8 * rs;                          // 16 rows, in 2-byte units
+        uint16_t* const mine = priv + tid;
+        constexpr int PB = 16;
+        auto add = [&](uint32_t v) {
+          const uint32_t a = v & 0xffu, b = v >> 8;
+          mx = max(mx, max(a, b));
+          mine[(a & 63u) * NT] += 1;
+          mine[(b & 63u) * NT] += 1;
+        };
+        int64_t r = 0;
+        for (; r + PB <= nr; r += PB) {
+          uint32_t v[PB];
+#pragma unroll
+          for (int u = 0; u < PB; u++) v[u] = src[u * rstep];
+          src += PB * rstep;
+#pragma unroll
+          for (int u = 0; u < PB; u++) add(v[u]);
+        }
+        for (; r < nr; r++, src += rstep) add(*src);
+      }
+      if (mx >= (uint32_t)tp.ncodes) mybad = true;
+      __syncthreads();
+      // into the CTA's histogram: warp w sums code s over the 8 warps' counters, then over the lanes of a group (its
+      // two rows and its 2^(G-1) column pairs), and one lane adds the total to the group's bin
+      const int sh = G - 1 < 4 ? G - 1 : 4;
+      for (int sl = warp; sl < tp.ncodes; sl += NW) {
+        int sum = 0;
+#pragma unroll
+        for (int j = 0; j < NW; j++) sum += priv[sl * NT + j * 32 + lane];
+        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+        for (int o = 1; o < (1 << sh); o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane < 16 && (c2 & ((1 << sh) - 1)) == 0 && 2 * c2 < W && sum > 0) {
+          const uint32_t bin = sbin[sl];
+          if (bin == 0xFFu) mybad = true;                    // a NaN / Inf code
+          else atomicAdd(&counts[(c2 >> sh) * nvp + (int)bin], sum);
+        }
+      }
+      counted = true;
+    } else if (pairs && W % 4 == 0 && rs % 4 == 0 && ((uintptr_t)pb) % 4 == 0) {
+      // 8-bit codes: 4-byte quads, lane l taking columns 4 (l % 8) .. 4 (l % 8) + 3 of row l / 8 of its warp's four
+      // rows, one shared atomic per code into its group's bin. A byte that is no code has bin 0xFF: remembered by the
+      // largest bin seen and counted where it cannot hurt (within the 256 spare counters after the histograms; the
+      // whole panel is refused)
+      const int q = lane & 7, ro = lane >> 3;
+      uint32_t mxb = 0;
+      if (4 * q < W) {
+        int rb[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) rb[i] = ((4 * q + i) >> G) * nvp;
+        const int64_t r0 = 4 * warp + ro;                    // rows r0, r0 + 32, ... of the CTA's
+        const int64_t nr = r0 < Kc ? (Kc - 1 - r0) / 32 + 1 : 0;
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(pb + (kbeg + r0) * rs) + q;
+        const int64_t rstep = 8 * rs;                          // 32 rows, in 4-byte units
+        constexpr int QB = 16;
+        auto add = [&](uint32_t v) {
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const uint32_t bn = sbin[(v >> (8 * i)) & 0xffu];
+            mxb = max(mxb, bn);
+            atomicAdd(&counts[rb[i] + (int)bn], 1);
+          }
+        };
+        int64_t r = 0;
+        for (; r + QB <= nr; r += QB) {
+          uint32_t v[QB];
+#pragma unroll
+          for (int u = 0; u < QB; u++) v[u] = src[u * rstep];
+          src += QB * rstep;
+#pragma unroll
+          for (int u = 0; u < QB; u++) add(v[u]);
+        }
+        for (; r < nr; r++, src += rstep) add(*src);
+      }
+      if (mxb == 0xFFu) mybad = true;
+      counted = true;
+    }
+  }
+  if (counted) {
+  } else if (pairs) {
     // a panel of at most 32 columns as float2 pairs: lane l takes the pair of columns 2 (l % 16), 2 (l % 16) + 1 of
     // row (l / 16) of its warp's two rows, so a warp instruction's 32 lanes count into (at G = 1) 16 different
     // groups' rows and the 16-byte-per-lane-pair row segments are read whole; the CTA steps 2 x 8 rows
     const int c2 = lane & 15, ro = lane >> 4;
     if (2 * c2 < W) {
-      const V2* src = reinterpret_cast<const V2*>(P + j0) + c2;
+      const V2* src = reinterpret_cast<const V2*>(pb) + c2;
       const int ga = (2 * c2) >> G, gb = (2 * c2 + 1) >> G;
       const int64_t step = 2 * NW;
       for (int64_t k0 = kbeg + 2 * warp + ro; k0 < kend; k0 += step * PBATCH) {
         V2 v[PBATCH];
 #pragma unroll
         for (int u = 0; u < PBATCH; u++)
-          v[u] = k0 + (int64_t)u * step < kend ? src[(k0 + (int64_t)u * step) * (sk / 2)] : V2{};
+          v[u] = k0 + (int64_t)u * step < kend ? src[(k0 + (int64_t)u * step) * (rs / 2)] : V2{};
 #pragma unroll
         for (int u = 0; u < PBATCH; u++) {
           if (k0 + (int64_t)u * step >= kend) break;
@@ -353,7 +481,7 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
       const int64_t e = e0 + (int64_t)u * NT;
       const int64_t k = kfast ? mnr : maj, jj = kfast ? maj : mnr;
       gcol[u] = e < total ? (int)(jj >> G) : -1;
-      v[u] = e < total ? P[(kbeg + k) * sk + (j0 + jj) * sj] : TIn{};
+      v[u] = e < total ? P[at(kbeg + k, j0 + jj)] : TIn{};
       maj += dmaj;
       mnr += dmin;
       if (mnr >= R) {
@@ -369,56 +497,72 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
   if (mybad) bad = 1;
   // the cluster's CTAs meet: every histogram of the panel is complete (cluster barriers order shared memory across
   // the cluster); CTA r merges groups r, r + cs, ... from all of them into its own rows, then they meet again so no
-  // CTA leaves while another still reads its histograms. Every thread of every CTA reaches both barriers.
+  // CTA leaves while another still reads its histograms. Every thread of every CTA reaches every barrier: a bad code
+  // anywhere in the panel sends the whole cluster out after the second one.
   cluster.sync();
   if (bad && tid == 0) atomicExch(status, 1);
+  int anybad = 0;
+  for (int q = 0; q < cs; q++) anybad |= *cluster.map_shared_rank(&bad, q);
   if (cs > 1) {
-    for (int i = tid; i < gpc * nvp; i += NT) {
-      const int gl = i / nvp;
-      if (gl % cs != rank) continue;
+    const int nown = (gpc - rank + cs - 1) / cs;             // this CTA's groups: rank, rank + cs, ...
+    for (int i = tid; i < nown * nv; i += NT) {
+      const int gi = i / nv, b = i - gi * nv;
+      const int idx = (rank + cs * gi) * nvp + b;
+      int part[8];                                           // cs <= 8: every remote read in flight at once
+#pragma unroll
+      for (int q = 0; q < 8; q++) part[q] = q < cs ? cluster.map_shared_rank(counts, q)[idx] : 0;
       int sum = 0;
-      for (int q = 0; q < cs; q++) sum += cluster.map_shared_rank(counts, q)[i];
-      counts[i] = sum;                                      // only this CTA reads row gl of its own histogram
+#pragma unroll
+      for (int q = 0; q < 8; q++) sum += part[q];
+      counts[idx] = sum;                                     // only this CTA reads row gl of its own histogram
     }
   }
   cluster.sync();
-  if (bad) return;                                          // every CTA saw its own flag before the barrier
+  if (anybad) return;
 
   for (int gl = rank + cs * warp; gl < gpc; gl += cs * NW) {
     const int64_t g = g0 + gl;
     if (g >= ng) break;
     const int* cnt = counts + gl * nvp;
-    double* PW = pw + warp * (MAXV + 1);
-    double* PWX = pwx + warp * (MAXV + 1);
-    // 2. prefix sums over the sorted codes, and the number of distinct codes present
-    double runw = 0.0, runx = 0.0;
+    double* PW = pw + warp * (nv + 1);                        // warp < nfw: gl = rank + cs * warp < gpc
+    double* PWX = pwx + warp * (nv + 1);
+    // 2. prefix sums over the sorted codes, and the number of distinct codes present: lane l sums its run of q
+    // consecutive codes, one warp scan gives each run's offset, then the run's prefixes are written (the sums are
+    // exact, so any order gives the same bits)
+    const int q = (nv + 31) >> 5, b0 = lane * q, b1 = b0 + q < nv ? b0 + q : nv;
+    double w = 0.0, wx = 0.0;
     int npres = 0;
-    for (int b0 = 0; b0 < nv; b0 += 32) {
-      const int b = b0 + lane;
-      const int cb = b < nv ? cnt[b] : 0;
-      double w = (double)cb, wx = b < nv ? __dmul_rn((double)cb, (double)sgrid[b]) : 0.0;
+    for (int b = b0; b < b1; b++) {
+      const int cb = cnt[b];
+      w = __dadd_rn(w, (double)cb);
+      wx = __dadd_rn(wx, __dmul_rn((double)cb, (double)sgrid[b]));
       npres += cb > 0;
-#pragma unroll
-      for (int s = 1; s < 32; s <<= 1) {                     // inclusive scans (exact sums)
-        const double ow = __shfl_up_sync(0xffffffffu, w, s), ox = __shfl_up_sync(0xffffffffu, wx, s);
-        if (lane >= s) {
-          w = __dadd_rn(w, ow);
-          wx = __dadd_rn(wx, ox);
-        }
-      }
-      if (b < nv) {
-        PW[b + 1] = __dadd_rn(runw, w);
-        PWX[b + 1] = __dadd_rn(runx, wx);
-      }
-      runw = __dadd_rn(runw, __shfl_sync(0xffffffffu, w, 31));
-      runx = __dadd_rn(runx, __shfl_sync(0xffffffffu, wx, 31));
-    }
-    if (lane == 0) {
-      PW[0] = 0.0;
-      PWX[0] = 0.0;
     }
 #pragma unroll
-    for (int s = 16; s > 0; s >>= 1) npres += __shfl_xor_sync(0xffffffffu, npres, s);
+    for (int s = 1; s < 32; s <<= 1) {                       // inclusive scans of the runs' sums
+      const double ow = __shfl_up_sync(0xffffffffu, w, s), ox = __shfl_up_sync(0xffffffffu, wx, s);
+      if (lane >= s) {
+        w = __dadd_rn(w, ow);
+        wx = __dadd_rn(wx, ox);
+      }
+      npres += __shfl_xor_sync(0xffffffffu, npres, s);
+    }
+    {
+      double rw = __shfl_up_sync(0xffffffffu, w, 1), rx = __shfl_up_sync(0xffffffffu, wx, 1);
+      if (lane == 0) {
+        rw = 0.0;
+        rx = 0.0;
+        PW[0] = 0.0;
+        PWX[0] = 0.0;
+      }
+      for (int b = b0; b < b1; b++) {
+        const int cb = cnt[b];
+        rw = __dadd_rn(rw, (double)cb);
+        rx = __dadd_rn(rx, __dmul_rn((double)cb, (double)sgrid[b]));
+        PW[b + 1] = rw;
+        PWX[b + 1] = rx;
+      }
+    }
     __syncwarp();
 
     double c = INFINITY;                                     // lane t < 16: centre t
@@ -435,18 +579,21 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
       if (lane < npres) c = scratch[warp][lane];
       __syncwarp();
     } else {
-      // 2b: quantile seeds: the first code whose cumulative weight share reaches (t + 0.5) / 16
+      // 2b: quantile seeds: the first code whose cumulative weight share (rounded, so non-decreasing) reaches
+      // (t + 0.5) / 16 (exact in float64), i.e. the number of codes whose share is below it: every lane divides for
+      // its codes at once and a ballot per probe counts them
       const double tot = PW[nv];
-      if (lane < LUT) {
-        const double probe = __ddiv_rn((double)lane + 0.5, (double)LUT);
-        int lo = 0, hi = nv;
-        while (lo < hi) {
-          const int mid = (lo + hi) >> 1;
-          if (__ddiv_rn(PW[mid + 1], tot) < probe) lo = mid + 1;
-          else hi = mid;
+      int seed = 0;
+      for (int bb = 0; bb < nv; bb += 32) {
+        const int b = bb + lane;
+        const double share = b < nv ? __ddiv_rn(PW[b + 1], tot) : INFINITY;
+#pragma unroll
+        for (int t = 0; t < LUT; t++) {
+          const int below = __popc(__ballot_sync(0xffffffffu, share < ((double)t + 0.5) / (double)LUT));
+          seed += lane == t ? below : 0;
         }
-        c = (double)sgrid[lo < nv - 1 ? lo : nv - 1];
       }
+      if (lane < LUT) c = (double)sgrid[seed < nv - 1 ? seed : nv - 1];
       c = dedupe_lanes(c, scratch[warp]);
       // 2c: weighted Lloyd passes
       for (int it = 0; it < max_iters; it++) {
@@ -529,12 +676,12 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
       int lo = 0, hi = tp.nsafe;
       while (lo < hi) {
         const int mid = (lo + hi) >> 1;
-        if ((double)tp.safe[mid] < c) lo = mid + 1;
+        if ((double)ssafe[mid] < c) lo = mid + 1;
         else hi = mid;
       }
       int best = lo < tp.nsafe ? lo : tp.nsafe - 1;
-      if (lo > 0 && (lo == tp.nsafe || fabs(__dsub_rn(c, (double)tp.safe[lo - 1])) <=
-                                            fabs(__dsub_rn(c, (double)tp.safe[lo]))))
+      if (lo > 0 && (lo == tp.nsafe || fabs(__dsub_rn(c, (double)ssafe[lo - 1])) <=
+                                            fabs(__dsub_rn(c, (double)ssafe[lo]))))
         best = lo - 1;
       member[warp][best] = 1;
     }
@@ -548,7 +695,7 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
     int need = LUT - nmem;
     for (int i0 = 0; i0 < tp.nsafe && need > 0; i0 += 32) {
       const int i = i0 + lane;
-      const int sidx = i < tp.nsafe ? tp.order[i] : 0;
+      const int sidx = i < tp.nsafe ? sorder[i] : 0;
       const bool fr = i < tp.nsafe && !member[warp][sidx];
       const unsigned mask = __ballot_sync(0xffffffffu, fr);
       __syncwarp();
@@ -562,17 +709,23 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
       const bool mb = i < tp.nsafe && member[warp][i];
       const unsigned mask = __ballot_sync(0xffffffffu, mb);
       const int pos = base + __popc(mask & lt);
-      if (mb && pos < LUT) T[g * LUT + pos] = tp.safe[i];
+      if (mb && pos < LUT) {
+        T[g * LUT + pos] = ssafe[i];
+        stab[warp][pos] = ssafe[i];
+      }
       base += __popc(mask);
     }
-    if (lane >= base && lane < LUT) T[g * LUT + lane] = INFINITY;
+    if (lane >= base && lane < LUT) {
+      T[g * LUT + lane] = INFINITY;
+      stab[warp][lane] = INFINITY;
+    }
     __syncwarp();
     if (cmap != nullptr) {
       // block.lut: the entry pick(P, T) chooses for each code's value (nearest of the two sorted entries around it,
       // ties to the lower index), so that the lookup of an element is one read
-      const float* t = T + g * LUT;
+      const float* t = stab[warp];
       for (int c = lane; c < tp.ncodes; c += 32) {
-        const float v = tp.vals[c];
+        const float v = svals[c];
         int b = 0;
         b += t[b + 7] < v ? 8 : 0;
         b += t[b + 3] < v ? 4 : 0;
@@ -584,6 +737,59 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
         cmap[g * tp.ncodes + c] = abs_f(__fsub_rn(v, rl)) <= abs_f(__fsub_rn(rh, v)) ? rl : rh;
       }
     }
+  }
+  if constexpr (BYTES) {
+  if (out == nullptr) return;
+
+  // 5. block.lut: every code of this CTA's rows replaced by its group's map entry. The panel's maps come from the
+  // cluster's fits through global memory (ordered by the fence and the cluster barrier; every CTA of the cluster
+  // reaches it) into padded shared rows over the dead histograms; the codes are read a second time (from L2).
+  __threadfence();
+  cluster.sync();
+  float* const smap = reinterpret_cast<float*>(counts);      // [groups of the panel][ncodes + 1]
+  const int nc = tp.ncodes, ncp = nc + 1;
+  const int ngp = (int)((g0 + gpc < ng ? g0 + gpc : ng) - g0);
+  for (int i = tid; i < ngp * nc; i += NT) {
+    const int gi = i / nc;
+    smap[i + gi] = __ldcg(cmap + g0 * nc + i);
+  }
+  __syncthreads();
+  if (pairs && W % 4 == 0 && rs % 4 == 0 && ((uintptr_t)pb) % 4 == 0 && n % 4 == 0 &&
+      ((uintptr_t)(out + j0)) % 16 == 0) {
+    // 4 codes (one 4-byte load, the histogram's quads) into one float4 store per lane
+    const int q = lane & 7, ro = lane >> 3;
+    if (4 * q < W) {
+      int mo[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) mo[i] = ((4 * q + i) >> G) * ncp;
+      const int64_t r0 = 4 * warp + ro;                      // rows r0, r0 + 32, ... of the CTA's
+      const int64_t nr = r0 < Kc ? (Kc - 1 - r0) / 32 + 1 : 0;
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(pb + (kbeg + r0) * rs) + q;
+      float4* dst = reinterpret_cast<float4*>(out + (kbeg + r0) * n + j0) + q;
+      const int64_t rstep = 8 * rs, ostep = 8 * n;             // 32 rows of codes (4-byte units), of out (float4s)
+      auto put = [&](uint32_t v, float4* o) {
+        __stcs(o, make_float4(smap[mo[0] + (int)(v & 0xffu)], smap[mo[1] + (int)((v >> 8) & 0xffu)],
+                              smap[mo[2] + (int)((v >> 16) & 0xffu)], smap[mo[3] + (int)(v >> 24)]));
+      };
+      constexpr int LB = 8;
+      int64_t r = 0;
+      for (; r + LB <= nr; r += LB) {
+        uint32_t v[LB];
+#pragma unroll
+        for (int u = 0; u < LB; u++) v[u] = __ldcs(src + u * rstep);
+#pragma unroll
+        for (int u = 0; u < LB; u++) put(v[u], dst + u * ostep);
+        src += LB * rstep;
+        dst += LB * ostep;
+      }
+      for (; r < nr; r++, src += rstep, dst += ostep) put(__ldcs(src), dst);
+    }
+  } else {
+    for (int64_t e = tid; e < total; e += NT) {              // element (k, jj) of the CTA's rows
+      const int64_t k = kbeg + e / W, jj = e % W;
+      out[k * n + j0 + jj] = smap[(int)(jj >> G) * ncp + (int)P[at(k, j0 + jj)]];
+    }
+  }
   }
 }
 
@@ -829,46 +1035,6 @@ __global__ void __launch_bounds__(CT) k_lut_finder_cols(const int64_t* __restric
   }
 }
 
-// block.lut's last step from code bytes: lookup(pick(P, T), T) of each element through the code -> entry map that
-// the tables kernel wrote per group (cmap, groups x ncodes), so an element is one shared-memory read. A CTA owns a
-// panel of PWL = 128 columns (lane l of every warp takes columns 4l .. 4l + 3 as one 4-byte load and one float4
-// store), stages its groups' maps, and takes a slice of rows, its 8 warps taking the rows in turn.
-constexpr int PWL = 128;
-__global__ void __launch_bounds__(CT) k_lut_code_lookup(const uint8_t* __restrict__ codes, const float* __restrict__ cmap,
-                                                        float* __restrict__ out, int64_t K, int64_t n, int G, int nc,
-                                                        int64_t rows) {
-  extern __shared__ float smap[];                            // [groups of the panel][ncodes]
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t jp = (int64_t)blockIdx.x * PWL;
-  const int64_t gfirst = jp >> G, glast = ((jp + PWL < n ? jp + PWL : n) - 1) >> G;
-  const int ngp = (int)(glast - gfirst + 1);
-  for (int i = threadIdx.x; i < ngp * nc; i += CT) smap[i] = __ldg(cmap + gfirst * nc + i);
-  __syncthreads();
-  const int64_t j = jp + 4 * lane;
-  if (j >= n) return;
-  int gofs[4];
-#pragma unroll
-  for (int i = 0; i < 4; i++) gofs[i] = (int)(((j + i) >> G) - gfirst) * nc;
-  const int64_t k0 = (int64_t)blockIdx.y * rows, k1 = k0 + rows < K ? k0 + rows : K;
-  constexpr int BATCH = 8;
-  for (int64_t kb = k0 + warp; kb < k1; kb += (int64_t)CW * BATCH) {
-    uint32_t c[BATCH];
-#pragma unroll
-    for (int u = 0; u < BATCH; u++) {
-      const int64_t k = kb + (int64_t)u * CW;
-      c[u] = k < k1 ? __ldcs(reinterpret_cast<const unsigned int*>(codes + k * n + j)) : 0u;
-    }
-#pragma unroll
-    for (int u = 0; u < BATCH; u++) {
-      const int64_t k = kb + (int64_t)u * CW;
-      if (k >= k1) break;
-      const float4 r = make_float4(smap[gofs[0] + (int)(c[u] & 0xffu)], smap[gofs[1] + (int)((c[u] >> 8) & 0xffu)],
-                                   smap[gofs[2] + (int)((c[u] >> 16) & 0xffu)], smap[gofs[3] + (int)(c[u] >> 24)]);
-      __stcs(reinterpret_cast<float4*>(out + k * n + j), r);
-    }
-  }
-}
-
 // the column kernels' grid: panels of `width` columns, and row slices so that about per_sm CTAs per SM are launched
 dim3 cols_grid(int64_t K, int64_t n, int64_t width, int per_sm, int64_t* rows) {
   const int64_t panels = (n + width - 1) / width;
@@ -888,10 +1054,52 @@ int fmt_slot_check(int e, int m, const char* what) {
   return MXQ_OK;
 }
 
+// The format's DevTables on the current device, uploaded on its first use there (a synchronous copy; again after the
+// context changes, as cudaDeviceReset makes a new one with fresh module globals)
+int device_tables(int e, int m, const DevTables** out) {
+  static std::mutex mu;
+  static unsigned long long loaded[64][4] = {};              // the context each slot was uploaded in
+  const int slot = (e == 3 && m == 2) ? 0 : (e == 2 && m == 3) ? 1 : (e == 5 && m == 2) ? 2 : 3;
+  const FormatTables* f = format_tables(e, m);
+  int dev = 0;
+  if (int r = check_cuda(cudaGetDevice(&dev), "lut tables: device")) return r;
+  MXQ_REQUIRE(dev >= 0 && dev < 64, MXQ_ERR_UNSUPPORTED, "lut tables: device %d", dev);
+  void* base = nullptr;
+  if (int r = check_cuda(cudaGetSymbolAddress(&base, g_dev_tables), "lut tables: device tables")) return r;
+  DevTables* mine = static_cast<DevTables*>(base) + slot;
+  const unsigned long long ctx = context_id();
+  std::lock_guard<std::mutex> lock(mu);
+  if (ctx == 0 || loaded[dev][slot] != ctx) {
+    std::unique_ptr<DevTables> h(new DevTables());
+    for (int i = 0; i < MAXV; i++) {
+      h->grid[i] = i < f->nv ? f->grid[i] : INFINITY;
+      h->safe[i] = i < f->nsafe ? f->safe[i] : INFINITY;
+      h->order[i] = i < f->nsafe ? f->order[i] : 0;
+      h->vals[i] = i < f->ncodes ? f->vals[i] : NAN;
+    }
+    const int keyshift = 23 - m;
+    for (int i = 0; i < KEYS; i++) h->bin[i] = 0xFF;
+    for (int b = 0; b < f->nv; b++) h->bin[f2u(f->grid[b]) >> keyshift] = (uint8_t)b;
+    for (int b = 0; b < f->nv; b++)                        // -0 counts as the zero code (the grid holds +0)
+      if (f->grid[b] == 0.0f) h->bin[0x80000000u >> keyshift] = (uint8_t)b;
+    for (int c = 0; c < MAXV; c++) {                       // a code byte's rank: its value's place in the grid
+      h->cbin[c] = 0xFF;
+      if (c < f->ncodes && !std::isnan(f->vals[c]) && !std::isinf(f->vals[c]))
+        for (int b = 0; b < f->nv; b++)
+          if (f->grid[b] == f->vals[c]) h->cbin[c] = (uint8_t)b;
+    }
+    if (int r = check_cuda(cudaMemcpy(mine, h.get(), sizeof(DevTables), cudaMemcpyHostToDevice), "lut tables: upload"))
+      return r;
+    loaded[dev][slot] = ctx;
+  }
+  *out = mine;
+  return MXQ_OK;
+}
+
 template <typename TIn>
 int launch_tables(const TIn* P, float* T, int64_t K, int64_t n, int64_t sk, int64_t sj, int32_t group,
                    int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream, bool zero_status = true,
-                   float* cmap = nullptr) {
+                   float* cmap = nullptr, float* out = nullptr) {
   if (int r = fmt_slot_check(e, m, "tables")) return r;
   MXQ_REQUIRE(group >= 0 && group < 31, MXQ_ERR_VALUE, "mxq.lut: group %d must be a non-negative integer", group);
   MXQ_REQUIRE(max_iters >= 0, MXQ_ERR_VALUE, "mxq.lut: max_iters %d must be a non-negative integer", max_iters);
@@ -906,37 +1114,28 @@ int launch_tables(const TIn* P, float* T, int64_t K, int64_t n, int64_t sk, int6
   TableParams tp;
   tp.nv = f->nv;
   tp.nsafe = f->nsafe;
+  tp.ncodes = f->ncodes;
   tp.nmag = f->nmag;
   tp.bias = (1 << (e - 1)) - 1;
   tp.m = m;
-  for (int i = 0; i < f->nv; i++) tp.grid[i] = f->grid[i];
-  for (int i = 0; i < f->nsafe; i++) {
-    tp.safe[i] = f->safe[i];
-    tp.order[i] = f->order[i];
-  }
   tp.keyshift = 23 - m;
   tp.lowmask = (1u << (23 - m)) - 1u;
-  for (int i = 0; i < KEYS; i++) tp.bin[i] = 0xFF;
-  for (int b = 0; b < f->nv; b++) tp.bin[f2u(f->grid[b]) >> tp.keyshift] = (uint8_t)b;
-  for (int b = 0; b < f->nv; b++)                          // -0 counts as the zero code (the grid holds +0)
-    if (f->grid[b] == 0.0f) tp.bin[0x80000000u >> tp.keyshift] = (uint8_t)b;
-  tp.ncodes = f->ncodes;
-  for (int c = 0; c < f->ncodes; c++) tp.vals[c] = f->vals[c];
-  for (int c = 0; c < MAXV; c++) {                         // a code byte's rank: its value's place in the grid
-    tp.cbin[c] = 0xFF;
-    if (c < f->ncodes && !std::isnan(f->vals[c]) && !std::isinf(f->vals[c]))
-      for (int b = 0; b < f->nv; b++)
-        if (f->grid[b] == f->vals[c]) tp.cbin[c] = (uint8_t)b;
-  }
+  if (int r = device_tables(e, m, &tp.dt)) return r;
   // A cluster of cs CTAs per panel of gpc groups (32 columns, or one group when a group is wider): the CTAs split
   // the panel's rows for the histogram and its groups for the fits; cs (1..8) makes about three CTAs per SM.
   const int gpc = group >= 5 ? 1 : (32 >> group);
   const int64_t panels = (ng + gpc - 1) / gpc;
   int cs = 1;
   while (cs < 8 && panels * cs < 3 * (int64_t)sm_count() && 2 * cs <= K) cs *= 2;
-  const size_t smem = (((size_t)gpc * (f->nv | 1) + 1) & ~(size_t)1) * sizeof(int) +
-                      2 * (size_t)NW * (MAXV + 1) * sizeof(double);
-  // static (~10 KB) plus the histograms and the prefix sums (33 KB) pass the 48 KB default
+  // dynamic shared memory: the histograms, then one region for the fits' prefix sums, the private counters of
+  // 6-bit code bytes, and (code bytes) room for the spare counts of bytes that are no code; the panel's maps over all
+  const int priv_ok = sizeof(TIn) == 1 && group >= 1 && f->ncodes <= 64;
+  size_t region = 2 * (size_t)fit_warps(gpc, cs) * (f->nv + 1) * sizeof(double);
+  if (priv_ok) region = std::max(region, (size_t)64 * NT * sizeof(uint16_t));
+  if (sizeof(TIn) == 1) region = std::max(region, (size_t)MAXV * sizeof(int));
+  size_t smem = (((size_t)gpc * (f->nv | 1) + 3) & ~(size_t)3) * sizeof(int) + region;
+  if (out != nullptr) smem = std::max(smem, (size_t)gpc * (f->ncodes + 1) * sizeof(float));
+  // the histograms and the prefix sums (up to 33 KB) with the static tables (~10 KB) may pass the 48 KB default
   if (int r = check_cuda(cudaFuncSetAttribute(k_lut_tables<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                          "lut.tables: shared memory attribute"))
     return r;
@@ -958,7 +1157,7 @@ int launch_tables(const TIn* P, float* T, int64_t K, int64_t n, int64_t sk, int6
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (int r = check_cuda(cudaLaunchKernelEx(&cfg, k_lut_tables<TIn>, P, K, n, sk, sj, (int)group, gpc, (int)max_iters,
-                                            tp, T, status, cmap),
+                                            priv_ok, tp, T, status, cmap, out),
                          "lut.tables"))
     return r;
   return MXQ_LAUNCH_CHECK("lut.tables");
@@ -982,37 +1181,12 @@ CodeTables code_tables(const FormatTables* f) {
 }  // namespace
 
 namespace mxq {
-// block.lut from code bytes (row-major K x n, n a multiple of 4, 16-byte aligned): the tables of the codes with every
-// group's code -> entry map (status not zeroed: the quantizer's bits stay), then every code replaced by its entry.
-// MXQ_ERR_UNSUPPORTED when a panel's maps do not fit in shared memory (8-bit formats at group 0).
-int lut_tables_codes_map(const uint8_t* codes, float* T, float* cmap, int64_t K, int64_t n, int32_t group,
-                         int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream) {
-  return launch_tables(codes, T, K, n, n, 1, group, max_iters, e, m, status, stream, false, cmap);
-}
-// the shared memory a panel's maps need (0 when the lookup cannot take these sizes)
-size_t lut_code_lookup_smem(int64_t n, int32_t group, int32_t e, int32_t m) {
-  const FormatTables* f = format_tables(e, m);
-  if (f == nullptr || n % 4) return 0;
-  const int64_t groups = group >= 7 ? 1 : (PWL >> group);
-  const size_t smem = (size_t)groups * f->ncodes * sizeof(float);
-  return smem <= (96u << 10) ? smem : 0;
-}
-int lut_code_lookup(const uint8_t* codes, const float* cmap, float* out, int64_t K, int64_t n, int32_t group,
-                    int32_t e, int32_t m, void* stream) {
-  if (int r = fmt_slot_check(e, m, "lookup")) return r;
-  if (K * n == 0) return MXQ_OK;
-  const size_t smem = lut_code_lookup_smem(n, group, e, m);
-  if (smem == 0 || (uintptr_t)codes % 4 || (uintptr_t)out % 16 || K >= (1ll << 31)) return MXQ_ERR_UNSUPPORTED;
-  if (int r = check_cuda(cudaFuncSetAttribute(k_lut_code_lookup, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)smem), "lut lookup: shared memory attribute"))
-    return r;
-  // CTAs per SM: each stages its panel's maps (from L2), so fewer, longer CTAs when the maps are large
-  const int per_sm = 8;
-  int64_t rows;
-  const dim3 grid = cols_grid(K, n, PWL, per_sm, &rows);
-  k_lut_code_lookup<<<grid, CT, smem, as_stream(stream)>>>(codes, cmap, out, K, n, group, format_tables(e, m)->ncodes,
-                                                          rows);
-  return MXQ_LAUNCH_CHECK("block.lut lookup");
+// block.lut from code bytes (K x n, stored by 32-column panels as the quantizer's OutCodes writes them): the tables of the codes (status not zeroed: the quantizer's bits stay),
+// every group's code -> entry map (cmap, groups x ncodes, the entry pick would choose for the code's value), and every
+// code replaced by its entry in `out`, in one launch
+int lut_tables_codes_lookup(const uint8_t* codes, float* T, float* cmap, float* out, int64_t K, int64_t n,
+                            int32_t group, int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream) {
+  return launch_tables(codes, T, K, n, n, 1, group, max_iters, e, m, status, stream, false, cmap, out);
 }
 }  // namespace mxq
 

@@ -131,6 +131,7 @@ __device__ __forceinline__ float divide(float v, float x, float r) {
 // form -- each code as its OCP bit pattern (a byte; FP4: a nibble, two per byte, the even element low) and each
 // scale as an E8M0 byte -- with a flag for any value the form cannot hold. Element index idx is a multiple of 4.
 struct OutF {
+  static constexpr bool kPanels = false;   // codes at their element index (the others but OutCodes alike)
   float* P;
   float* X;
   template <bool FINITE = false>
@@ -145,6 +146,7 @@ struct OutF {
 // Destination 0 takes streaming stores; the others plain stores (remote writes over NVLink).
 constexpr int kMaxDst = 8;
 struct OutMulti {
+  static constexpr bool kPanels = false;
   float* P[kMaxDst];
   float* X[kMaxDst];
   int n;
@@ -212,6 +214,7 @@ __device__ __forceinline__ uint32_t ocp_code_finite(float v) {
 
 template <int E, int M>
 struct OutPack {
+  static constexpr bool kPanels = false;
   uint8_t* P;
   uint8_t* X;
   int* status;
@@ -244,13 +247,26 @@ struct OutPack {
   }
 };
 
-// block.lut's codes: each code as its OCP bit pattern in a byte (the 6- and 8-bit LUT formats) and each scale as
-// float32; status bit 1 for a code the format cannot hold (as OutPack), 4 for a lost tile
+// A code for block.lut's table fit: the OCP bit pattern, read back in the LUT code space, where every E4M3 byte is a
+// finite value (0x7F / 0xFF are +-480, formats.py:91-96) so E4M3's NaN has no code there: it counts as one the format
+// cannot hold, as a NaN code does in the fit of float codes
+template <int E, int M>
+__device__ __forceinline__ uint32_t lut_code(float v, bool& bad) {
+  if (E == 4 && M == 3 && (f2u(v) & 0x7fffffffu) > 0x7f800000u) bad = true;
+  return ocp_code<E, M>(v, bad);
+}
+
+// block.lut's codes: each code as a byte (lut_code; the 6- and 8-bit LUT formats) and each scale as float32; status
+// bit 1 for a code the format cannot hold (as OutPack), 4 for a lost tile. The bytes of a blocks-along-rows operand
+// (len rows x inner columns) are stored by 32-column panels: panel p holds its rows one after another, 32 bytes each
+// (byte (l, col) at ((col / 32) len + l) 32 + col % 32), so the table fit reads each panel as one contiguous run.
 template <int E, int M>
 struct OutCodes {
+  static constexpr bool kPanels = true;
   uint8_t* P;
   float* X;
   int* status;
+  int64_t len;
   bool bad_code = false;
   template <bool FINITE = false>
   __device__ __forceinline__ void codes(int64_t idx, float4 v) {
@@ -261,12 +277,12 @@ struct OutCodes {
       c2 = ocp_code_finite<E, M>(v.z);
       c3 = ocp_code_finite<E, M>(v.w);
     } else {
-      c0 = ocp_code<E, M>(v.x, bad_code);
-      c1 = ocp_code<E, M>(v.y, bad_code);
-      c2 = ocp_code<E, M>(v.z, bad_code);
-      c3 = ocp_code<E, M>(v.w, bad_code);
+      c0 = lut_code<E, M>(v.x, bad_code);
+      c1 = lut_code<E, M>(v.y, bad_code);
+      c2 = lut_code<E, M>(v.z, bad_code);
+      c3 = lut_code<E, M>(v.w, bad_code);
     }
-    __stcs(reinterpret_cast<unsigned int*>(P + idx), c0 | (c1 << 8) | (c2 << 16) | (c3 << 24));
+    *reinterpret_cast<unsigned int*>(P + idx) = c0 | (c1 << 8) | (c2 << 16) | (c3 << 24);
   }
   __device__ __forceinline__ void scale(int64_t idx, float x) { X[idx] = x; }
   __device__ __forceinline__ void finish() {
@@ -298,6 +314,14 @@ __device__ __forceinline__ TileAt tile_at(int64_t tile, uint32_t ctiles, uint32_
   return t;
 }
 
+// the store of the 4 codes at (l, col) .. (l, col + 3) of a blocks-along-rows tile, at their element index idx or, for an
+// output stored by 32-column panels, at their place in the panel
+template <bool FINITE, class Out>
+__device__ __forceinline__ void put_codes(Out& out, int64_t l, int64_t col, int64_t idx, float4 v) {
+  if constexpr (Out::kPanels) out.template codes<FINITE>(((col >> 5) * out.len + l) * 32 + (col & 31), v);
+  else out.template codes<FINITE>(idx, v);
+}
+
 // (2) for a clean tile: every thread quantizes TR / RPI float4 (float4 q = tid + NT i: row q / C4, column q % C4)
 template <int FAM, int E, int M, bool COLS, int BS, int MODE, bool VIA, class Out>
 __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out& out, const TileAt& at,
@@ -319,7 +343,7 @@ __device__ __forceinline__ void pass_clean(const float* T, const float* s_r, Out
     v.w = element_clean<FAM, E, M, MODE, VIA>(__fmul_rn(v.w, rs.w), via_e, via_m);
     if (COLS) {
       const int64_t l = at.b * BS + row, col = at.ct * TC + c4 * 4;
-      if (l < len && col < inner) out.template codes<true>((at.o * len + l) * inner + col, v);
+      if (l < len && col < inner) put_codes<true>(out, l, col, (at.o * len + l) * inner + col, v);
     } else {
       const int64_t grow = at.rest * TR + row, col = at.ct * TC + c4 * 4;
       if (grow < outer && col < len) out.template codes<true>(grow * len + col, v);
@@ -339,7 +363,7 @@ __device__ __forceinline__ void lose_tile(Out& out, const TileAt& at, int64_t ou
     const int row = tid / C4 + RPI * i;
     if (COLS) {
       const int64_t l = at.b * BS + row, col = at.ct * TC + c4 * 4;
-      if (l < len && col < inner) out.codes((at.o * len + l) * inner + col, q4);
+      if (l < len && col < inner) put_codes<false>(out, l, col, (at.o * len + l) * inner + col, q4);
     } else {
       const int64_t grow = at.rest * TR + row, col = at.ct * TC + c4 * 4;
       if (grow < outer && col < len) out.codes(grow * len + col, q4);
@@ -502,7 +526,7 @@ __global__ void __launch_bounds__(NT) k_quant_tma(const __grid_constant__ CUtens
     v.w = element<FAM, E, M>(divide<FAM>(v.w, xs.w, rs.w), prm);
     if (COLS) {
       const int64_t l = at.b * BS + row, col = ct * TC + c4 * 4;
-      if (l < len && col < inner) out.codes((at.o * len + l) * inner + col, v);
+      if (l < len && col < inner) put_codes<false>(out, l, col, (at.o * len + l) * inner + col, v);
     } else {
       const int64_t grow = rest * TR + row, col = ct * TC + c4 * 4;
       if (grow < outer && col < len) out.codes(grow * len + col, v);
@@ -559,7 +583,9 @@ int launch_dest(const CUtensorMap& map, bool cols, const Dest& d, int64_t outer,
   if (d.multi != nullptr) return launch<FAM, E, M, 32>(map, cols, *d.multi, outer, len, inner, prm, st);
   if (d.codes8) {
     if constexpr (FAM == MXQ_FAMILY_MXGEMMINI && E + M >= 5)
-      return launch<FAM, E, M, 32>(map, cols, OutCodes<E, M>{d.Pc, d.X, d.status}, outer, len, inner, prm, st);
+      return cols && outer == 1 ? launch<FAM, E, M, 32>(map, cols, OutCodes<E, M>{d.Pc, d.X, d.status, len}, outer, len,
+                                                        inner, prm, st)
+                                : MXQ_ERR_UNSUPPORTED;
     else
       return MXQ_ERR_UNSUPPORTED;
   }
@@ -646,8 +672,9 @@ int quantize_tma_packed(const float* V, uint8_t* Pc, uint8_t* Xc, int* status, i
 }  // namespace mxq
 
 namespace mxq {
-// block.lut's codes: block.mxgemmini (no via) of V as byte codes (OCP bit patterns) and float32 scales; status bit 1
-// for a code the format cannot hold. MXQ_ERR_UNSUPPORTED for layouts the TMA kernel does not take.
+// block.lut's codes: block.mxgemmini (no via) of V (blocks along rows: outer 1, len rows, inner columns) as byte
+// codes stored by 32-column panels (OutCodes) and float32 scales; status bit 1 for a code the format cannot hold.
+// MXQ_ERR_UNSUPPORTED for layouts the TMA kernel does not take.
 int quantize_tma_codes(const float* V, uint8_t* codes, float* X, int* status, int64_t outer, int64_t len,
                        int64_t inner, const mxq_quant_spec& s, cudaStream_t st) {
   if (s.family != MXQ_FAMILY_MXGEMMINI || s.via_e != 0) return MXQ_ERR_UNSUPPORTED;

@@ -59,3 +59,27 @@ def test_lut_no_rows(oracle):
         Pl, X = prod.lut_block_quantize(V, fmt, 0, 32, "rne", 2.0 ** -23, 1, 50)
         Plo, Xo = oracle.lut_block_quantize(V, fmt, 0, 32, "rne", 2.0 ** -23, 1, 50)
         assert Pl.shape == Plo.shape and X.shape == Xo.shape
+
+
+@pytest.mark.parametrize("fmt", ["MXFP6_E3M2", "MXFP6_E2M3", "MXFP8_E4M3", "MXFP8_E5M2"])
+def test_lut_block_bad_values(oracle, fmt):
+    """block.lut of an operand holding a NaN or an Inf: the oracle refuses it (a code that is not a value of the
+    format reaches the table fit) and so does the product, with the same ValueError, for every group size and both
+    axes, with the bad value in one panel of several; the next call on clean data is still bit for bit."""
+    rng = np.random.default_rng(7)
+    K, n = 256, 160
+    V = (rng.standard_normal((K, n)) * 2.0 ** rng.uniform(-4, 4, (1, n))).astype(np.float32)
+    for bad in (np.nan, np.inf):
+        Vb = V.copy()
+        Vb[100, 70] = bad
+        for G in (0, 1, 3):
+            for axis in (0, 1):
+                with pytest.raises(ValueError):
+                    oracle.lut_block_quantize(Vb, fmt, axis, 32, "rne", 2.0 ** -23, G, 50)
+                with pytest.raises(ValueError, match="not a"):
+                    prod.lut_block_quantize(Vb, fmt, axis, 32, "rne", 2.0 ** -23, G, 50)
+    for G in (1, 3):
+        P, X = prod.lut_block_quantize(V, fmt, 0, 32, "rne", 2.0 ** -23, G, 50)
+        Po, Xo = oracle.lut_block_quantize(V, fmt, 0, 32, "rne", 2.0 ** -23, G, 50)
+        assert_bits(P, Po, f"block.lut {fmt} G{G} after a refused call")
+        assert_bits(X, Xo, f"block.lut X {fmt} G{G} after a refused call")
