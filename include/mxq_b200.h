@@ -7,8 +7,9 @@
  *   - the return value is MXQ_OK (0) or an MXQ_ERR_* code; mxq_last_error() returns this thread's message;
  *   - kernels never trap on data: NaN and Inf are values, and results follow the reference's rules for them.
  * Thread safety: the library's mutable global state is the per-thread error message, caches filled once under a
- * lock (per-device SM counts, the driver's tensor-map entry point, the static scratch's per-device address), and the
- * wait-status word (mxq_wait_status_word), which kernels only increment.
+ * lock (per-device SM counts, the driver's tensor-map entry point, the static scratch's per-device address, each LUT
+ * format's tables in device memory: uploaded by a synchronous copy at the first LUT call on a device, and again when
+ * that device's context has changed), and the wait-status word (mxq_wait_status_word), which kernels only increment.
  */
 #ifndef MXQ_B200_H
 #define MXQ_B200_H

@@ -30,6 +30,9 @@ int quantize_tma_codes(const float* V, uint8_t* codes, float* X, int* status, in
                        int64_t inner, const mxq_quant_spec& s, cudaStream_t st);
 int lut_tables_codes_lookup(const uint8_t* codes, float* T, float* cmap, float* out, int64_t K, int64_t n,
                             int32_t group, int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream);
+int block_lut_fused(const float* V, float* out, float* X, float* T, float* cmap, uint8_t* codesT, int64_t K, int64_t n,
+                    int32_t group, int32_t max_iters, int32_t e, int32_t m, int32_t rounding, float scale_floor,
+                    int32_t* status, void* stream);
 }  // namespace mxq
 
 namespace {
@@ -80,11 +83,29 @@ int mxq_block_lut_quantize(const float* V, float* P_lut, float* X, int64_t rows,
               "block.lut: the workspace needs %lld bytes, 256-byte aligned (got %lld)", (long long)need,
               (long long)workspace_bytes);
   const bool ax0 = axis % 2 == 0;
-  // Axis 0 (the K x n operand is V's own row-major layout): the codes as bytes (their OCP bit patterns) from the fused
-  // quantizer, then one launch that fits the tables from the bytes, leaves each group's code -> entry map and reads
-  // one map entry per element. The workspace holds the bytes, the tables and the maps (less than the float codes of
-  // the general path below).
-  if (ax0 && rows * cols > 0 && cols % 4 == 0 && (uintptr_t)V % 16 == 0 && (uintptr_t)P_lut % 16 == 0) {
+  // Axis 0 (the K x n operand is V's own row-major layout) with blocks of 32: one launch that quantizes V, fits the
+  // tables and writes the looked-up values (block_lut_fused: rows a multiple of 32, groups of at most 32 columns);
+  // else the codes as bytes (their OCP bit patterns) from the fused quantizer, then one launch that fits the tables
+  // from the bytes, leaves each group's code -> entry map and reads one map entry per element. The workspace holds
+  // the bytes, the tables and the maps (less than the float codes of the general path below).
+  if (ax0 && block == 32 && rows * cols > 0) {
+    const int64_t ng = (cols + ((int64_t)1 << group) - 1) >> group;
+    const int64_t nc = (int64_t)1 << (1 + spec->e + spec->m);
+    uint8_t* codesT = static_cast<uint8_t*>(workspace);        // column-major: cols x rows
+    float* Tb = reinterpret_cast<float*>(codesT + round_up(rows * cols));
+    float* cmap = Tb + round_up(ng * kTableWidth * (int64_t)sizeof(float)) / (int64_t)sizeof(float);
+    const int64_t used = round_up(rows * cols) + round_up(ng * kTableWidth * (int64_t)sizeof(float)) +
+                         ng * nc * (int64_t)sizeof(float);
+    if (used <= workspace_bytes) {
+      cudaStream_t st = as_stream(stream);
+      if (int r = check_cuda(cudaMemsetAsync(status, 0, sizeof(int32_t), st), "block.lut")) return r;
+      const int q = mxq::block_lut_fused(V, P_lut, X, Tb, cmap, codesT, rows, cols, group, max_iters, spec->e, spec->m,
+                                         spec->rounding, spec->scale_floor, status, stream);
+      if (q != MXQ_ERR_UNSUPPORTED) return q;
+    }
+  }
+  if (ax0 && block == 32 && rows * cols > 0 && cols % 4 == 0 && (uintptr_t)V % 16 == 0 &&
+      (uintptr_t)P_lut % 16 == 0) {
     const int64_t ng = (cols + ((int64_t)1 << group) - 1) >> group;
     const int64_t nc = (int64_t)1 << (1 + spec->e + spec->m);
     uint8_t* codes = static_cast<uint8_t*>(workspace);         // by 32-column panels: rows x (cols rounded up to 32)

@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "numerics.cuh"
+#include "quant_elem.cuh"
 
 using namespace mxq;
 namespace cg = cooperative_groups;
@@ -180,6 +181,16 @@ struct TableParams {                           // by value: what the tables kern
   const DevTables* dt;
 };
 
+// block.lut in one launch (the kernel's fused mode): V's block.mxgemmini quantization (blocks of 32 along rows) is
+// done in the kernel, its scales written to X and its codes (OCP bytes) to codesT, column-major (byte (k, j) at
+// j K + k), for the kernel's own lookup
+struct FusedArgs {
+  float* X;
+  uint8_t* codesT;
+  float scale_floor;
+  int rounding;
+};
+
 constexpr int NW = NT / 32;                    // warps per CTA
 constexpr double MIN_GAP = 1.16415321826934814453125e-10;   // 2^-33: centres this far apart never tie by rounding
 
@@ -223,9 +234,9 @@ __device__ __forceinline__ double dedupe_lanes(double v, double* scratch) {
 }
 
 // The warps of a CTA that fit a group: group gl of a cs-CTA cluster's gpc is fitted by CTA gl % cs, warp gl / cs
-__host__ __device__ __forceinline__ int fit_warps(int gpc, int cs) {
+__host__ __device__ __forceinline__ int fit_warps(int gpc, int cs, int nw) {
   const int w = (gpc + cs - 1) / cs;
-  return w < NW ? w : NW;
+  return w < nw ? w : nw;
 }
 
 // The tables (kmeans.py:46-122). A cluster of cs CTAs per panel of gpc column groups: (1) the panel's codes
@@ -242,55 +253,60 @@ __host__ __device__ __forceinline__ int fit_warps(int gpc, int cs) {
 // centres are at least 2^-33 apart (distances below 2^17 then never round to a tie across a centre); a pass that
 // finds two closer centres assigns code by code instead.
 // TIn: float codes at P[k sk + j sj], or (block.lut) code bytes stored by 32-column panels, byte (k, j) at
-// ((j / 32) K + k) 32 + j % 32 (sk, sj unused)
-template <typename TIn>
-__global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P, int64_t K, int64_t n, int64_t sk,
-                                                   int64_t sj, int G, int gpc, int max_iters, int priv_ok,
+// ((j / 32) K + k) 32 + j % 32 (sk, sj unused). QM >= 0: the fused block.lut (FE, FM the element format, QM the
+// rounding mode of its clean blocks): P is V (row-major K x n, K a multiple of 32, panels of at most 32 columns), and
+// the codes are made here (FusedArgs)
+template <typename TIn, int FE = 0, int FM = 0, int QM = -1, int NTH = NT>
+__global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __restrict__ P, int64_t K, int64_t n,
+                                                   int64_t sk, int64_t sj, int G, int gpc, int max_iters, int priv_ok,
                                                    const __grid_constant__ TableParams tp, float* __restrict__ T,
                                                    int* __restrict__ status, float* __restrict__ cmap,
-                                                   float* __restrict__ out) {
+                                                   float* __restrict__ out, const FusedArgs fa) {
+  constexpr int NTK = NTH, NWK = NTH / 32;                  // threads and warps of a CTA
   // dynamic shared memory: counts [gpc][nv | 1] (this CTA's rows; then merged, its own groups), then the fits'
   // prefix sums [2][nfw][nv + 1] doubles for the nfw warps that fit a group; with `out`, the panel's code -> entry
   // maps [gpc][ncodes + 1] over the same bytes once the fits are done
-  constexpr bool BYTES = sizeof(TIn) == 1;
+  constexpr bool FUSED = QM >= 0;
+  constexpr bool BYTES = sizeof(TIn) == 1 || FUSED;          // codes counted and looked up as OCP bytes
   extern __shared__ int counts[];
-  __shared__ double scratch[NW][LUT], fsum[NW][LUT], fw[NW][LUT];
+  __shared__ double scratch[NWK][LUT], fsum[NWK][LUT], fw[NWK][LUT];
   __shared__ __align__(16) float sgrid[MAXV];                // the format's tables, read with per-lane indices
   __shared__ __align__(16) float ssafe[MAXV];
   __shared__ __align__(16) float svals[MAXV];
   __shared__ __align__(16) uint8_t sorder[MAXV];
-  __shared__ float stab[NW][LUT];                            // each fitting warp's finished table
-  __shared__ unsigned char member[NW][MAXV];
+  __shared__ float stab[NWK][LUT];                            // each fitting warp's finished table
+  __shared__ unsigned char member[NWK][MAXV];
   __shared__ __align__(16) uint8_t sbin[BYTES ? MAXV : KEYS];
   __shared__ int bad;
   cg::cluster_group cluster = cg::this_cluster();
   const int cs = (int)cluster.num_blocks(), rank = (int)cluster.block_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nv = tp.nv;
-  const int nfw = fit_warps(gpc, cs);
+  const int nfw = fit_warps(gpc, cs, NWK);
   const unsigned lt = (1u << lane) - 1u;
   const int64_t ng = (n + ((int64_t)1 << G) - 1) >> G;
   const int64_t g0 = (int64_t)(blockIdx.x / cs) * gpc;       // the cluster's panel of groups
   const int64_t j0 = g0 << G, jend = (g0 + gpc) << G, j1 = jend < n ? jend : n;
   const int64_t W = j1 - j0;
-  const int64_t kper = (K + cs - 1) / cs;                    // this CTA's rows of the panel
+  const int64_t kper = FUSED ? ((K / 32 + cs - 1) / cs) * 32 : (K + cs - 1) / cs;   // this CTA's rows of the panel
+                                                             // (fused: whole blocks of 32)
   const int64_t kbeg = (int64_t)rank * kper < K ? (int64_t)rank * kper : K;
   const int64_t kend = kbeg + kper < K ? kbeg + kper : K;
   const int nvp = nv | 1;                                   // a group's histogram row, odd: a bin of 32 groups hits 32 banks
   double* const pw = reinterpret_cast<double*>(counts + ((gpc * nvp + 3) & ~3));   // [nfw][nv + 1]
   double* const pwx = pw + nfw * (nv + 1);
-  for (int i = tid; i < gpc * nvp; i += NT) counts[i] = 0;
+  for (int i = tid; i < gpc * nvp; i += NTK) counts[i] = 0;
   // the tables the fits index per lane, into shared memory once
   {
     const DevTables* dt = tp.dt;
-    for (int i = tid; i < MAXV / 4; i += NT) {
+    for (int i = tid; i < MAXV / 4; i += NTK) {
       reinterpret_cast<float4*>(sgrid)[i] = __ldg(reinterpret_cast<const float4*>(dt->grid) + i);
       reinterpret_cast<float4*>(ssafe)[i] = __ldg(reinterpret_cast<const float4*>(dt->safe) + i);
       if (cmap != nullptr) reinterpret_cast<float4*>(svals)[i] = __ldg(reinterpret_cast<const float4*>(dt->vals) + i);
     }
-    for (int i = tid; i < MAXV / 16; i += NT)
+    for (int i = tid; i < MAXV / 16; i += NTK)
       reinterpret_cast<uint4*>(sorder)[i] = __ldg(reinterpret_cast<const uint4*>(dt->order) + i);
     const uint4* bsrc = reinterpret_cast<const uint4*>(BYTES ? dt->cbin : dt->bin);   // a code's grid rank
-    for (int i = tid; i < (BYTES ? MAXV : KEYS) / 16; i += NT) reinterpret_cast<uint4*>(sbin)[i] = __ldg(bsrc + i);
+    for (int i = tid; i < (BYTES ? MAXV : KEYS) / 16; i += NTK) reinterpret_cast<uint4*>(sbin)[i] = __ldg(bsrc + i);
   }
   if (tid == 0) bad = 0;
   __syncthreads();
@@ -302,6 +318,93 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
   bool mybad = false;
   constexpr int BATCH = 8;                                  // loads in flight per thread
   constexpr int PBATCH = 8;                                 // the pair path's
+  // the panel's first element and row stride (a panel never spans two 32-column runs of code bytes), and any
+  // element's place
+  const TIn* const pb = BYTES ? P + j0 * K : P + j0 * sj;
+  const int64_t rs = BYTES ? 32 : sk, cst = BYTES ? 1 : sj;
+  auto at = [&](int64_t k, int64_t j) -> int64_t { return BYTES ? ((j >> 5) * K + k) * 32 + (j & 31) : k * sk + j * sj; };
+  const bool pairs = cst == 1 && W <= 32 && W % 2 == 0 && rs % 2 == 0 && ((uintptr_t)pb) % (2 * sizeof(TIn)) == 0;
+  if constexpr (FUSED) {
+    // A. block.mxgemmini of the CTA's rows of the panel (block.py, mxgemmini.py): lane l owns column j0 + l, warp w
+    // blocks w, w + 8, ... of 32 rows. A lane loads its block's 32 values (a warp load is one 128-byte row
+    // segment), takes the block max, the scale (X) and its reciprocal, quantizes the 32 values -- the short step when
+    // the block is finite with a power-of-two scale, else the general one (the TMA quantizer's two element steps) --
+    // and writes the 32 code bytes as two 16-byte stores to its column of codesT. Each code is counted as it is
+    // made: 6-bit codes in the thread's own 16-bit counters (private_counts), 8-bit ones by shared atomics.
+    const bool live = lane < W;
+    const int64_t j = j0 + lane;
+    const int grow = (lane >> G) * nvp;
+    uint16_t* const mine = reinterpret_cast<uint16_t*>(pw) + tid;   // [64][NTK]
+    const bool six = FE + FM == 5;
+    if (six) {
+      for (int i = tid; i < 64 * NTK / 8; i += NTK) reinterpret_cast<uint4*>(mine - tid)[i] = make_uint4(0u, 0u, 0u, 0u);
+      __syncthreads();
+    }
+    uint32_t mxb = 0;                                        // 8-bit: the largest bin seen (0xFF: no code)
+    auto tally = [&](uint32_t c) {
+      if (six) {
+        mine[c * NTK] += 1;
+      } else {
+        const uint32_t bn = sbin[c];
+        mxb = max(mxb, bn);
+        atomicAdd(&counts[grow + (int)bn], 1);
+      }
+    };
+    const int64_t b0 = kbeg / 32, b1 = kend / 32;
+    for (int64_t b = b0 + warp; b < b1 && live; b += NWK) {
+      float v[32];
+      const float* src = reinterpret_cast<const float*>(P) + b * 32 * n + j;
+#pragma unroll
+      for (int i = 0; i < 32; i++) v[i] = __ldcs(src + i * n);
+      uint32_t mbits = 0u;                                   // max |v| as bits: a NaN pattern tops every number
+#pragma unroll
+      for (int i = 0; i < 32; i++) mbits = max(mbits, f2u(v[i]) & 0x7fffffffu);
+      const bool nan = mbits > 0x7f800000u;
+      const float x = scale_mxquant(nan ? qnan_f() : u2f(mbits), fa.scale_floor);
+      const float r = reciprocal_of<MXQ_FAMILY_MXGEMMINI>(x, nan);
+      fa.X[b * n + j] = x;
+      uint32_t w[8];
+      if (mbits < 0x7f800000u && r != 0.0f) {
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          const uint32_t c = code_clean<FE, FM, QM>(__fmul_rn(v[i], r));
+          tally(c);
+          w[i >> 2] = (i & 3) ? (w[i >> 2] | (c << (8 * (i & 3)))) : c;
+        }
+      } else {
+        bool nocode = false;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+          const float z = r != 0.0f ? __fmul_rn(v[i], r) : div_rn(v[i], x);
+          const uint32_t c = lut_code<FE, FM>(ocp_grid<FE, FM>(z, fa.rounding), nocode);
+          tally(c);
+          w[i >> 2] = (i & 3) ? (w[i >> 2] | (c << (8 * (i & 3)))) : c;
+        }
+        if (nocode) mybad = true;
+      }
+      uint4* dst = reinterpret_cast<uint4*>(fa.codesT + j * K + b * 32);
+      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+    if (!six && mxb == 0xFFu) mybad = true;
+    if (six) {
+      __syncthreads();
+      // into the CTA's histogram: warp w sums code s over the 8 warps' counters, then over the 2^G lanes (columns)
+      // of a group, and the group's first lane adds the total to the code's bin
+      const int sh = G < 5 ? G : 5;
+      for (int sl = warp; sl < 64; sl += NWK) {
+        int sum = 0;
+#pragma unroll
+        for (int q = 0; q < NWK; q++) sum += mine[sl * NTK - tid + q * 32 + lane];
+        for (int o = 1; o < (1 << sh); o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if ((lane & ((1 << sh) - 1)) == 0 && lane < W && sum > 0) {
+          const uint32_t bin = sbin[sl];
+          if (bin == 0xFFu) mybad = true;
+          else atomicAdd(&counts[(lane >> sh) * nvp + (int)bin], sum);
+        }
+      }
+    }
+  } else {
   // a code's grid rank from its bit pattern: the key (sign, exponent, top m fraction bits) through the table; any
   // other fraction bit set, or a key that names no code (NaN, Inf, off-grid), is not a code
   // (code bytes: the byte's rank through its own table)
@@ -320,22 +423,16 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
     else atomicAdd(&counts[gc * nvp + (int)b], 1);
   };
   using V2 = typename std::conditional<BYTES, uchar2, float2>::type;
-  // the panel's first element and row stride (a panel never spans two 32-column runs of code bytes), and any
-  // element's place
-  const TIn* const pb = BYTES ? P + j0 * K : P + j0 * sj;
-  const int64_t rs = BYTES ? 32 : sk, cst = BYTES ? 1 : sj;
-  auto at = [&](int64_t k, int64_t j) -> int64_t { return BYTES ? ((j >> 5) * K + k) * 32 + (j & 31) : k * sk + j * sj; };
-  const bool pairs = cst == 1 && W <= 32 && W % 2 == 0 && rs % 2 == 0 && ((uintptr_t)pb) % (2 * sizeof(TIn)) == 0;
   bool counted = false;
   if constexpr (BYTES) {
     if (pairs && priv_ok && G >= 1 && tp.ncodes <= 64 && Kc <= 16 * 32767) {
-      // 6-bit codes: every thread counts its bytes in its own column of [64][NT] 16-bit counters (a thread's column
+      // 6-bit codes: every thread counts its bytes in its own column of [64][NTK] 16-bit counters (a thread's column
       // pair lies in one group at G >= 1, and it sees at most 2 ceil(Kc / 16) codes) with plain shared loads and
       // stores: no atomics, and the 32 counters of one code of a warp are 64 consecutive bytes, so lanes never meet
       // in a bank whatever their codes. A code past the format's (a byte >= ncodes) is remembered by the largest
       // byte seen and counted, masked, where it cannot hurt: the whole panel is refused.
       uint16_t* const priv = reinterpret_cast<uint16_t*>(pw);
-      for (int i = tid; i < 64 * NT / 8; i += NT) reinterpret_cast<uint4*>(priv)[i] = make_uint4(0u, 0u, 0u, 0u);
+      for (int i = tid; i < 64 * NTK / 8; i += NTK) reinterpret_cast<uint4*>(priv)[i] = make_uint4(0u, 0u, 0u, 0u);
       __syncthreads();
       const int c2 = lane & 15, ro = lane >> 4;
       uint32_t mx = 0;
@@ -349,8 +446,8 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
         auto add = [&](uint32_t v) {
           const uint32_t a = v & 0xffu, b = v >> 8;
           mx = max(mx, max(a, b));
-          mine[(a & 63u) * NT] += 1;
-          mine[(b & 63u) * NT] += 1;
+          mine[(a & 63u) * NTK] += 1;
+          mine[(b & 63u) * NTK] += 1;
         };
         int64_t r = 0;
         for (; r + PB <= nr; r += PB) {
@@ -368,10 +465,10 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
       // into the CTA's histogram: warp w sums code s over the 8 warps' counters, then over the lanes of a group (its
       // two rows and its 2^(G-1) column pairs), and one lane adds the total to the group's bin
       const int sh = G - 1 < 4 ? G - 1 : 4;
-      for (int sl = warp; sl < tp.ncodes; sl += NW) {
+      for (int sl = warp; sl < tp.ncodes; sl += NWK) {
         int sum = 0;
 #pragma unroll
-        for (int j = 0; j < NW; j++) sum += priv[sl * NT + j * 32 + lane];
+        for (int j = 0; j < NWK; j++) sum += priv[sl * NTK + j * 32 + lane];
         sum += __shfl_xor_sync(0xffffffffu, sum, 16);
         for (int o = 1; o < (1 << sh); o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
         if (lane < 16 && (c2 & ((1 << sh) - 1)) == 0 && 2 * c2 < W && sum > 0) {
@@ -429,7 +526,7 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
     if (2 * c2 < W) {
       const V2* src = reinterpret_cast<const V2*>(pb) + c2;
       const int ga = (2 * c2) >> G, gb = (2 * c2 + 1) >> G;
-      const int64_t step = 2 * NW;
+      const int64_t step = 2 * NWK;
       for (int64_t k0 = kbeg + 2 * warp + ro; k0 < kend; k0 += step * PBATCH) {
         V2 v[PBATCH];
 #pragma unroll
@@ -443,10 +540,10 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
         }
       }
     }
-  } else if (!BYTES && sj == 1 && W % 4 == 0 && W <= 4 * NT && sk % 4 == 0 && ((uintptr_t)(P + j0)) % 16 == 0) {
+  } else if (!BYTES && sj == 1 && W % 4 == 0 && W <= 4 * NTK && sk % 4 == 0 && ((uintptr_t)(P + j0)) % 16 == 0) {
     // rows of the panel as float4: thread (row r, quad q) of rows_per_pass rows at a time, pointers advanced by
     // whole rows (no index arithmetic per element)
-    const int qpr = (int)(W / 4), rows_per_pass = NT / qpr, r = tid / qpr, q = tid - r * qpr;
+    const int qpr = (int)(W / 4), rows_per_pass = NTK / qpr, r = tid / qpr, q = tid - r * qpr;
     if (r < rows_per_pass) {
       const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(P) + j0) + q;
       int gc[4];
@@ -470,15 +567,15 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
     }
   } else if (total > 0) {
   // element e = (kfast ? jj * Kc + k : k * W + jj) walked without a division per element: the position (major,
-  // minor) advances by NT elements as (NT / R, NT % R) with R the minor extent, plus a carry
-  const int64_t R = kfast ? Kc : W, dmaj = NT / R, dmin = NT % R;
+  // minor) advances by NTK elements as (NTK / R, NTK % R) with R the minor extent, plus a carry
+  const int64_t R = kfast ? Kc : W, dmaj = NTK / R, dmin = NTK % R;
   int64_t maj = tid / R, mnr = tid % R;
-  for (int64_t e0 = tid; e0 < total; e0 += (int64_t)NT * BATCH) {
+  for (int64_t e0 = tid; e0 < total; e0 += (int64_t)NTK * BATCH) {
     TIn v[BATCH];
     int gcol[BATCH];
 #pragma unroll
     for (int u = 0; u < BATCH; u++) {
-      const int64_t e = e0 + (int64_t)u * NT;
+      const int64_t e = e0 + (int64_t)u * NTK;
       const int64_t k = kfast ? mnr : maj, jj = kfast ? maj : mnr;
       gcol[u] = e < total ? (int)(jj >> G) : -1;
       v[u] = e < total ? P[at(kbeg + k, j0 + jj)] : TIn{};
@@ -494,6 +591,7 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
       if (gcol[u] >= 0) count(v[u], gcol[u]);
   }
   }
+  }
   if (mybad) bad = 1;
   // the cluster's CTAs meet: every histogram of the panel is complete (cluster barriers order shared memory across
   // the cluster); CTA r merges groups r, r + cs, ... from all of them into its own rows, then they meet again so no
@@ -505,7 +603,7 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
   for (int q = 0; q < cs; q++) anybad |= *cluster.map_shared_rank(&bad, q);
   if (cs > 1) {
     const int nown = (gpc - rank + cs - 1) / cs;             // this CTA's groups: rank, rank + cs, ...
-    for (int i = tid; i < nown * nv; i += NT) {
+    for (int i = tid; i < nown * nv; i += NTK) {
       const int gi = i / nv, b = i - gi * nv;
       const int idx = (rank + cs * gi) * nvp + b;
       int part[8];                                           // cs <= 8: every remote read in flight at once
@@ -520,7 +618,7 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
   cluster.sync();
   if (anybad) return;
 
-  for (int gl = rank + cs * warp; gl < gpc; gl += cs * NW) {
+  for (int gl = rank + cs * warp; gl < gpc; gl += cs * NWK) {
     const int64_t g = g0 + gl;
     if (g >= ng) break;
     const int* cnt = counts + gl * nvp;
@@ -749,12 +847,26 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
   float* const smap = reinterpret_cast<float*>(counts);      // [groups of the panel][ncodes + 1]
   const int nc = tp.ncodes, ncp = nc + 1;
   const int ngp = (int)((g0 + gpc < ng ? g0 + gpc : ng) - g0);
-  for (int i = tid; i < ngp * nc; i += NT) {
+  for (int i = tid; i < ngp * nc; i += NTK) {
     const int gi = i / nc;
     smap[i + gi] = __ldcg(cmap + g0 * nc + i);
   }
   __syncthreads();
-  if (pairs && W % 4 == 0 && rs % 4 == 0 && ((uintptr_t)pb) % 4 == 0 && n % 4 == 0 &&
+  if constexpr (FUSED) {
+    // lane l: column j0 + l, its codes of each of the warp's blocks (two 16-byte loads, from L2), 32 coalesced rows
+    if (lane < W) {
+      const int64_t j = j0 + lane;
+      const float* m = smap + (lane >> G) * ncp;
+      for (int64_t b = kbeg / 32 + warp; b < kend / 32; b += NWK) {
+        const uint4* src = reinterpret_cast<const uint4*>(fa.codesT + j * K + b * 32);
+        const uint4 c0 = __ldcs(src), c1 = __ldcs(src + 1);
+        const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        float* dst = out + b * 32 * n + j;
+#pragma unroll
+        for (int i = 0; i < 32; i++) __stcs(dst + i * n, m[(w[i >> 2] >> (8 * (i & 3))) & 0xffu]);
+      }
+    }
+  } else if (pairs && W % 4 == 0 && rs % 4 == 0 && ((uintptr_t)pb) % 4 == 0 && n % 4 == 0 &&
       ((uintptr_t)(out + j0)) % 16 == 0) {
     // 4 codes (one 4-byte load, the histogram's quads) into one float4 store per lane
     const int q = lane & 7, ro = lane >> 3;
@@ -785,7 +897,7 @@ __global__ void __launch_bounds__(NT, 4) k_lut_tables(const TIn* __restrict__ P,
       for (; r < nr; r++, src += rstep, dst += ostep) put(__ldcs(src), dst);
     }
   } else {
-    for (int64_t e = tid; e < total; e += NT) {              // element (k, jj) of the CTA's rows
+    for (int64_t e = tid; e < total; e += NTK) {              // element (k, jj) of the CTA's rows
       const int64_t k = kbeg + e / W, jj = e % W;
       out[k * n + j0 + jj] = smap[(int)(jj >> G) * ncp + (int)P[at(k, j0 + jj)]];
     }
@@ -1096,10 +1208,13 @@ int device_tables(int e, int m, const DevTables** out) {
   return MXQ_OK;
 }
 
-template <typename TIn>
+template <typename TIn, int FE = 0, int FM = 0, int QM = -1>
 int launch_tables(const TIn* P, float* T, int64_t K, int64_t n, int64_t sk, int64_t sj, int32_t group,
                    int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream, bool zero_status = true,
-                   float* cmap = nullptr, float* out = nullptr) {
+                   float* cmap = nullptr, float* out = nullptr, const FusedArgs& fa = FusedArgs{}) {
+  constexpr bool FUSED = QM >= 0;
+  constexpr int NTH = NT;
+  auto kernel = k_lut_tables<TIn, FE, FM, QM, NTH>;
   if (int r = fmt_slot_check(e, m, "tables")) return r;
   MXQ_REQUIRE(group >= 0 && group < 31, MXQ_ERR_VALUE, "mxq.lut: group %d must be a non-negative integer", group);
   MXQ_REQUIRE(max_iters >= 0, MXQ_ERR_VALUE, "mxq.lut: max_iters %d must be a non-negative integer", max_iters);
@@ -1122,31 +1237,33 @@ int launch_tables(const TIn* P, float* T, int64_t K, int64_t n, int64_t sk, int6
   tp.lowmask = (1u << (23 - m)) - 1u;
   if (int r = device_tables(e, m, &tp.dt)) return r;
   // A cluster of cs CTAs per panel of gpc groups (32 columns, or one group when a group is wider): the CTAs split
-  // the panel's rows for the histogram and its groups for the fits; cs (1..8) makes about three CTAs per SM.
+  // the panel's rows (fused: whole blocks of 32) for the histogram and its groups for the fits; cs (1..8) makes about
+  // three CTAs per SM. (Clusters of eight CTAs of 128 threads, eight to an SM, measured slower for the fused kernel:
+  // more registers spilled, and the eight-CTA clusters did not spread more evenly over the SMs.)
   const int gpc = group >= 5 ? 1 : (32 >> group);
   const int64_t panels = (ng + gpc - 1) / gpc;
   int cs = 1;
-  while (cs < 8 && panels * cs < 3 * (int64_t)sm_count() && 2 * cs <= K) cs *= 2;
+  while (cs < 8 && panels * cs < 3 * (int64_t)sm_count() && 2 * cs <= (FUSED ? K / 32 : K)) cs *= 2;
   // dynamic shared memory: the histograms, then one region for the fits' prefix sums, the private counters of
   // 6-bit code bytes, and (code bytes) room for the spare counts of bytes that are no code; the panel's maps over all
-  const int priv_ok = sizeof(TIn) == 1 && group >= 1 && f->ncodes <= 64;
-  size_t region = 2 * (size_t)fit_warps(gpc, cs) * (f->nv + 1) * sizeof(double);
-  if (priv_ok) region = std::max(region, (size_t)64 * NT * sizeof(uint16_t));
-  if (sizeof(TIn) == 1) region = std::max(region, (size_t)MAXV * sizeof(int));
+  const int priv_ok = (FUSED || (sizeof(TIn) == 1 && group >= 1)) && f->ncodes <= 64;
+  size_t region = 2 * (size_t)fit_warps(gpc, cs, NTH / 32) * (f->nv + 1) * sizeof(double);
+  if (priv_ok) region = std::max(region, (size_t)64 * NTH * sizeof(uint16_t));
+  if (FUSED || sizeof(TIn) == 1) region = std::max(region, (size_t)MAXV * sizeof(int));
   size_t smem = (((size_t)gpc * (f->nv | 1) + 3) & ~(size_t)3) * sizeof(int) + region;
   if (out != nullptr) smem = std::max(smem, (size_t)gpc * (f->ncodes + 1) * sizeof(float));
   // the histograms and the prefix sums (up to 33 KB) with the static tables (~10 KB) may pass the 48 KB default
-  if (int r = check_cuda(cudaFuncSetAttribute(k_lut_tables<TIn>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+  if (int r = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                          "lut.tables: shared memory attribute"))
     return r;
   // all of shared memory for the L1 / shared split, so four CTAs (with their static ~40 KB) fit on an SM
-  if (int r = check_cuda(cudaFuncSetAttribute(k_lut_tables<TIn>, cudaFuncAttributePreferredSharedMemoryCarveout, 100),
+  if (int r = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100),
                          "lut.tables: shared memory carveout"))
     return r;
   MXQ_REQUIRE(panels * cs < (1ll << 31), MXQ_ERR_UNSUPPORTED, "lut.tables: %lld column groups", (long long)ng);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(panels * cs));
-  cfg.blockDim = dim3(NT);
+  cfg.blockDim = dim3(NTH);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -1156,8 +1273,8 @@ int launch_tables(const TIn* P, float* T, int64_t K, int64_t n, int64_t sk, int6
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (int r = check_cuda(cudaLaunchKernelEx(&cfg, k_lut_tables<TIn>, P, K, n, sk, sj, (int)group, gpc, (int)max_iters,
-                                            priv_ok, tp, T, status, cmap, out),
+  if (int r = check_cuda(cudaLaunchKernelEx(&cfg, kernel, P, K, n, sk, sj, (int)group, gpc, (int)max_iters,
+                                            priv_ok, tp, T, status, cmap, out, fa),
                          "lut.tables"))
     return r;
   return MXQ_LAUNCH_CHECK("lut.tables");
@@ -1187,6 +1304,32 @@ namespace mxq {
 int lut_tables_codes_lookup(const uint8_t* codes, float* T, float* cmap, float* out, int64_t K, int64_t n,
                             int32_t group, int32_t max_iters, int32_t e, int32_t m, int32_t* status, void* stream) {
   return launch_tables(codes, T, K, n, n, 1, group, max_iters, e, m, status, stream, false, cmap, out);
+}
+
+// block.lut in one launch (axis 0, block.mxgemmini without via, blocks of 32): V (row-major K x n) quantized, its
+// scales to X, its code bytes to codesT (n x K), the tables to T, each group's code -> entry map to cmap and the
+// looked-up values to out. MXQ_ERR_UNSUPPORTED unless K is a multiple of 32, group <= 5 and the buffers are aligned
+// (status is not zeroed).
+int block_lut_fused(const float* V, float* out, float* X, float* T, float* cmap, uint8_t* codesT, int64_t K, int64_t n,
+                    int32_t group, int32_t max_iters, int32_t e, int32_t m, int32_t rounding, float scale_floor,
+                    int32_t* status, void* stream) {
+  if (K % 32 || K == 0 || n == 0 || group > 5 || rounding < 0 || rounding > 2 || (uintptr_t)codesT % 16 ||
+      K >= (1ll << 31) || n >= (1ll << 31))
+    return MXQ_ERR_UNSUPPORTED;
+  const FusedArgs fa{X, codesT, scale_floor, rounding};
+  auto go = [&](auto fe, auto fm) -> int {
+    constexpr int E = decltype(fe)::value, M = decltype(fm)::value;
+    if (rounding == 0)
+      return launch_tables<float, E, M, 0>(V, T, K, n, n, 1, group, max_iters, e, m, status, stream, false, cmap, out, fa);
+    if (rounding == 1)
+      return launch_tables<float, E, M, 1>(V, T, K, n, n, 1, group, max_iters, e, m, status, stream, false, cmap, out, fa);
+    return launch_tables<float, E, M, 2>(V, T, K, n, n, 1, group, max_iters, e, m, status, stream, false, cmap, out, fa);
+  };
+  if (e == 3 && m == 2) return go(std::integral_constant<int, 3>{}, std::integral_constant<int, 2>{});
+  if (e == 2 && m == 3) return go(std::integral_constant<int, 2>{}, std::integral_constant<int, 3>{});
+  if (e == 4 && m == 3) return go(std::integral_constant<int, 4>{}, std::integral_constant<int, 3>{});
+  if (e == 5 && m == 2) return go(std::integral_constant<int, 5>{}, std::integral_constant<int, 2>{});
+  return MXQ_ERR_UNSUPPORTED;
 }
 }  // namespace mxq
 

@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "numerics.cuh"
 #include "tma.cuh"
+#include "quant_elem.cuh"
 
 using namespace mxq;
 
@@ -37,17 +38,6 @@ struct TParams {
   int skip_load;           // 1 only in mxq_testing_wait_timeout: the load is never issued, so the wait runs out
 };
 
-template <int E, int M>
-struct Fmt {
-  static constexpr int BIAS = (1 << (E - 1)) - 1;
-  static constexpr float MAX_NORM = (E == 4 && M == 3) ? 448.0f
-                                    : (E == 5 && M == 2) ? 57344.0f
-                                    : (E == 3 && M == 2) ? 28.0f
-                                    : (E == 2 && M == 3) ? 7.5f
-                                                         : 6.0f;
-  static constexpr int EMAX = (E == 5) ? 15 : (E == 4) ? 8 : (E == 3) ? 4 : 2;   // microxcaling emax
-};
-
 // float_em._qtorch ties away (mxq/element_quant/float_em.py:64-84), constants folded
 template <int E, int M>
 __device__ __forceinline__ float qtorch_ties_away(float z) {
@@ -60,22 +50,6 @@ __device__ __forceinline__ float qtorch_ties_away(float z) {
   if (qm >= OVF) r = s | MAXMAG;
   if (qm < MINMAG) r = qm > MID ? (s | MINMAG) : 0u;
   return u2f(r);
-}
-
-// float_em._ocp (float_em.py:113-134): q_ocp_bits with the format's constants folded; the core for finite x
-template <int E, int M>
-__device__ __forceinline__ float ocp_grid_core(float x, int mode) {
-  constexpr uint32_t LO = (uint32_t)(128 - Fmt<E, M>::BIAS) << 23;     // biased emin in place
-  const uint32_t u = f2u(x), a = u & 0x7fffffffu;
-  const uint32_t e23 = (a & 0x7f800000u) > LO ? (a & 0x7f800000u) : LO;
-  const float k = round_nonneg(__fmul_rn(u2f(a), u2f(((uint32_t)(254 + M) << 23) - e23)), mode);
-  const float val = fminf(__fmul_rn(k, u2f(e23 - ((uint32_t)M << 23))), Fmt<E, M>::MAX_NORM);
-  const float r = u2f(f2u(val) | (u & 0x80000000u));
-  return a == 0u ? 0.0f : r;
-}
-template <int E, int M>
-__device__ __forceinline__ float ocp_grid(float x, int mode) {
-  return (f2u(x) & 0x7fffffffu) >= 0x7f800000u ? x : ocp_grid_core<E, M>(x, mode);
 }
 
 template <int FAM, int E, int M>
@@ -109,16 +83,6 @@ __device__ __forceinline__ float block_scale(float amax, const TParams& p) {
   if (p.placement == 0) return scale_ocp(amax, Fmt<E, M>::EMAX, p.scale_emax);
   if (p.placement == 1) return scale_ocp(amax, Fmt<E, M>::EMAX - 1, p.scale_emax);
   return scale_ocp_no_clip(amax, E, M, p.rounding, p.scale_emax);
-}
-
-// the reciprocal that turns v / X into an exact multiply, or 0 when the division must be a division (X not a
-// normal power of two, or -- for the qtorch family, whose codes see NaN sign bits -- a block holding a NaN)
-template <int FAM>
-__device__ __forceinline__ float reciprocal_of(float x, bool nan_block) {
-  const uint32_t u = f2u(x);
-  const bool pow2 = ((u & 0x807fffffu) == 0u && u >= 0x00800000u && u < 0x7f800000u) || u == 0x00400000u;
-  if (!pow2 || (FAM == MXQ_FAMILY_MXQUANT && nan_block)) return 0.0f;
-  return pow2f(-ilogb_f(x));
 }
 
 template <int FAM>
@@ -166,29 +130,6 @@ struct OutMulti {
   __device__ __forceinline__ void lost() {}                // the tile's NaN codes and scales say it
 };
 
-// an OCP element code's bit pattern (sign at bit E + M); `bad` set for what the format lacks (Inf, and NaN in FP6 /
-// FP4; E4M3 keeps NaN as S.1111.111, E5M2 Inf as S.11111.00 and NaN as S.11111.11)
-template <int E, int M>
-__device__ __forceinline__ uint32_t ocp_code(float v, bool& bad) {
-  constexpr int BIAS = (1 << (E - 1)) - 1;
-  const uint32_t u = f2u(v), a = u & 0x7fffffffu, s = (u >> 31) << (E + M);
-  if (a >= 0x7f800000u) {
-    if (E == 5 && M == 2) return s | (a == 0x7f800000u ? 0x7cu : 0x7fu);
-    if (E == 4 && M == 3 && a > 0x7f800000u) return s | 0x7fu;
-    bad = true;
-    return s;
-  }
-  const int ev = (int)(a >> 23) - 127;
-  uint32_t c;
-  if (ev >= 1 - BIAS) {
-    c = ((uint32_t)(ev + BIAS) << M) | ((a >> (23 - M)) & ((1u << M) - 1u));
-  } else {                                     // below the format's normal range: a multiple of its subnormal step
-    const int sh = 24 - BIAS - M - ev;
-    c = a == 0u ? 0u : (((a & 0x007fffffu) | 0x00800000u) >> (sh < 31 ? sh : 31));
-  }
-  return s | c;
-}
-
 __device__ __forceinline__ uint32_t e8m0(float x, bool& bad) {     // 2^(b - 127); 0xFF NaN
   const uint32_t u = f2u(x);
   if ((u & 0x7fffffffu) > 0x7f800000u) return 0xffu;
@@ -196,20 +137,6 @@ __device__ __forceinline__ uint32_t e8m0(float x, bool& bad) {     // 2^(b - 127
   if ((u & 0x807fffffu) == 0u && u >= 0x00800000u && u < 0x7f800000u) return u >> 23;
   bad = true;                                                       // not a power of two the byte can hold
   return 0u;
-}
-
-// the same for a finite code on the format's grid (a clean tile's), branch-free: a normal code's bits are the
-// float's exponent and top mantissa bits re-biased; a code below the normal range is the integer |v| / 2^(1-BIAS-M),
-// read from a float add at 2^23
-template <int E, int M>
-__device__ __forceinline__ uint32_t ocp_code_finite(float v) {
-  constexpr int BIAS = (1 << (E - 1)) - 1;
-  constexpr uint32_t MIN_NORMAL = (uint32_t)(128 - BIAS) << 23;
-  const uint32_t u = f2u(v), a = u & 0x7fffffffu;
-  const uint32_t normal = (a >> (23 - M)) - ((uint32_t)(127 - BIAS) << M);
-  const float scaled = __fmul_rn(u2f(a), u2f((uint32_t)(126 + BIAS + M) << 23));      // |v| * 2^(BIAS - 1 + M)
-  const uint32_t sub = f2u(__fadd_rn(scaled, 8388608.0f)) - 0x4b000000u;
-  return ((u >> 31) << (E + M)) | (a >= MIN_NORMAL ? normal : sub);
 }
 
 template <int E, int M>
@@ -246,15 +173,6 @@ struct OutPack {
     if (threadIdx.x == 0) atomicOr(status, 4);
   }
 };
-
-// A code for block.lut's table fit: the OCP bit pattern, read back in the LUT code space, where every E4M3 byte is a
-// finite value (0x7F / 0xFF are +-480, formats.py:91-96) so E4M3's NaN has no code there: it counts as one the format
-// cannot hold, as a NaN code does in the fit of float codes
-template <int E, int M>
-__device__ __forceinline__ uint32_t lut_code(float v, bool& bad) {
-  if (E == 4 && M == 3 && (f2u(v) & 0x7fffffffu) > 0x7f800000u) bad = true;
-  return ocp_code<E, M>(v, bad);
-}
 
 // block.lut's codes: each code as a byte (lut_code; the 6- and 8-bit LUT formats) and each scale as float32; status
 // bit 1 for a code the format cannot hold (as OutPack), 4 for a lost tile. The bytes of a blocks-along-rows operand

@@ -320,3 +320,26 @@ def test_lut_vs_oracle(oracle, fmt):
             codes = oracle.lut_encode(Pc, fmt)
             assert_bits(prod.lut_encode(Pc, fmt), codes, f"encode {fmt}")
             assert_bits(prod.lut_finder(codes, T, fmt, G), oracle.lut_finder(codes, T, fmt, G), f"finder {fmt} G{G}")
+
+
+@pytest.mark.parametrize("fmt", ["MXFP6_E3M2", "MXFP8_E4M3", "MXFP8_E5M2"])
+def test_lut_block_paths(oracle, fmt):
+    """block.lut along axis 0 takes one launch when the rows are whole blocks of 32 and a group spans at most 32
+    columns, the two-launch byte path for other row counts, and the float path for other block sizes: each against
+    the oracle, with ragged column panels (n not a multiple of 32), groups wider than a panel (G = 6) and blocks of 16."""
+    rng = np.random.default_rng(sum(map(ord, fmt)))
+    for K, n in ((96, 36), (500, 96), (100, 72), (64, 200)):
+        V = (rng.standard_normal((K, n)) * 2.0 ** rng.uniform(-6, 6, (1, n))).astype(np.float32)
+        for block_size in (32, 16):
+            for G in (0, 1, 3, 6):
+                P, X = prod.lut_block_quantize(V, fmt, 0, block_size, "rne", 2.0 ** -23, G, 50)
+                Po, Xo = oracle.lut_block_quantize(V, fmt, 0, block_size, "rne", 2.0 ** -23, G, 50)
+                assert_bits(P, Po, f"block.lut {fmt} {K}x{n} block {block_size} G{G}")
+                assert_bits(X, Xo, f"block.lut X {fmt} {K}x{n} block {block_size} G{G}")
+    # the other rounding modes through the one-launch path
+    V = (rng.standard_normal((128, 64)) * 2.0 ** rng.uniform(-6, 6, (1, 64))).astype(np.float32)
+    for mode in ("ties_away", "truncate"):
+        P, X = prod.lut_block_quantize(V, fmt, 0, 32, mode, 2.0 ** -23, 1, 50)
+        Po, Xo = oracle.lut_block_quantize(V, fmt, 0, 32, mode, 2.0 ** -23, 1, 50)
+        assert_bits(P, Po, f"block.lut {fmt} {mode}")
+        assert_bits(X, Xo, f"block.lut X {fmt} {mode}")
