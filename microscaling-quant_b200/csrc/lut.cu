@@ -191,6 +191,49 @@ struct FusedArgs {
   int rounding;
 };
 
+// block.mxgemmini (block.py, mxgemmini.py) of one 32-row block of one column, by one lane: the 32 values col[0],
+// col[n], ... (a warp's load is one 128-byte row segment when its lanes take consecutive columns), the block max, the
+// scale (to *xout) and its reciprocal, and every code -- the direct code of the short step when the block is finite
+// with a power-of-two scale, else the general OCP grid step (the TMA quantizer's two element steps, the same bits)
+// -- counted by tally(code) as it is made and stored as 32 bytes (two 16-byte stores) at dst. Returns whether a value
+// had no code in the format.
+template <int FE, int FM, int QM, class Tally>
+__device__ __forceinline__ bool quant_block(const float* col, int64_t n, float* xout, uint8_t* dst, float scale_floor,
+                                            int rounding, Tally& tally) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __ldcs(col + i * n);
+  uint32_t mbits = 0u;                                       // max |v| as bits: a NaN pattern tops every number
+#pragma unroll
+  for (int i = 0; i < 32; i++) mbits = max(mbits, f2u(v[i]) & 0x7fffffffu);
+  const bool nan = mbits > 0x7f800000u;
+  const float x = scale_mxquant(nan ? qnan_f() : u2f(mbits), scale_floor);
+  const float r = reciprocal_of<MXQ_FAMILY_MXGEMMINI>(x, nan);
+  *xout = x;
+  uint32_t w[8];
+  bool nocode = false;
+  if (mbits < 0x7f800000u && r != 0.0f) {
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+      const uint32_t c = code_clean<FE, FM, QM>(__fmul_rn(v[i], r));
+      tally(c);
+      w[i >> 2] = (i & 3) ? (w[i >> 2] | (c << (8 * (i & 3)))) : c;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+      const float z = r != 0.0f ? __fmul_rn(v[i], r) : div_rn(v[i], x);
+      const uint32_t c = lut_code<FE, FM>(ocp_grid<FE, FM>(z, rounding), nocode);
+      tally(c);
+      w[i >> 2] = (i & 3) ? (w[i >> 2] | (c << (8 * (i & 3)))) : c;
+    }
+  }
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  return nocode;
+}
+
 constexpr int NW = NT / 32;                    // warps per CTA
 constexpr double MIN_GAP = 1.16415321826934814453125e-10;   // 2^-33: centres this far apart never tie by rounding
 
@@ -351,41 +394,10 @@ __global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __res
       }
     };
     const int64_t b0 = kbeg / 32, b1 = kend / 32;
-    for (int64_t b = b0 + warp; b < b1 && live; b += NWK) {
-      float v[32];
-      const float* src = reinterpret_cast<const float*>(P) + b * 32 * n + j;
-#pragma unroll
-      for (int i = 0; i < 32; i++) v[i] = __ldcs(src + i * n);
-      uint32_t mbits = 0u;                                   // max |v| as bits: a NaN pattern tops every number
-#pragma unroll
-      for (int i = 0; i < 32; i++) mbits = max(mbits, f2u(v[i]) & 0x7fffffffu);
-      const bool nan = mbits > 0x7f800000u;
-      const float x = scale_mxquant(nan ? qnan_f() : u2f(mbits), fa.scale_floor);
-      const float r = reciprocal_of<MXQ_FAMILY_MXGEMMINI>(x, nan);
-      fa.X[b * n + j] = x;
-      uint32_t w[8];
-      if (mbits < 0x7f800000u && r != 0.0f) {
-#pragma unroll
-        for (int i = 0; i < 32; i++) {
-          const uint32_t c = code_clean<FE, FM, QM>(__fmul_rn(v[i], r));
-          tally(c);
-          w[i >> 2] = (i & 3) ? (w[i >> 2] | (c << (8 * (i & 3)))) : c;
-        }
-      } else {
-        bool nocode = false;
-#pragma unroll
-        for (int i = 0; i < 32; i++) {
-          const float z = r != 0.0f ? __fmul_rn(v[i], r) : div_rn(v[i], x);
-          const uint32_t c = lut_code<FE, FM>(ocp_grid<FE, FM>(z, fa.rounding), nocode);
-          tally(c);
-          w[i >> 2] = (i & 3) ? (w[i >> 2] | (c << (8 * (i & 3)))) : c;
-        }
-        if (nocode) mybad = true;
-      }
-      uint4* dst = reinterpret_cast<uint4*>(fa.codesT + j * K + b * 32);
-      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    }
+    for (int64_t b = b0 + warp; b < b1 && live; b += NWK)
+      if (quant_block<FE, FM, QM>(reinterpret_cast<const float*>(P) + b * 32 * n + j, n, fa.X + b * n + j,
+                                  fa.codesT + j * K + b * 32, fa.scale_floor, fa.rounding, tally))
+        mybad = true;
     if (!six && mxb == 0xFFu) mybad = true;
     if (six) {
       __syncthreads();
