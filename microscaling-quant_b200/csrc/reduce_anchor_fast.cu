@@ -42,6 +42,11 @@ __device__ __forceinline__ uint32_t max_s16x2(uint32_t a, uint32_t b) {
   asm("max.s16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
+__device__ __forceinline__ uint32_t min_s16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("min.s16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
 __device__ __forceinline__ int lo_s16(uint32_t v) { return (int)(int16_t)(v & 0xffffu); }
 __device__ __forceinline__ int hi_s16(uint32_t v) { return (int)(int16_t)(v >> 16); }
 
@@ -105,7 +110,7 @@ __device__ __noinline__ int exact_top(const float* a, int sa, const float* b, in
   return top;
 }
 
-template <int RM, int RN>
+template <int RM, int RN, bool RNE>
 __global__ void __launch_bounds__(256, 2)
     k_anchor_hw(const float* __restrict__ PA, const float* __restrict__ XA, const float* __restrict__ PB,
                 const float* __restrict__ XB, float* __restrict__ Y, int64_t K, int64_t M, int64_t N, ArithP A,
@@ -125,7 +130,7 @@ __global__ void __launch_bounds__(256, 2)
   auto row_of = [&](int i) { return i < HM ? ar0 + i : ar1 + (i - HM); };
   auto col_of = [&](int j) { return j < HN ? bc0 + j : bc1 + (j - HN); };
   const int gshift = P.head + 2 - P.b;                          // G = top + gshift
-  const float keep_magic = P.drop_rne ? 12582912.0f : 8388608.0f;   // 1.5 * 2^23 (RNE) or 2^23 (toward zero)
+  const float keep_magic = RNE ? 12582912.0f : 8388608.0f;   // 1.5 * 2^23 (RNE) or 2^23 (toward zero)
 
   uint32_t Cp[RM][RN / 2];
 #pragma unroll
@@ -195,23 +200,39 @@ __global__ void __launch_bounds__(256, 2)
         // the grid of each output: 2^-G as a multiplier (pairs of columns), 2^G to scale the sum back
         F2 inv2[RM][RN / 2];
         bool flush = false;
+        uint32_t mn2 = top2[0][0];                          // the least label max of this thread's outputs
 #pragma unroll
         for (int i = 0; i < RM; i++)
 #pragma unroll
-          for (int j = 0; j < RN / 2; j++) {
-            float v[2];
+          for (int j = 0; j < RN / 2; j++) mn2 = min_s16x2(mn2, top2[i][j]);
+        const int mn = min(lo_s16(mn2), hi_s16(mn2));
+        if (mn < -16) {                                      // an output whose codes' label max is below -16
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-              int t = h ? hi_s16(top2[i][j]) : lo_s16(top2[i][j]);
-              if (t < -16)
-                t = exact_top(Ak + row_of(i), BM, Bk + col_of(2 * j + h), BN, Lak + row_of(i), Lbk + col_of(2 * j + h),
-                              A);
-              const int G = (t == NO_LABEL ? 0 : t) + gshift;
-              v[h] = u2f((uint32_t)(127 - G) << 23);
-              flush |= G < -16;
+          for (int i = 0; i < RM; i++)
+#pragma unroll
+            for (int j = 0; j < RN / 2; j++) {
+              float v[2];
+#pragma unroll
+              for (int h = 0; h < 2; h++) {
+                int t = h ? hi_s16(top2[i][j]) : lo_s16(top2[i][j]);
+                if (t < -16)
+                  t = exact_top(Ak + row_of(i), BM, Bk + col_of(2 * j + h), BN, Lak + row_of(i),
+                                Lbk + col_of(2 * j + h), A);
+                const int G = (t == NO_LABEL ? 0 : t) + gshift;
+                v[h] = u2f((uint32_t)(127 - G) << 23);
+                flush |= G < -16;
+              }
+              inv2[i][j] = pk2(v[0], v[1]);
             }
-            inv2[i][j] = pk2(v[0], v[1]);
-          }
+        } else {                                             // every label max is the anchor's label
+#pragma unroll
+          for (int i = 0; i < RM; i++)
+#pragma unroll
+            for (int j = 0; j < RN / 2; j++)
+              inv2[i][j] = pk2(u2f((uint32_t)(127 - lo_s16(top2[i][j]) - gshift) << 23),
+                               u2f((uint32_t)(127 - hi_s16(top2[i][j]) - gshift) << 23));
+          flush = mn + gshift < -16;
+        }
         flush = __any_sync(0xffffffffu, flush);
         // pass 2: the terms, summed exactly in float32. Pairs of columns stay in 64-bit register pairs for sm_100's
         // packed FP32 instructions (the same IEEE operations, half the issue slots); the masks act on both halves
@@ -240,14 +261,14 @@ __global__ void __launch_bounds__(256, 2)
                   const float bj = h ? hi2(b2[j]) : lo2(b2[j]);
                   const float p = __fmul_rn(a[i], bj);
                   const float y = __fmul_rn(u2f(f2u(p) & 0xfff00000u), h ? hi2(inv2[i][j]) : lo2(inv2[i][j]));
-                  const float c = P.drop_rne ? keep_magic : u2f((f2u(y) & 0x80000000u) | 0x4b000000u);
-                  const float term = P.drop_rne ? __fsub_rn(__fadd_rn(y, c), c) : __fsub_rn(__fadd_rz(y, c), c);
+                  const float c = RNE ? keep_magic : u2f((f2u(y) & 0x80000000u) | 0x4b000000u);
+                  const float term = RNE ? __fsub_rn(__fadd_rn(y, c), c) : __fsub_rn(__fadd_rz(y, c), c);
                   r[h] = __fadd_rn(h ? hi2(acc2[i][j]) : lo2(acc2[i][j]),
                                    fabsf(p) >= 1.52587890625e-05f ? term : 0.0f);
                 }
                 acc2[i][j] = pk2(r[0], r[1]);
               }
-          } else {
+          } else if (RNE) {
             const F2 rne_magic = pk2(keep_magic, keep_magic);
 #pragma unroll
             for (int i = 0; i < RM; i++) {
@@ -256,17 +277,39 @@ __global__ void __launch_bounds__(256, 2)
               for (int j = 0; j < RN / 2; j++) {
                 const F2 p = mul2(ai, b2[j]) & 0xfff00000fff00000ull;          // products truncated to 3 bits
                 const F2 y = mul2(p, inv2[i][j]);
-                if (P.drop_rne) {
-                  acc2[i][j] = add2(acc2[i][j], sub2(add2(y, rne_magic), rne_magic));
-                } else {
-                  const F2 c = (y & 0x8000000080000000ull) | 0x4b0000004b000000ull;   // copysign(2^23, y)
-                  acc2[i][j] = add2(acc2[i][j], sub2(addrz2(y, c), c));
-                }
+                acc2[i][j] = add2(acc2[i][j], sub2(add2(y, rne_magic), rne_magic));
+              }
+            }
+          } else {
+            // copysign(2^23, y): y = p 2^-G has the sign of a_i b_j, so the constant is 2^23 with a_i's sign, made
+            // once per row, XOR b_j's sign bit, taken once per column pair -- one operation per output half
+            uint32_t ca[RM];
+            F2 sb2[RN / 2];
+#pragma unroll
+            for (int i = 0; i < RM; i++) ca[i] = (f2u(a[i]) & 0x80000000u) | 0x4b000000u;
+#pragma unroll
+            for (int j = 0; j < RN / 2; j++) sb2[j] = b2[j] & 0x8000000080000000ull;
+#pragma unroll
+            for (int i = 0; i < RM; i++) {
+              const F2 ai = pk2(a[i], a[i]);
+              const F2 ci = ((F2)ca[i] << 32) | ca[i];
+#pragma unroll
+              for (int j = 0; j < RN / 2; j++) {
+                const F2 p = mul2(ai, b2[j]) & 0xfff00000fff00000ull;          // products truncated to 3 bits
+                const F2 y = mul2(p, inv2[i][j]);
+                const F2 c = ci ^ sb2[j];
+                acc2[i][j] = add2(acc2[i][j], sub2(addrz2(y, c), c));
               }
             }
           }
         }
-        // S4 (bf16 lane) and the tile add, C packed as bf16 pairs
+        // S4 (bf16 lane) and the tile add, C packed as bf16 pairs; the block's scales for this thread's rows and
+        // columns read once
+        float xav[RM], xbv[RN];
+#pragma unroll
+        for (int i = 0; i < RM; i++) xav[i] = xa(i);
+#pragma unroll
+        for (int j = 0; j < RN; j++) xbv[j] = xb(j);
 #pragma unroll
         for (int i = 0; i < RM; i++)
 #pragma unroll
@@ -275,8 +318,8 @@ __global__ void __launch_bounds__(256, 2)
             const float s0 = __fmul_rn(lo2(acc2[i][j]), u2f(0x7f000000u - f2u(lo2(inv2[i][j]))));
             const float s1 = __fmul_rn(hi2(acc2[i][j]), u2f(0x7f000000u - f2u(hi2(inv2[i][j]))));
             const uint32_t c = bf16x2_rne(s0, s1);                 // S4: the tree's bf16 lane
-            const uint32_t t = bf16x2_rne(__fmul_rn(unpack_hi(c), __fmul_rn(xa(i), xb(2 * j))),
-                                          __fmul_rn(unpack_lo(c), __fmul_rn(xa(i), xb(2 * j + 1))));
+            const uint32_t t = bf16x2_rne(__fmul_rn(unpack_hi(c), __fmul_rn(xav[i], xbv[2 * j])),
+                                          __fmul_rn(unpack_lo(c), __fmul_rn(xav[i], xbv[2 * j + 1])));
             Cp[i][j] = bf16x2_rne(__fadd_rn(unpack_hi(Cp[i][j]), unpack_hi(t)),
                                   __fadd_rn(unpack_lo(Cp[i][j]), unpack_lo(t)));
           }
@@ -336,12 +379,12 @@ int anchor_fast(const float* PA, const float* XA, const float* PB, const float* 
   constexpr int RM = 4, RN = 8;
   using TT = Tile<RM, RN>;
   const size_t smem = TT::SMEM + (size_t)BK * (TT::BM + TT::BN) * sizeof(int);
-  if (int r = check_cuda(cudaFuncSetAttribute(k_anchor_hw<RM, RN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              (int)smem),
+  auto kernel = P.drop_rne ? k_anchor_hw<RM, RN, true> : k_anchor_hw<RM, RN, false>;
+  if (int r = check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                          "anchor_tree: shared memory attribute"))
     return r;
   dim3 grid((unsigned)((N + TT::BN - 1) / TT::BN), (unsigned)((M + TT::BM - 1) / TT::BM));
-  k_anchor_hw<RM, RN><<<grid, TT::NT, smem, st>>>(PA, XA, PB, XB, Y, K, M, N, A, P);
+  kernel<<<grid, TT::NT, smem, st>>>(PA, XA, PB, XB, Y, K, M, N, A, P);
   return MXQ_LAUNCH_CHECK("anchor_tree");
 }
 
