@@ -384,9 +384,14 @@ __global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __res
       __syncthreads();
     }
     uint32_t mxb = 0;                                        // 8-bit: the largest bin seen (0xFF: no code)
+    // the thread's counter of code c at a 32-bit shared address (the increment is a load, an add and a store)
+    const uint32_t mbase = (uint32_t)__cvta_generic_to_shared(mine);
     auto tally = [&](uint32_t c) {
       if (six) {
-        mine[c * NTK] += 1;
+        const uint32_t at = mbase + c * (2 * NTK);
+        unsigned short cnt;
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(cnt) : "r"(at));
+        asm volatile("st.shared.u16 [%0], %1;" ::"r"(at), "h"((unsigned short)(cnt + 1)) : "memory");
       } else {
         const uint32_t bn = sbin[c];
         mxb = max(mxb, bn);
