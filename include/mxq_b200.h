@@ -231,9 +231,9 @@ int mxq_block_lut_quantize(const float* V, float* P_lut, float* X, int64_t rows,
  * 16 MiB (one per device) instead of the caller, so the call allocates nothing. Sizes whose workspace
  * (mxq_block_lut_workspace) exceeds 16 MiB are rejected with MXQ_ERR_VALUE. Every call on a device shares the
  * array: calls whose work overlaps on the GPU (other streams, or other host threads, without ordering between
- * them) race on it. Nothing in the array needs to start at zero. The array's device address is looked up once per
- * device and kept for the life of the process, so this entry point must not be called on a device after
- * cudaDeviceReset (or any other teardown of its primary context) in the same process. */
+ * them) race on it. Nothing in the array needs to start at zero. The array's device address is looked up again
+ * whenever the device's current context has changed (cudaDeviceReset makes a new one, and the module's arrays with
+ * it). */
 int mxq_block_lut_quantize_static(const float* V, float* P_lut, float* X, int64_t rows, int64_t cols, int32_t axis,
                                   int64_t block, const mxq_quant_spec* spec, int32_t group, int32_t max_iters,
                                   int32_t* status, void* stream);

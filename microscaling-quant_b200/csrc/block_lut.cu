@@ -38,18 +38,22 @@ int block_lut_fused(const float* V, float* out, float* X, float* T, float* cmap,
 namespace {
 std::mutex g_scratch_mu;
 void* g_scratch_ptr[kMaxDevices] = {};
+unsigned long long g_scratch_ctx[kMaxDevices] = {};
 
-// The current device's address of g_block_lut_scratch, looked up once per device with that device current.
+// The current device's address of g_block_lut_scratch, looked up with that device current once per context (a
+// context made after cudaDeviceReset loads the module again, and the array may move)
 int static_scratch(void** out) {
   int dev = 0;
   if (int r = check_cuda(cudaGetDevice(&dev), "block.lut static scratch: current device")) return r;
   MXQ_REQUIRE(dev >= 0 && dev < kMaxDevices, MXQ_ERR_UNSUPPORTED, "block.lut static scratch: device %d", dev);
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_ptr[dev] == nullptr) {
+  const unsigned long long ctx = mxq::context_id();
+  if (g_scratch_ptr[dev] == nullptr || ctx == 0 || g_scratch_ctx[dev] != ctx) {
     void* p = nullptr;
     if (int r = check_cuda(cudaGetSymbolAddress(&p, g_block_lut_scratch), "block.lut static scratch: address"))
       return r;
     g_scratch_ptr[dev] = p;
+    g_scratch_ctx[dev] = mxq::context_id();                 // the lookup made the context current if it was not
   }
   *out = g_scratch_ptr[dev];
   return MXQ_OK;
