@@ -246,7 +246,9 @@ int mxq_device_timeouts(uint32_t* out);
  * (allocated on first use, shared by every device) that a TMA-staged kernel increments when a bounded wait gives up
  * -- the tile it was loading is then written as NaN codes and NaN scales (the compact form sets status bit 4
  * instead). The host reads it with a plain load and no synchronisation; it counts the kernels that have finished.
- * A caller checks it after its calls and clears it (stores 0) once it has handled the event. */
+ * A caller checks it after its calls and clears it (stores 0) once it has handled the event. A cudaDeviceReset of the
+ * device whose context allocated the word frees it; the library then allocates a new one at its next use on that
+ * device, so a caller that keeps the address fetches it again after such a reset. */
 int mxq_wait_status_word(uint32_t** out);
 /* No reference counterpart; for tests of the timeout path only: mxq_block_quantize of a rows x cols V (blocks of 32
  * along rows, mxgemmini MXFP8_E4M3) through the TMA kernel with its loads never issued and waits of wait_rounds

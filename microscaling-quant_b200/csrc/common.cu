@@ -99,7 +99,14 @@ int encode_tmap_f32(CUtensorMap* map, const void* base, int rank, const uint64_t
 unsigned* wait_status_word() {
   static std::mutex mu;
   static unsigned* word = nullptr;
+  static int alloc_dev = -1;
+  static unsigned long long alloc_ctx = 0;
   std::lock_guard<std::mutex> lock(mu);
+  if (word != nullptr && alloc_ctx != 0) {
+    // a cudaDeviceReset of the device whose context allocated the word freed it with that context: make a new one
+    int dev = -1;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev == alloc_dev && context_id() != alloc_ctx) word = nullptr;
+  }
   if (word == nullptr) {
     void* p = nullptr;
     if (check_cuda(cudaHostAlloc(&p, 64, cudaHostAllocMapped | cudaHostAllocPortable), "wait-status word"))
@@ -114,6 +121,8 @@ unsigned* wait_status_word() {
     }
     *static_cast<volatile unsigned*>(p) = 0u;
     word = static_cast<unsigned*>(p);
+    if (cudaGetDevice(&alloc_dev) != cudaSuccess) alloc_dev = -1;
+    alloc_ctx = context_id();
   }
   return word;
 }
