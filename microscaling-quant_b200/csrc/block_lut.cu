@@ -1,7 +1,9 @@
-// block.lut.quantize (mxq/block/lut.py:23-34) as one C-ABI call: the fused mxgemmini quantizer writes V's codes
-// into a workspace, the table fit reads them as the K x n operand (axis 0: V itself; axis 1: V read transposed in
-// place) and writes its tables into the same workspace, and pick with lookup replaces every code by its table
-// entry in V's layout. Three kernels on one stream; nothing is allocated and nothing waits on the host.
+// block.lut.quantize (mxq/block/lut.py:23-34) as one C-ABI call on one stream, allocating nothing and never waiting
+// on the host. Axis 0, blocks of 32: one launch (the tables kernel's fused mode) that quantizes V, fits the tables
+// and writes every entry (rows a multiple of 32), else the TMA quantizer's code bytes and one launch that fits and
+// looks up from them. Otherwise: the fused mxgemmini quantizer writes V's float codes into the workspace, the table
+// fit reads them as the K x n operand (axis 1: V read transposed in place) and writes its tables into the same
+// workspace, and pick with lookup replaces every code by its table entry in V's layout.
 #include "common.cuh"
 
 #include <mutex>

@@ -5,10 +5,12 @@ keyword-required, as in the reference.
     P, X = quantize(V, "MXFP6_E3M2", axis=0, block_size=32, rounding_mode="rne", scale_floor=2**-23,
                     group=1, max_iters=50)                                V_hat = P * expand(X)
 
-One C call (mxq_block_lut_quantize). Along axis 0 the fused quantizer writes each code as a byte (its OCP bit
-pattern), the table fit histograms the bytes and leaves each group's code -> entry map, and the last kernel reads
-one map entry per element; along axis 1 (the operand read transposed in place, never copied) the quantizer writes
-float codes, and the fit and a fused pick + lookup read them. Codes, tables and maps live in a workspace.
+One C call (mxq_block_lut_quantize). Along axis 0 with blocks of 32 and whole 32-row blocks, one kernel quantizes V,
+counts each code as it is made, fits each group's table, and writes every element's entry through the group's code ->
+entry map; other row counts take the TMA quantizer writing the codes as bytes (their OCP bit patterns) and one kernel
+that fits and looks up from the bytes; along axis 1 (the operand read transposed in place, never copied) and for other
+block sizes the quantizer writes float codes, and the fit and a fused pick + lookup read them. Codes, tables and maps
+live in a workspace.
 """
 import ctypes
 
