@@ -141,6 +141,22 @@ def _copy_streams(dev):
     return _streams[dev]
 
 
+def _runs(total: int, per: int):
+    """[start, stop) runs of at most `per` units covering range(total), their sizes ramping up from per / 8 at the start
+    and back down at the end: the first copy in and the last copy out, which nothing overlaps, stay short."""
+    head = [max(1, per >> 3), max(1, per >> 2), max(1, per >> 1)]
+    if total <= 2 * sum(head) + per:
+        sizes = [per] * (total // per) + ([total % per] if total % per else [])
+    else:
+        middle = total - 2 * sum(head)
+        sizes = head + [per] * (middle // per) + ([middle % per] if middle % per else []) + head[::-1]
+    runs, at = [], 0
+    for n in sizes:
+        runs.append((at, at + n))
+        at += n
+    return runs
+
+
 def _quantize_streamed(V, spec, axis_, outer, L, inner, nb, block_size, dev):
     """A host V quantized through the device in independent chunks, copies in, kernels and copies out on three
     streams so PCIe carries both directions while the device quantizes. Chunks are whole outer slices when
@@ -158,14 +174,12 @@ def _quantize_streamed(V, spec, axis_, outer, L, inner, nb, block_size, dev):
     chunks = []                        # (v0, v1, x0, x1, (outer, len, inner)) per chunk
     if outer > 1 and 4 * L * inner <= STREAM_CHUNK_BYTES:       # whole outer slices
         per = max(1, STREAM_CHUNK_BYTES // (4 * L * inner))
-        for o0 in range(0, outer, per):
-            o1 = min(outer, o0 + per)
+        for o0, o1 in _runs(outer, per):
             chunks.append((o0 * L * inner, o1 * L * inner, o0 * nb * inner, o1 * nb * inner, (o1 - o0, L, inner)))
     else:                              # runs of whole blocks inside each outer slice (the last may be short)
         per = max(1, STREAM_CHUNK_BYTES // (4 * block_size * inner))
         for o in range(outer):
-            for b0 in range(0, nb, per):
-                b1 = min(nb, b0 + per)
+            for b0, b1 in (_runs(nb, per) if outer == 1 else [(b, min(nb, b + per)) for b in range(0, nb, per)]):
                 r0, r1 = b0 * block_size, min(L, b1 * block_size)
                 vb, xb = o * L * inner, o * nb * inner
                 chunks.append((vb + r0 * inner, vb + r1 * inner, xb + b0 * inner, xb + b1 * inner, (1, r1 - r0, inner)))

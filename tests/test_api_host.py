@@ -133,3 +133,17 @@ def test_mxqconfig_apply_refuses_non_linear():
     from mxq.nn.torchao import MXQConfig, apply
     with pytest.raises(TypeError, match="applies to nn.Linear"):
         apply(torch.nn.Conv1d(2, 2, 1), MXQConfig())
+
+
+def test_stream_runs_cover_and_ramp():
+    """The host-streaming chunk runs: contiguous, covering every unit once, none longer than the chunk, and short at
+    both ends when there are enough units for the ramps."""
+    from mxq.block._driver import _runs
+    for total in (1, 2, 7, 10, 31, 53, 60, 100, 256, 1000):
+        for per in (1, 2, 3, 8, 16, 64):
+            r = _runs(total, per)
+            assert r[0][0] == 0 and r[-1][1] == total
+            assert all(a[1] == b[0] for a, b in zip(r, r[1:]))
+            assert all(0 < b - a <= per for a, b in r)
+            if total > 2 * (max(1, per >> 3) + max(1, per >> 2) + max(1, per >> 1)) + per:
+                assert r[0][1] - r[0][0] == max(1, per >> 3) and r[-1][1] - r[-1][0] == max(1, per >> 3)
