@@ -253,6 +253,12 @@ __device__ __forceinline__ int grid_rank(float v, const TableParams& tp) {
   return r < 0 ? 0 : (r >= tp.nv ? tp.nv - 1 : r);
 }
 
+// a count (0 <= c < 2^31) as float64 by its bit pattern: 2^52 + c has c in its low mantissa bits, and subtracting
+// 2^52 is exact -- an FP64 add instead of the slower integer conversion
+__device__ __forceinline__ double i2d(int c) {
+  return __dsub_rn(__hiloint2double(0x43300000, c), 4503599627370496.0);
+}
+
 // _dedupe (kmeans.py:38-43) across lanes 0-15 of a warp, lane t holding v_t: sort ascending (by rank, ties in lane
 // order), equal neighbours turned into +inf, sort again. `scratch` holds 16 doubles of this warp.
 __device__ __forceinline__ double dedupe_lanes(double v, double* scratch) {
@@ -314,6 +320,7 @@ __global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __res
   extern __shared__ int counts[];
   __shared__ double scratch[NWK][LUT], fsum[NWK][LUT], fw[NWK][LUT];
   __shared__ __align__(16) float sgrid[MAXV];                // the format's tables, read with per-lane indices
+  __shared__ double sgridd[MAXV], ssafed[MAXV];              // the same as float64: no conversion in the fits
   __shared__ __align__(16) float ssafe[MAXV];
   __shared__ __align__(16) float svals[MAXV];
   __shared__ __align__(16) uint8_t sorder[MAXV];
@@ -350,6 +357,10 @@ __global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __res
       reinterpret_cast<uint4*>(sorder)[i] = __ldg(reinterpret_cast<const uint4*>(dt->order) + i);
     const uint4* bsrc = reinterpret_cast<const uint4*>(BYTES ? dt->cbin : dt->bin);   // a code's grid rank
     for (int i = tid; i < (BYTES ? MAXV : KEYS) / 16; i += NTK) reinterpret_cast<uint4*>(sbin)[i] = __ldg(bsrc + i);
+  }
+  for (int i = tid; i < MAXV; i += NTK) {
+    sgridd[i] = (double)__ldg(tp.dt->grid + i);
+    ssafed[i] = (double)__ldg(tp.dt->safe + i);
   }
   if (tid == 0) bad = 0;
   __syncthreads();
@@ -649,8 +660,8 @@ __global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __res
     int npres = 0;
     for (int b = b0; b < b1; b++) {
       const int cb = cnt[b];
-      w = __dadd_rn(w, (double)cb);
-      wx = __dadd_rn(wx, __dmul_rn((double)cb, (double)sgrid[b]));
+      w = __dadd_rn(w, i2d(cb));
+      wx = __dadd_rn(wx, __dmul_rn(i2d(cb), sgridd[b]));
       npres += cb > 0;
     }
 #pragma unroll
@@ -672,8 +683,8 @@ __global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __res
       }
       for (int b = b0; b < b1; b++) {
         const int cb = cnt[b];
-        rw = __dadd_rn(rw, (double)cb);
-        rx = __dadd_rn(rx, __dmul_rn((double)cb, (double)sgrid[b]));
+        rw = __dadd_rn(rw, i2d(cb));
+        rx = __dadd_rn(rx, __dmul_rn(i2d(cb), sgridd[b]));
         PW[b + 1] = rw;
         PWX[b + 1] = rx;
       }
@@ -687,7 +698,7 @@ __global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __res
         const int b = b0 + lane;
         const bool pr = b < nv && cnt[b] > 0;
         const unsigned mask = __ballot_sync(0xffffffffu, pr);
-        if (pr) scratch[warp][base + __popc(mask & lt)] = (double)sgrid[b];
+        if (pr) scratch[warp][base + __popc(mask & lt)] = sgridd[b];
         base += __popc(mask);
       }
       __syncwarp();
@@ -695,20 +706,28 @@ __global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __res
       __syncwarp();
     } else {
       // 2b: quantile seeds: the first code whose cumulative weight share (rounded, so non-decreasing) reaches
-      // (t + 0.5) / 16 (exact in float64), i.e. the number of codes whose share is below it: every lane divides for
-      // its codes at once and a ballot per probe counts them
+      // p_t = (t + 0.5) / 16, i.e. seed_t = #{codes b : share_b < p_t}. Code b's count of probes at or below its
+      // share, q_b = #{t : p_t <= share_b}, is floor(16 share_b - 0.5) + 1 clamped to [0, 16] (16 share_b - 0.5 is
+      // exact; the floor is the round-down add of 2^52); then share_b < p_t exactly when q_b <= t, so seed_t is the
+      // prefix sum up to t of a 17-bin histogram of the q_b, which every lane fills for its codes at once
       const double tot = PW[nv];
-      int seed = 0;
-      for (int bb = 0; bb < nv; bb += 32) {
-        const int b = bb + lane;
-        const double share = b < nv ? __ddiv_rn(PW[b + 1], tot) : INFINITY;
-#pragma unroll
-        for (int t = 0; t < LUT; t++) {
-          const int below = __popc(__ballot_sync(0xffffffffu, share < ((double)t + 0.5) / (double)LUT));
-          seed += lane == t ? below : 0;
-        }
+      int* const qh = reinterpret_cast<int*>(fsum[warp]);   // 17 counters (fsum's first use comes later)
+      if (lane <= LUT) qh[lane] = 0;
+      __syncwarp();
+      for (int b = lane; b < nv; b += 32) {
+        const double y = __dsub_rn(__dmul_rn(__ddiv_rn(PW[b + 1], tot), (double)LUT), 0.5);
+        const int q = y < 0.0 ? 0 : min(__double2loint(__dadd_rd(y, 4503599627370496.0)) + 1, LUT);
+        atomicAdd(&qh[q], 1);
       }
-      if (lane < LUT) c = (double)sgrid[seed < nv - 1 ? seed : nv - 1];
+      __syncwarp();
+      int seed = lane <= LUT ? qh[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {                     // inclusive prefix sums over lanes 0..16
+        const int up = __shfl_up_sync(0xffffffffu, seed, o);
+        if (lane >= o) seed += up;
+      }
+      __syncwarp();
+      if (lane < LUT) c = sgridd[seed < nv - 1 ? seed : nv - 1];
       c = dedupe_lanes(c, scratch[warp]);
       // 2c: weighted Lloyd passes
       for (int it = 0; it < max_iters; it++) {
@@ -721,7 +740,7 @@ __global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __res
             // the first code strictly closer to centre t + 1 (monotone along the sorted codes, as the gap check
             // above guarantees): start at the codes around the midpoint of the two centres and walk to it
             auto closer = [&](int k) {
-              const double x = (double)sgrid[k];
+              const double x = sgridd[k];
               return fabs(__dsub_rn(x, cn)) < fabs(__dsub_rn(x, c));
             };
             int i = grid_rank((float)__dmul_rn(__dadd_rn(c, cn), 0.5), tp);
@@ -751,7 +770,7 @@ __global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __res
           __syncwarp();
           for (int b = lane; b < nv; b += 32) {
             if (cnt[b] == 0) continue;
-            const double x = (double)sgrid[b];
+            const double x = sgridd[b];
             int best = 0;
             double bd = fabs(__dsub_rn(x, cc[0]));
 #pragma unroll
@@ -762,8 +781,8 @@ __global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __res
                 best = t;
               }
             }
-            atomicAdd(&fsum[warp][best], __dmul_rn((double)cnt[b], x));
-            atomicAdd(&fw[warp][best], (double)cnt[b]);
+            atomicAdd(&fsum[warp][best], __dmul_rn(i2d(cnt[b]), x));
+            atomicAdd(&fw[warp][best], i2d(cnt[b]));
           }
           __syncwarp();
           const double ws = lane < LUT ? fw[warp][lane] : 0.0, sm = lane < LUT ? fsum[warp][lane] : 0.0;
@@ -791,12 +810,11 @@ __global__ void __launch_bounds__(NTH, 1024 / NTH) k_lut_tables(const TIn* __res
       int lo = 0, hi = tp.nsafe;
       while (lo < hi) {
         const int mid = (lo + hi) >> 1;
-        if ((double)ssafe[mid] < c) lo = mid + 1;
+        if (ssafed[mid] < c) lo = mid + 1;
         else hi = mid;
       }
       int best = lo < tp.nsafe ? lo : tp.nsafe - 1;
-      if (lo > 0 && (lo == tp.nsafe || fabs(__dsub_rn(c, (double)ssafe[lo - 1])) <=
-                                            fabs(__dsub_rn(c, (double)ssafe[lo]))))
+      if (lo > 0 && (lo == tp.nsafe || fabs(__dsub_rn(c, ssafed[lo - 1])) <= fabs(__dsub_rn(c, ssafed[lo]))))
         best = lo - 1;
       member[warp][best] = 1;
     }
