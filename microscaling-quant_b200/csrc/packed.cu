@@ -97,10 +97,9 @@ __global__ void __launch_bounds__(256) k_unpack4(const uint8_t* __restrict__ cod
   }
 }
 
-// dequantize_packed on vectors: a thread decodes 4 codes and multiplies by their scales (one E8M0 byte for a run
-// along a row, 4 bytes for a run along inner). Preconditions as k_dequantize4 (quantize.cu), codes aligned to the
-// word, and for COLS the 4 scale bytes at a multiple of 4.
-template <int E, int M, bool COLS>
+// dequantize_packed on vectors with blocks along the row (inner 1): a thread decodes 4 codes and multiplies by their
+// block's scale (one E8M0 byte). Preconditions as k_dequantize4 (quantize.cu), codes aligned to the word.
+template <int E, int M>
 __global__ void __launch_bounds__(256) k_dequantize_packed4(const uint8_t* __restrict__ codes,
                                                             const uint8_t* __restrict__ scales,
                                                             float4* __restrict__ out, uint32_t n4, uint32_t len,
@@ -118,18 +117,42 @@ __global__ void __launch_bounds__(256) k_dequantize_packed4(const uint8_t* __res
     v = make_float4(ocp_value(w & 255u, E, M), ocp_value((w >> 8) & 255u, E, M), ocp_value((w >> 16) & 255u, E, M),
                     ocp_value(w >> 24, E, M));
   }
-  float4 x;
-  if (COLS) {
-    const uint32_t ol = e / inner, j = e - ol * inner, o = ol / len, l = ol - o * len;
-    const uint32_t w = reinterpret_cast<const uint32_t*>(scales)[((o * nb + l / block) * inner + j) / 4u];
-    x = make_float4(e8m0_value(w & 255u), e8m0_value((w >> 8) & 255u), e8m0_value((w >> 16) & 255u),
-                    e8m0_value(w >> 24));
-  } else {
-    const uint32_t o = e / len, l = e - o * len;
-    const float s = e8m0_value(scales[o * nb + l / block]);
-    x = make_float4(s, s, s, s);
+  const uint32_t o = e / len, l = e - o * len;
+  const float s = e8m0_value(scales[o * nb + l / block]);
+  out[q] = make_float4(__fmul_rn(v.x, s), __fmul_rn(v.y, s), __fmul_rn(v.z, s), __fmul_rn(v.w, s));
+}
+
+// dequantize_packed with blocks along len and inner a multiple of 4 (axis 0 of a matrix): a thread owns 4 adjacent
+// columns of one block of rows, reads their 4 scale bytes once and walks the block's rows, one 4-code word in and one
+// float4 out per row (a warp's loads and stores are consecutive across its lanes' columns). Threads: outer x nb x
+// inner / 4, fewer than 2^32; one index split per thread instead of three divisions per float4.
+template <int E, int M>
+__global__ void __launch_bounds__(256) k_dequantize_packed_cols(const uint8_t* __restrict__ codes,
+                                                                const uint8_t* __restrict__ scales,
+                                                                float4* __restrict__ out, uint32_t nthreads,
+                                                                uint32_t len, uint32_t inner, uint32_t block,
+                                                                uint32_t nb) {
+  const uint32_t t = blockIdx.x * 256u + threadIdx.x;
+  if (t >= nthreads) return;
+  const uint32_t iq = inner / 4u, jq = t % iq, rest = t / iq, b = rest % nb, o = rest / nb;
+  const uint32_t w = reinterpret_cast<const uint32_t*>(scales)[(o * nb + b) * iq + jq];
+  const float x0 = e8m0_value(w & 255u), x1 = e8m0_value((w >> 8) & 255u), x2 = e8m0_value((w >> 16) & 255u),
+              x3 = e8m0_value(w >> 24);
+  const uint32_t l0 = b * block, l1 = l0 + block < len ? l0 + block : len;
+  uint32_t q = (o * len + l0) * iq + jq;                   // float4 index of (row l0, columns 4 jq ..)
+  for (uint32_t l = l0; l < l1; l++, q += iq) {
+    float4 v;
+    if (E + M == 3) {
+      const uint32_t c = reinterpret_cast<const uint16_t*>(codes)[q];
+      v = make_float4(ocp_value(c & 15u, E, M), ocp_value((c >> 4) & 15u, E, M), ocp_value((c >> 8) & 15u, E, M),
+                      ocp_value((c >> 12) & 15u, E, M));
+    } else {
+      const uint32_t c = reinterpret_cast<const uint32_t*>(codes)[q];
+      v = make_float4(ocp_value(c & 255u, E, M), ocp_value((c >> 8) & 255u, E, M), ocp_value((c >> 16) & 255u, E, M),
+                      ocp_value(c >> 24, E, M));
+    }
+    __stcs(out + q, make_float4(__fmul_rn(v.x, x0), __fmul_rn(v.y, x1), __fmul_rn(v.z, x2), __fmul_rn(v.w, x3)));
   }
-  out[q] = make_float4(__fmul_rn(v.x, x.x), __fmul_rn(v.y, x.y), __fmul_rn(v.z, x.z), __fmul_rn(v.w, x.w));
 }
 
 // the (e, m) of an MX element format as template arguments: f(std::integral_constant<int, E>, ...<int, M>)
@@ -202,14 +225,24 @@ int mxq_dequantize_packed(const uint8_t* codes, const uint8_t* scales, float* ou
   const bool al = (uintptr_t)codes % word == 0 && (uintptr_t)out % 16 == 0 && n < (1ll << 32) &&
                   outer * nb * inner < (1ll << 32);
   const bool cols = inner % 4 == 0 && (uintptr_t)scales % 4 == 0, rows = inner == 1 && len % 4 == 0 && block % 4 == 0;
-  if (al && (cols || rows)) {
+  if (al && cols) {
+    const uint32_t nthreads = (uint32_t)(outer * nb * (inner / 4)), grid = (nthreads + 255) / 256;
+    cudaStream_t st = as_stream(stream);
+    by_format(e, m, [&](auto E, auto M) {
+      k_dequantize_packed_cols<decltype(E)::value, decltype(M)::value><<<grid, 256, 0, st>>>(
+          codes, scales, reinterpret_cast<float4*>(out), nthreads, (uint32_t)len, (uint32_t)inner, (uint32_t)block,
+          (uint32_t)nb);
+      return 0;
+    });
+    return MXQ_LAUNCH_CHECK("dequantize_packed");
+  }
+  if (al && rows) {
     const uint32_t n4 = (uint32_t)(n / 4), grid = (n4 + 255) / 256;
     cudaStream_t st = as_stream(stream);
     by_format(e, m, [&](auto E, auto M) {
-      constexpr int e_ = decltype(E)::value, m_ = decltype(M)::value;
-      auto kern = cols ? k_dequantize_packed4<e_, m_, true> : k_dequantize_packed4<e_, m_, false>;
-      kern<<<grid, 256, 0, st>>>(codes, scales, reinterpret_cast<float4*>(out), n4, (uint32_t)len, (uint32_t)inner,
-                                 (uint32_t)block, (uint32_t)nb);
+      k_dequantize_packed4<decltype(E)::value, decltype(M)::value><<<grid, 256, 0, st>>>(
+          codes, scales, reinterpret_cast<float4*>(out), n4, (uint32_t)len, (uint32_t)inner, (uint32_t)block,
+          (uint32_t)nb);
       return 0;
     });
     return MXQ_LAUNCH_CHECK("dequantize_packed");
