@@ -77,20 +77,32 @@ template <int E, int M>
 __global__ void __launch_bounds__(256) k_unpack4(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales,
                                                  float4* __restrict__ P, float4* __restrict__ X, uint32_t nc4,
                                                  uint32_t ns4) {
-  const uint32_t q = blockIdx.x * 256u + threadIdx.x;
-  if (q < nc4) {
-    uint32_t w;
-    if (E + M == 3) {
-      w = reinterpret_cast<const uint16_t*>(codes)[q];
-      P[q] = make_float4(ocp_value(w & 15u, E, M), ocp_value((w >> 4) & 15u, E, M), ocp_value((w >> 8) & 15u, E, M),
-                         ocp_value((w >> 12) & 15u, E, M));
-    } else {
-      w = reinterpret_cast<const uint32_t*>(codes)[q];
-      P[q] = make_float4(ocp_value(w & 255u, E, M), ocp_value((w >> 8) & 255u, E, M),
-                         ocp_value((w >> 16) & 255u, E, M), ocp_value(w >> 24, E, M));
+  // a grid of a few CTAs per SM striding over the words, four words' loads in flight per thread before their
+  // decodes and stores
+  const uint32_t stride = gridDim.x * 256u;
+  constexpr int U = 4;
+  for (uint32_t q0 = blockIdx.x * 256u + threadIdx.x; q0 < nc4; q0 += U * stride) {
+    uint32_t w[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const uint32_t q = q0 + u * stride;
+      w[u] = q < nc4 ? (E + M == 3 ? (uint32_t)reinterpret_cast<const uint16_t*>(codes)[q]
+                                   : reinterpret_cast<const uint32_t*>(codes)[q])
+                     : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const uint32_t q = q0 + u * stride;
+      if (q >= nc4) break;
+      if (E + M == 3)
+        __stcs(P + q, make_float4(ocp_value(w[u] & 15u, E, M), ocp_value((w[u] >> 4) & 15u, E, M),
+                                  ocp_value((w[u] >> 8) & 15u, E, M), ocp_value((w[u] >> 12) & 15u, E, M)));
+      else
+        __stcs(P + q, make_float4(ocp_value(w[u] & 255u, E, M), ocp_value((w[u] >> 8) & 255u, E, M),
+                                  ocp_value((w[u] >> 16) & 255u, E, M), ocp_value(w[u] >> 24, E, M)));
     }
   }
-  if (q < ns4) {
+  for (uint32_t q = blockIdx.x * 256u + threadIdx.x; q < ns4; q += stride) {
     const uint32_t w = reinterpret_cast<const uint32_t*>(scales)[q];
     X[q] = make_float4(e8m0_value(w & 255u), e8m0_value((w >> 8) & 255u), e8m0_value((w >> 16) & 255u),
                        e8m0_value(w >> 24));
@@ -202,7 +214,7 @@ int mxq_unpack(const uint8_t* codes, const uint8_t* scales, float* P, float* X, 
   if (n_codes % 4 == 0 && n_scales % 4 == 0 && n < (1ll << 32) && (uintptr_t)codes % word == 0 &&
       (uintptr_t)scales % 4 == 0 && (uintptr_t)P % 16 == 0 && (uintptr_t)X % 16 == 0) {
     const uint32_t nc4 = (uint32_t)(n_codes / 4), ns4 = (uint32_t)(n_scales / 4);
-    const uint32_t grid = ((nc4 > ns4 ? nc4 : ns4) + 255) / 256;
+    const uint32_t grid = grid_for((int64_t)(nc4 > ns4 ? nc4 : ns4), 256, 8);
     cudaStream_t st = as_stream(stream);
     by_format(e, m, [&](auto E, auto M) {
       k_unpack4<decltype(E)::value, decltype(M)::value><<<grid, 256, 0, st>>>(
