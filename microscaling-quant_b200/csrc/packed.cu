@@ -110,28 +110,51 @@ __global__ void __launch_bounds__(256) k_unpack4(const uint8_t* __restrict__ cod
 }
 
 // dequantize_packed on vectors with blocks along the row (inner 1): a thread decodes 4 codes and multiplies by their
-// block's scale (one E8M0 byte). Preconditions as k_dequantize4 (quantize.cu), codes aligned to the word.
+// block's scale (one E8M0 byte), striding over the float4s with four words' and scale bytes' loads in flight.
+// bsh >= 0 when block = 2^bsh divides len: the scale of element e is then byte e >> bsh, no division. Preconditions as
+// k_dequantize4 (quantize.cu), codes aligned to the word.
 template <int E, int M>
 __global__ void __launch_bounds__(256) k_dequantize_packed4(const uint8_t* __restrict__ codes,
                                                             const uint8_t* __restrict__ scales,
                                                             float4* __restrict__ out, uint32_t n4, uint32_t len,
-                                                            uint32_t inner, uint32_t block, uint32_t nb) {
-  const uint32_t q = blockIdx.x * 256u + threadIdx.x;
-  if (q >= n4) return;
-  const uint32_t e = q * 4u;
-  float4 v;
-  if (E + M == 3) {
-    const uint32_t w = reinterpret_cast<const uint16_t*>(codes)[q];
-    v = make_float4(ocp_value(w & 15u, E, M), ocp_value((w >> 4) & 15u, E, M), ocp_value((w >> 8) & 15u, E, M),
-                    ocp_value((w >> 12) & 15u, E, M));
-  } else {
-    const uint32_t w = reinterpret_cast<const uint32_t*>(codes)[q];
-    v = make_float4(ocp_value(w & 255u, E, M), ocp_value((w >> 8) & 255u, E, M), ocp_value((w >> 16) & 255u, E, M),
-                    ocp_value(w >> 24, E, M));
+                                                            uint32_t block, uint32_t nb, int bsh) {
+  const uint32_t stride = gridDim.x * 256u;
+  constexpr int U = 4;
+  for (uint32_t q0 = blockIdx.x * 256u + threadIdx.x; q0 < n4; q0 += U * stride) {
+    uint32_t w[U], sb[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const uint32_t q = q0 + u * stride;
+      w[u] = sb[u] = 0u;
+      if (q < n4) {
+        w[u] = E + M == 3 ? (uint32_t)reinterpret_cast<const uint16_t*>(codes)[q]
+                          : reinterpret_cast<const uint32_t*>(codes)[q];
+        const uint32_t e = q * 4u;
+        uint32_t si;
+        if (bsh >= 0) {
+          si = e >> bsh;
+        } else {
+          const uint32_t o = e / len, l = e - o * len;
+          si = o * nb + l / block;
+        }
+        sb[u] = scales[si];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const uint32_t q = q0 + u * stride;
+      if (q >= n4) break;
+      float4 v;
+      if (E + M == 3)
+        v = make_float4(ocp_value(w[u] & 15u, E, M), ocp_value((w[u] >> 4) & 15u, E, M),
+                        ocp_value((w[u] >> 8) & 15u, E, M), ocp_value((w[u] >> 12) & 15u, E, M));
+      else
+        v = make_float4(ocp_value(w[u] & 255u, E, M), ocp_value((w[u] >> 8) & 255u, E, M),
+                        ocp_value((w[u] >> 16) & 255u, E, M), ocp_value(w[u] >> 24, E, M));
+      const float s = e8m0_value(sb[u]);
+      __stcs(out + q, make_float4(__fmul_rn(v.x, s), __fmul_rn(v.y, s), __fmul_rn(v.z, s), __fmul_rn(v.w, s)));
+    }
   }
-  const uint32_t o = e / len, l = e - o * len;
-  const float s = e8m0_value(scales[o * nb + l / block]);
-  out[q] = make_float4(__fmul_rn(v.x, s), __fmul_rn(v.y, s), __fmul_rn(v.z, s), __fmul_rn(v.w, s));
 }
 
 // dequantize_packed with blocks along len and inner a multiple of 4 (axis 0 of a matrix): a thread owns 4 adjacent
@@ -249,12 +272,15 @@ int mxq_dequantize_packed(const uint8_t* codes, const uint8_t* scales, float* ou
     return MXQ_LAUNCH_CHECK("dequantize_packed");
   }
   if (al && rows) {
-    const uint32_t n4 = (uint32_t)(n / 4), grid = (n4 + 255) / 256;
+    const uint32_t n4 = (uint32_t)(n / 4), grid = grid_for(n4, 256, 8);
+    int bsh = -1;
+    if ((block & (block - 1)) == 0 && len % block == 0)
+      for (bsh = 0; (1ll << bsh) < block; bsh++) {
+      }
     cudaStream_t st = as_stream(stream);
     by_format(e, m, [&](auto E, auto M) {
       k_dequantize_packed4<decltype(E)::value, decltype(M)::value><<<grid, 256, 0, st>>>(
-          codes, scales, reinterpret_cast<float4*>(out), n4, (uint32_t)len, (uint32_t)inner, (uint32_t)block,
-          (uint32_t)nb);
+          codes, scales, reinterpret_cast<float4*>(out), n4, (uint32_t)len, (uint32_t)block, (uint32_t)nb, bsh);
       return 0;
     });
     return MXQ_LAUNCH_CHECK("dequantize_packed");

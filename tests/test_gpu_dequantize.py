@@ -68,8 +68,11 @@ FMTS = ["MXFP8_E4M3", "MXFP8_E5M2", "MXFP6_E3M2", "MXFP6_E2M3", "MXFP4"]
 
 # (shape of V, axis, padded shape): the compact quantizer needs rows of 4-aligned runs, so a ragged V is quantized
 # inside a zero-padded one (zeros change no block's maximum) and its codes and scales are cut out of the result
+# ((5, 48), 1): rows of a ragged last block (the scale index by division); the two large ones take the grid-stride
+# loops of the float4 kernels more than once round
 COMPACT = [((4, 64, 12), 1, None), ((6, 64), 1, None), ((64, 8), 0, None), ((3, 34), 1, (3, 64)),
-           ((2, 40, 6), 1, (2, 40, 8))]
+           ((2, 40, 6), 1, (2, 40, 8)), ((5, 48), 1, None), ((1024, 2048), 1, None), ((1200, 2000), 1, None),
+           ((2048, 1024), 0, None)]
 
 
 @pytest.mark.parametrize("shape,axis,padded", COMPACT)
