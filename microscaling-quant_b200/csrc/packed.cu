@@ -175,18 +175,27 @@ __global__ void __launch_bounds__(256) k_dequantize_packed_cols(const uint8_t* _
               x3 = e8m0_value(w >> 24);
   const uint32_t l0 = b * block, l1 = l0 + block < len ? l0 + block : len;
   uint32_t q = (o * len + l0) * iq + jq;                   // float4 index of (row l0, columns 4 jq ..)
-  for (uint32_t l = l0; l < l1; l++, q += iq) {
-    float4 v;
-    if (E + M == 3) {
-      const uint32_t c = reinterpret_cast<const uint16_t*>(codes)[q];
-      v = make_float4(ocp_value(c & 15u, E, M), ocp_value((c >> 4) & 15u, E, M), ocp_value((c >> 8) & 15u, E, M),
-                      ocp_value((c >> 12) & 15u, E, M));
-    } else {
-      const uint32_t c = reinterpret_cast<const uint32_t*>(codes)[q];
-      v = make_float4(ocp_value(c & 255u, E, M), ocp_value((c >> 8) & 255u, E, M), ocp_value((c >> 16) & 255u, E, M),
-                      ocp_value(c >> 24, E, M));
+  constexpr int U = 4;                                     // rows whose code words are loaded before any decode
+  for (uint32_t l = l0; l < l1; l += U, q += U * iq) {
+    uint32_t c[U];
+#pragma unroll
+    for (int u = 0; u < U; u++)
+      c[u] = l + u < l1 ? (E + M == 3 ? (uint32_t)reinterpret_cast<const uint16_t*>(codes)[q + u * iq]
+                                      : reinterpret_cast<const uint32_t*>(codes)[q + u * iq])
+                        : 0u;
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      if (l + u >= l1) break;
+      float4 v;
+      if (E + M == 3)
+        v = make_float4(ocp_value(c[u] & 15u, E, M), ocp_value((c[u] >> 4) & 15u, E, M),
+                        ocp_value((c[u] >> 8) & 15u, E, M), ocp_value((c[u] >> 12) & 15u, E, M));
+      else
+        v = make_float4(ocp_value(c[u] & 255u, E, M), ocp_value((c[u] >> 8) & 255u, E, M),
+                        ocp_value((c[u] >> 16) & 255u, E, M), ocp_value(c[u] >> 24, E, M));
+      __stcs(out + q + u * iq,
+             make_float4(__fmul_rn(v.x, x0), __fmul_rn(v.y, x1), __fmul_rn(v.z, x2), __fmul_rn(v.w, x3)));
     }
-    __stcs(out + q, make_float4(__fmul_rn(v.x, x0), __fmul_rn(v.y, x1), __fmul_rn(v.z, x2), __fmul_rn(v.w, x3)));
   }
 }
 
