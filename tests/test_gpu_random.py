@@ -343,3 +343,30 @@ def test_lut_block_paths(oracle, fmt):
         Po, Xo = oracle.lut_block_quantize(V, fmt, 0, 32, mode, 2.0 ** -23, 1, 50)
         assert_bits(P, Po, f"block.lut {fmt} {mode}")
         assert_bits(X, Xo, f"block.lut X {fmt} {mode}")
+
+
+@pytest.mark.parametrize("fmt", ["MXFP6_E3M2", "MXFP6_E2M3", "MXFP8_E4M3", "MXFP8_E5M2"])
+def test_lut_block_large(oracle, fmt):
+    """block.lut's one-launch path on an operand of 2^22 elements (2048 rows in clusters of four CTAs, 65 panels):
+    against the oracle with a ragged last panel (2050 columns), every group width of the path (a column, a pair, a
+    whole panel), all three rounding modes, a column of zeros and blocks of tiny values under a floor that is no
+    power of two (the general element step); then a NaN refused and the next call bit for bit again."""
+    rng = np.random.default_rng(sum(map(ord, fmt)) + 5)
+    K, n = 2048, 2050
+    V = (rng.standard_normal((K, n)) * 2.0 ** rng.uniform(-8, 8, (1, n))).astype(np.float32)
+    V[:, 7] = 0.0
+    V[64:96, 40] *= 2.0 ** -120
+    for G, mode, floor in ((0, "rne", 2.0 ** -23), (1, "rne", 2.0 ** -23), (5, "rne", 2.0 ** -23),
+                           (1, "ties_away", 2.0 ** -23), (1, "truncate", 2.0 ** -23), (1, "rne", 1e-30)):
+        P, X = prod.lut_block_quantize(V, fmt, 0, 32, mode, floor, G, 50)
+        Po, Xo = oracle.lut_block_quantize(V, fmt, 0, 32, mode, floor, G, 50)
+        assert_bits(P, Po, f"block.lut {fmt} G{G} {mode} floor {floor}")
+        assert_bits(X, Xo, f"block.lut X {fmt} G{G} {mode} floor {floor}")
+    Vb = V.copy()
+    Vb[1000, 1030] = np.nan
+    with pytest.raises(ValueError, match="not a"):
+        prod.lut_block_quantize(Vb, fmt, 0, 32, "rne", 2.0 ** -23, 1, 50)
+    P, X = prod.lut_block_quantize(V, fmt, 0, 32, "rne", 2.0 ** -23, 3, 50)
+    Po, Xo = oracle.lut_block_quantize(V, fmt, 0, 32, "rne", 2.0 ** -23, 3, 50)
+    assert_bits(P, Po, f"block.lut {fmt} G3 after a refused call")
+    assert_bits(X, Xo, f"block.lut X {fmt} G3 after a refused call")
