@@ -191,6 +191,13 @@ struct FusedArgs {
   int rounding;
 };
 
+// the larger of two floats, NaN when either is (max.NaN: a NaN is never dropped)
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
 // block.mxgemmini (block.py, mxgemmini.py) of one 32-row block of one column, by one lane: the 32 values col[0],
 // col[n], ... (a warp's load is one 128-byte row segment when its lanes take consecutive columns), the block max, the
 // scale (to *xout) and its reciprocal, and every code -- the direct code of the short step when the block is finite
@@ -203,19 +210,26 @@ __device__ __forceinline__ bool quant_block(const float* col, int64_t n, float* 
   float v[32];
 #pragma unroll
   for (int i = 0; i < 32; i++) v[i] = __ldcs(col + i * n);
-  uint32_t mbits = 0u;                                       // max |v| as bits: a NaN pattern tops every number
+  // max |v| by a tree of NaN-propagating maxima (a NaN anywhere makes it NaN)
+  float t[16];
 #pragma unroll
-  for (int i = 0; i < 32; i++) mbits = max(mbits, f2u(v[i]) & 0x7fffffffu);
-  const bool nan = mbits > 0x7f800000u;
-  const float x = scale_mxquant(nan ? qnan_f() : u2f(mbits), scale_floor);
+  for (int i = 0; i < 16; i++) t[i] = max_nan(fabsf(v[2 * i]), fabsf(v[2 * i + 1]));
+#pragma unroll
+  for (int h = 8; h >= 1; h >>= 1)
+#pragma unroll
+    for (int i = 0; i < h; i++) t[i] = max_nan(t[i], t[i + h]);
+  const float mx = t[0];
+  const bool nan = mx != mx;
+  const float x = scale_mxquant(nan ? qnan_f() : mx, scale_floor);
   const float r = reciprocal_of<MXQ_FAMILY_MXGEMMINI>(x, nan);
   *xout = x;
   uint32_t w[8];
   bool nocode = false;
-  if (mbits < 0x7f800000u && r != 0.0f) {
+  if (mx < INFINITY && r != 0.0f) {
 #pragma unroll
     for (int i = 0; i < 32; i++) {
-      const uint32_t c = code_clean<FE, FM, QM>(__fmul_rn(v[i], r));
+      // the sign of a zero kept: both zeros have one grid rank and one table entry
+      const uint32_t c = code_clean<FE, FM, QM, true>(__fmul_rn(v[i], r));
       tally(c);
       w[i >> 2] = (i & 3) ? (w[i >> 2] | (c << (8 * (i & 3)))) : c;
     }

@@ -89,7 +89,9 @@ __device__ __forceinline__ uint32_t ocp_code_finite(float v) {
 // the binade's first code (k runs over [2^M, 2^(M+1)] in a normal binade, [0, 2^(M+1)] in the lowest, and reaching
 // 2^(M+1) carries into the next binade's exponent as the code of the value would); saturation at MAX_NORM is the
 // minimum with its code (codes grow with the value), and a zero input is +0 (q_ocp_small drops its sign)
-template <int E, int M, int MODE>
+// ZERO_SIGN: a zero keeps its sign (the negative-zero code for -0), one select fewer -- for block.lut's internal
+// codes, where both zeros count into the same grid rank and look up the same table entry
+template <int E, int M, int MODE, bool ZERO_SIGN = false>
 __device__ __forceinline__ uint32_t code_clean(float z) {
   constexpr int BIAS = (1 << (E - 1)) - 1;
   constexpr uint32_t LO = (uint32_t)(128 - BIAS) << 23;               // the lowest binade's exponent field in place
@@ -104,6 +106,7 @@ __device__ __forceinline__ uint32_t code_clean(float z) {
   else s = __fadd_rz(__fadd_rn(u2f(a), u2f(e23 - ((uint32_t)(M + 1) << 23))), c);
   const uint32_t k = f2u(s) - cb;
   const uint32_t mag = min(k + ((e23 - LO) >> (23 - M)), MAXC);
+  if (ZERO_SIGN) return ((u >> 31) << (E + M)) | mag;
   return a == 0u ? 0u : (((u >> 31) << (E + M)) | mag);
 }
 
